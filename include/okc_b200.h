@@ -1,0 +1,171 @@
+/*
+ * okc_b200 — C ABI of the B200 (sm_100a) decode-step kernels.
+ *
+ * Every entry point takes raw device pointers, explicit sizes and a CUDA stream,
+ * enqueues its kernels on that stream and returns at once (no host synchronisation,
+ * so every call can be captured in a CUDA graph).  Return value: OKC_OK or a negative
+ * OKC_ERR_* code; a call that returns an error enqueued nothing that writes outputs.
+ * No entry point allocates memory: scratch ("workspace") is passed in by the caller,
+ * sized by the matching *_workspace_bytes() query, and must be zero-filled once
+ * before its first use (it keeps its own state self-consistent across calls).
+ *
+ * Device-side errors (a bad page id, a device wait that timed out) cannot be
+ * returned synchronously; kernels OR an OKC_DEVERR_* bit into the 32-bit error word
+ * at the start of the workspace.  okc_read_device_error() reads and clears it.
+ *
+ * Tensor layouts are row-major and dense unless a leading dimension says otherwise.
+ * Element types: bf16 = IEEE bfloat16, e4m3 = OCP FP8 E4M3 (float8_e4m3fn),
+ * e2m1 = OCP FP4 E2M1 packed two per byte (low nibble = even element).
+ */
+#ifndef OKC_B200_H
+#define OKC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* okc_stream_t; /* == cudaStream_t */
+
+enum {
+  OKC_OK = 0,
+  OKC_ERR_INVALID = -1,     /* bad size, null pointer or unsupported shape */
+  OKC_ERR_ALIGNMENT = -2,   /* a pointer or leading dimension breaks 16-byte alignment */
+  OKC_ERR_WORKSPACE = -3,   /* workspace too small */
+  OKC_ERR_LAUNCH = -4,      /* the CUDA launch itself failed */
+  OKC_ERR_DEVICE = -5,      /* no sm_100 device / kernel image */
+};
+
+enum {
+  OKC_DEVERR_TIMEOUT = 1,   /* a bounded device wait (mbarrier) gave up */
+  OKC_DEVERR_PAGE = 2,      /* a page-table entry outside [0, num_pages) was skipped */
+  OKC_DEVERR_INDEX = 4,     /* an expert id or slot outside its range was skipped */
+};
+
+/* Library version string, e.g. "okc_b200 0.1 sm_100a". */
+const char* okc_version(void);
+
+/* Reads the device error word at the start of `workspace` (synchronises `stream`),
+ * clears it, and returns it (0 = no error, else OKC_DEVERR_* bits; <0 = CUDA error). */
+int okc_read_device_error(const void* workspace, okc_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * Projection: y[M,N] = x[M,K] · W[N,K]^T (+ residual[M,N]), bf16 in, fp32 accumulate.
+ * Replaces the projection dispatch of muse_decode_layer/decode/projections.py:50-77
+ * (`_project`: M=1 `_gemv` :8-15, split-K `_small_gemm` :18-39 + `_reduce_projection`
+ * :42-48) and muse_bf16_proj/projection/runtime.py:80-220 (`run_config`).
+ * Picks the split-K skinny kernel (M <= 32, cluster/DSMEM split-K reduction) or the
+ * tcgen05 kernel (M >= 33) itself.  out_fp32 != 0 writes fp32 y (a row-parallel partial
+ * that an all-reduce sums), else bf16.  residual (bf16, may be NULL) is added to the
+ * fp32 accumulator before the single rounding.  K must be a multiple of 8, ldx/ldw/ldy
+ * multiples of 8 elements, pointers 16-byte aligned.
+ * ---------------------------------------------------------------------------------- */
+size_t okc_gemm_bf16_workspace_bytes(int M, int N, int K);
+int okc_gemm_bf16(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
+                  const void* residual, int M, int N, int K, int out_fp32,
+                  void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
+/* Forces one kernel family (0 = auto, 1 = skinny split-K, 2 = tcgen05) and, for the
+ * skinny family, a split count (0 = auto).  Exposed for tests and tuning sweeps. */
+int okc_gemm_bf16_ex(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
+                     const void* residual, int M, int N, int K, int out_fp32,
+                     int family, int splits,
+                     void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * RMSNorm: y[t] = bf16(x[t] * rsqrt(mean(x[t]^2) + eps) * g), g = w or (1 + w).
+ * Replaces `_norm` muse_decode_layer/decode/boundaries.py:8-14 and `rms`/`gain`
+ * muse_prefill_layer/submission.py:89-96.  x bf16 [T,H] (ldx), w bf16 [H].
+ * ---------------------------------------------------------------------------------- */
+int okc_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, int ldy, int T, int H,
+                     float eps, int unit_offset, okc_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * RoPE + FP8 KV-append (one decode token per sequence, q_len = 1).
+ * Replaces `_qkv_norm_store` muse_decode_layer/decode/attention.py:13-37, the append of
+ * muse_attention_decode/submission.py:283-305 and the cache write of
+ * muse_prefill_layer/submission.py:155-156.
+ * qkv: bf16 [B, ldqkv] holding q (Hq*D) | k (Hkv*D) | v (Hkv*D) per row.
+ * positions: int64 [B] (the new token's position = cached length).  page_table int32
+ * [B, max_pages] (ld = table_ld).  Slot = page_table[b][pos / P] * P + pos % P.
+ * Writes q_out bf16 [B, Hq, D] (rotated), k_cache/v_cache e4m3 [num_pages, P, Hkv, D] at
+ * the slot (k rotated, / k_scale[h]; v / v_scale[h]; RNE, overflow -> NaN like torch),
+ * and slots_out int64 [B] (may be NULL).  inv_freq fp32 [D/2] (NULL = no RoPE).
+ * ---------------------------------------------------------------------------------- */
+int okc_rope_kv_append(const void* qkv, int ldqkv, const int64_t* positions,
+                       const int32_t* page_table, int table_ld, int max_pages,
+                       const float* inv_freq, const float* k_scale, const float* v_scale,
+                       void* q_out, void* k_cache, void* v_cache, int64_t* slots_out,
+                       int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
+                       void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * Paged FP8 attention decode (q_len = 1), split-KV with a log-sum-exp merge.
+ * Replaces `_fused_attn` muse_attention_decode/submission.py:191-351 (its cached-context
+ * splits and two-level merge), `_attention_parts`/`_attention_finish`
+ * muse_decode_layer/decode/attention.py:40-113, and the attention of
+ * muse_prefill_layer/submission.py:158-176 (GQA grouping q.view(B, Hkv, G, D)).
+ * q bf16 [B, Hq, D] (ldq = row stride in elements); caches e4m3 [num_pages, P, Hkv, D];
+ * page_table int32 [B, table_ld]; seq_lens int32 [B] = keys to attend per sequence;
+ * k_scale/v_scale fp32 [Hkv]; out bf16 [B, Hq, D] (ldo).  out = softmax(q·K^T * sm_scale)
+ * · V with K = e4m3 * k_scale[h], V = e4m3 * v_scale[h].  Supported: D in {64, 128},
+ * Hkv in {1, 2, 4, 8}, G = Hq/Hkv <= 8, P dividing 32 or a multiple of 32.
+ * ---------------------------------------------------------------------------------- */
+size_t okc_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int num_ctas);
+int okc_attn_decode_fp8(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                        const int32_t* page_table, int table_ld, const int32_t* seq_lens,
+                        const float* k_scale, const float* v_scale, void* out, int ldo,
+                        int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
+                        float sm_scale, int num_ctas,
+                        void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
+ * MoE routing: logits = bf16(x · Wr^T) (fixed fp32 summation order, see DESIGN),
+ * ids = top-k of the logits (ties -> lower expert id), weights = softmax over the
+ * chosen logits (renormalize != 0) or the full-softmax probabilities of the chosen
+ * experts (renormalize == 0).  x bf16 [T,H], wr bf16 [E,H]; ids int32 [T,k];
+ * weights fp32 [T,k]; logits_out fp32 [T,E] (may be NULL).  E <= 256, k <= 16.
+ * Replaces `route` muse_prefill_layer/submission.py:179-184 and the routing call of
+ * muse_decode_layer/decode/runtime.py:55-63 (softmax top-k per the BASELINE contract).
+ * ---------------------------------------------------------------------------------- */
+int okc_moe_route(const void* x, const void* wr, int32_t* ids, float* weights,
+                  float* logits_out, int T, int H, int E, int topk, int renormalize,
+                  okc_stream_t stream);
+
+/* Token permutation: per expert, the pair ids p = t*topk + slot routed to it, ascending.
+ * Replaces `_route` muse_moe_w4a16/submission.py:274-291 and `moe_align_block_size`
+ * (muse_decode_layer/decode/experts.py:80).  ids int32 [T*topk] (values outside
+ * [expert_lo, expert_lo + E_local) are not local and are skipped).  Outputs:
+ * counts int32 [E_local], offsets int32 [E_local + 1] (exclusive prefix of counts),
+ * pairs int32 [T*topk] (expert-major, ascending p inside each expert),
+ * tiles int32 [1 + max_tiles]: tiles[0] = number of (expert, first row) tiles of `bm`
+ * pairs, then (expert << 16 | first) per tile.  T*topk <= 65536. */
+int okc_moe_permute(const int32_t* ids, int T, int topk, int expert_lo, int E_local, int bm,
+                    int32_t* counts, int32_t* offsets, int32_t* pairs, int32_t* tiles,
+                    int max_tiles, okc_stream_t stream);
+
+/* W4A16 experts: for each local expert e and each pair p routed to it,
+ *   h = x[p / topk] · W13[e]^T  (W13 e2m1 [E, 2I, H/2], sf e4m3 [E, 2I, H/16], gs fp32 [E])
+ *   inter[p] = bf16( silu(bf16(h[:I])) * bf16(h[I:]) )
+ *   y[p] = bf16( inter[p] · W2[e]^T )  (W2 e2m1 [E, H, I/2], sf [E, H, I/16], gs [E])
+ * and out[t] = bf16( sum_slot weights[t, slot] * y[t*topk + slot] ) over local slots.
+ * Weight element = e2m1 * sf (exact in bf16) with gs applied to the fp32 accumulator.
+ * Replaces `_expert_gemm` + `_finalize` muse_moe_w4a16/submission.py:163-308 and
+ * `_nvfp4_gate_up`/`_nvfp4_down` muse_decode_layer/decode/nvfp4_gemv.py:21-75.
+ * Needs the okc_moe_permute outputs.  inter/y are scratch inside `workspace`.
+ * H multiple of 256, I multiple of 128. */
+size_t okc_moe_experts_workspace_bytes(int T, int topk, int H, int I);
+int okc_moe_experts_w4a16(const void* x, const int32_t* ids, const float* weights,
+                          const int32_t* counts, const int32_t* offsets, const int32_t* pairs,
+                          const void* w13, const void* w13_sf, const float* w13_gs,
+                          const void* w2, const void* w2_sf, const float* w2_gs,
+                          void* out, int T, int topk, int H, int I, int expert_lo, int E_local,
+                          void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* OKC_B200_H */

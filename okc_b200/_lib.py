@@ -1,0 +1,80 @@
+"""ctypes binding of libokc_b200.so (the C ABI declared in include/okc_b200.h).
+
+There is no fallback: if the library is missing or was built without sm_100a code the
+import of okc_b200.ops fails with an error that says so.  Build it with
+``python -m okc_b200.build``.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIB_PATH = Path(os.environ.get("OKC_B200_LIB", _PKG / "_lib" / "libokc_b200.so"))
+
+OKC_OK = 0
+OKC_ERR_INVALID = -1
+OKC_ERR_ALIGNMENT = -2
+OKC_ERR_WORKSPACE = -3
+OKC_ERR_LAUNCH = -4
+OKC_ERR_DEVICE = -5
+ERR_NAMES = {
+    OKC_ERR_INVALID: "invalid argument or unsupported shape",
+    OKC_ERR_ALIGNMENT: "pointer or leading dimension not 16-byte aligned",
+    OKC_ERR_WORKSPACE: "workspace too small",
+    OKC_ERR_LAUNCH: "CUDA launch failed",
+    OKC_ERR_DEVICE: "no sm_100a device or kernel image",
+}
+DEVERR_TIMEOUT, DEVERR_PAGE, DEVERR_INDEX = 1, 2, 4
+
+_p, _i, _f, _sz, _i64 = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_int64
+
+# name -> (restype, argtypes); must match include/okc_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "okc_version": (C.c_char_p, []),
+    "okc_read_device_error": (_i, [_p, _p]),
+    "okc_gemm_bf16_workspace_bytes": (_sz, [_i, _i, _i]),
+    "okc_gemm_bf16": (_i, [_p, _i, _p, _i, _p, _i, _p, _i, _i, _i, _i, _p, _sz, _p]),
+    "okc_gemm_bf16_ex": (_i, [_p, _i, _p, _i, _p, _i, _p, _i, _i, _i, _i, _i, _i, _p, _sz, _p]),
+    "okc_rmsnorm_bf16": (_i, [_p, _i, _p, _p, _i, _i, _i, _f, _i, _p]),
+    "okc_rope_kv_append": (_i, [_p, _i, _p, _p, _i, _i, _p, _p, _p, _p, _p, _p, _p,
+                                _i, _i, _i, _i, _i, _i64, _p, _sz, _p]),
+    "okc_attn_decode_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
+    "okc_attn_decode_fp8": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
+                                 _i, _i, _i, _i, _i, _i64, _f, _i, _p, _sz, _p]),
+    "okc_moe_route": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),
+    "okc_moe_permute": (_i, [_p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _i, _p]),
+    "okc_moe_experts_workspace_bytes": (_sz, [_i, _i, _i, _i]),
+    "okc_moe_experts_w4a16": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
+                                   _i, _i, _i, _i, _i, _i, _p, _sz, _p]),
+}
+
+_lib = None
+
+
+class OkcError(RuntimeError):
+    pass
+
+
+def load() -> C.CDLL:
+    """Loads the library once; raises OkcError (never falls back) when it is absent."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise OkcError(f"{LIB_PATH} is missing: build it with `python -m okc_b200.build` "
+                       "(the okc_b200 operators have no CPU fallback)")
+    lib = C.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def check(status: int, what: str) -> None:
+    if status != OKC_OK:
+        raise OkcError(f"{what}: {ERR_NAMES.get(status, 'error')} (status {status})")

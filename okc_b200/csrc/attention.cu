@@ -1,0 +1,584 @@
+// Paged FP8-KV attention decode (q_len = 1) and the fused RoPE + FP8 KV-append.
+//
+// KV cache layout (the reference's, muse_decode_layer/decode/spec.py:48-49):
+//   k_cache / v_cache  e4m3 [num_pages][P][Hkv][D]   (one token row = Hkv*D bytes)
+// so a run of tokens of one page is ONE contiguous span holding every KV head.
+//
+// attn_decode_kernel (roofline: HBM, algorithmic bytes = sum_b len_b * Hkv * D * 2):
+//  * Work = all sequences' tokens cut into "units" of TS = 32 * 8/Hkv tokens; the units
+//    are split evenly over a persistent grid (stream-K), so ragged context lengths stay
+//    balanced.  A CTA that crosses a sequence boundary flushes a partial (m, l, acc).
+//  * Warp 8 is the producer: per unit it looks up the page table and issues one
+//    cp.async.bulk per (page, K|V) span into a 3-stage shared-memory ring (mbarrier
+//    complete_tx), with an L2 evict-first hint (the cache is streamed once).
+//  * Warps 0..7 are consumers: warp w attends KV head w % Hkv over the 32-token sub-tile
+//    w / Hkv of each unit.  QK^T and PV run as e4m3 mma.sync m16n8k32 directly on the
+//    cache bytes (no per-element dequant): the query rows are carried as two e4m3 terms
+//    q ~= (q1 + q2/16) * 2^-a (a per row), which fill the 16 MMA rows (8 query heads x 2
+//    terms) and keep ~8 significant bits, the precision of the bf16 query; likewise the
+//    probabilities p ~= (p1 + p2/16) / 256.  k_scale / v_scale / sm_scale are applied in
+//    fp32 to the scores and to the merged output.  Online softmax in fp32 (exp2 domain).
+//  * K fragments are 16-byte shared loads (K-axis permutation, see common.cuh); V
+//    fragments are 16-byte loads of 4 token rows, transposed 4x4 in registers with PRMT.
+// attn_merge_kernel: deterministic log-sum-exp merge of the partials of each sequence.
+//
+// Mirrors muse_attention_decode/submission.py:100-351 (tile loop, online softmax,
+// split partials and merge) and muse_prefill_layer/submission.py:137-176 (semantics).
+#include "kernels.cuh"
+
+namespace okc {
+
+template <int D, int HKV>
+struct AttnCfg {
+  static constexpr int NSUB = 8 / HKV;          // 32-token sub-tiles per unit
+  static constexpr int TS = 32 * NSUB;          // tokens per unit (stage)
+  static constexpr int ROW = HKV * D;           // bytes per token row
+  static constexpr int KV_BYTES = TS * ROW;     // bytes of K (or V) per stage
+  static constexpr int STAGE = 2 * KV_BYTES;
+  static constexpr int NS = (196608 / STAGE) > 4 ? 4 : (196608 / STAGE);
+  static constexpr int RL = D / 8;              // bytes per K run / V run per lane
+  static constexpr int KSTEPS = D / 32;         // k32 MMA steps over the head dim
+  static constexpr int DB = D / 8;              // n8 blocks over the head dim (PV)
+  static constexpr int THREADS = 9 * 32;
+};
+
+
+// ---------------------------------------------------------------------------------------
+// Balanced partition of U units over C CTAs: CTA c gets q or q+1 consecutive units.
+__host__ __device__ __forceinline__ void unit_range(int U, int C, int c, int& u0, int& u1) {
+  const int q = U / C, r = U % C;
+  u0 = c * q + (c < r ? c : r);
+  u1 = u0 + q + (c < r ? 1 : 0);
+}
+__host__ __device__ __forceinline__ int cta_of_unit(int U, int C, int u) {
+  const int q = U / C, r = U % C;
+  const int big = r * (q + 1);
+  return u < big ? u / (q + 1) : r + (u - big) / q;
+}
+
+// Exclusive prefix of per-sequence unit counts into prefix[0..B], by warp 0.
+__device__ __forceinline__ void unit_prefix(const int32_t* seq_lens, int B, int TS, int* prefix) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int carry = 0;
+    for (int base = 0; base < B; base += 32) {
+      const int b = base + lane;
+      int len = b < B ? seq_lens[b] : 0;
+      if (len < 0) len = 0;
+      const int n = (len + TS - 1) / TS;
+      int v = n;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (b < B) prefix[b] = carry + v - n;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) prefix[B] = carry;
+  }
+}
+
+__device__ __forceinline__ int find_seq(const int* prefix, int B, int u) {
+  int lo = 0, hi = B - 1;  // largest b with prefix[b] <= u
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= u) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// 4x4 byte transpose: out_i = (w0.byte_i, w1.byte_i, w2.byte_i, w3.byte_i).
+__device__ __forceinline__ void transpose4x4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
+                                             uint32_t& o0, uint32_t& o1, uint32_t& o2, uint32_t& o3) {
+  const uint32_t t0 = prmt(w0, w1, 0x5140), t1 = prmt(w2, w3, 0x5140);
+  const uint32_t t2 = prmt(w0, w1, 0x7362), t3 = prmt(w2, w3, 0x7362);
+  o0 = prmt(t0, t1, 0x5410);
+  o1 = prmt(t0, t1, 0x7632);
+  o2 = prmt(t2, t3, 0x5410);
+  o3 = prmt(t2, t3, 0x7632);
+}
+
+template <int D, int HKV>
+__global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kernel(AttnArgs a) {
+  using C = AttnCfg<D, HKV>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* stages = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::NS * C::STAGE);
+  uint64_t* empty = full + C::NS;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty + C::NS);
+  int* prefix = const_cast<int*>(abort_flag) + 4;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  unit_prefix(a.seq_lens, a.B, C::TS, prefix);
+  __syncthreads();
+
+  const int U = prefix[a.B];
+  int u0, u1;
+  unit_range(U, a.num_ctas, blockIdx.x, u0, u1);
+  if (u0 >= u1) return;
+
+  if (warp == 8) {
+    // ------------------------------- producer -------------------------------------
+    const uint64_t pol = l2_evict_first_policy();
+    int b = find_seq(prefix, a.B, u0);
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    for (int u = u0; u < u1; ++u) {
+      while (prefix[b + 1] <= u) ++b;
+      if (*abort_flag) break;
+      const int len = a.seq_lens[b];
+      const int t0 = (u - prefix[b]) * C::TS;
+      const int t_end = min(len, t0 + C::TS);
+      const int p_first = t0 / a.P, p_last = (t_end - 1) / a.P;
+      const int nseg = p_last - p_first + 1;
+      // page lookups first, so the expected byte count is exact
+      uint32_t my_bytes = 0;
+      for (int sg = lane; sg < nseg; sg += 32) {
+        const int lp = p_first + sg;
+        const int page = lp < a.table_ld ? a.page_table[(size_t)b * a.table_ld + lp] : -1;
+        const int lo = max(t0, lp * a.P), hi = min(t_end, (lp + 1) * a.P);
+        if (page >= 0 && page < a.num_pages) my_bytes += 2u * (uint32_t)(hi - lo) * C::ROW;
+        else atomicOr(a.err, OKC_DEVERR_PAGE);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) my_bytes += __shfl_xor_sync(0xffffffffu, my_bytes, o);
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&empty[stage], phase ^ 1u, a.err);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) { *abort_flag = 1; break; }
+      if (lane == 0) {
+        if (my_bytes) mbar_arrive_expect_tx(&full[stage], my_bytes);
+        else mbar_arrive(&full[stage]);
+      }
+      __syncwarp();
+      uint8_t* sk = stages + (size_t)stage * C::STAGE;
+      uint8_t* sv = sk + C::KV_BYTES;
+      for (int sg = lane; sg < nseg; sg += 32) {
+        const int lp = p_first + sg;
+        const int page = lp < a.table_ld ? a.page_table[(size_t)b * a.table_ld + lp] : -1;
+        if (page < 0 || page >= a.num_pages) continue;
+        const int lo = max(t0, lp * a.P), hi = min(t_end, (lp + 1) * a.P);
+        const size_t src = ((size_t)page * a.P + (lo - lp * a.P)) * C::ROW;
+        const uint32_t bytes = (uint32_t)(hi - lo) * C::ROW;
+        const int dst = (lo - t0) * C::ROW;
+        bulk_g2s(sk + dst, a.k_cache + src, bytes, &full[stage], pol);
+        bulk_g2s(sv + dst, a.v_cache + src, bytes, &full[stage], pol);
+      }
+      ++issued;
+      if (++stage == C::NS) { stage = 0; phase ^= 1u; }
+    }
+    // Before leaving, make sure the copies this warp issued have landed (bounded).
+    if (lane == 0) {
+      const int n = min(issued, C::NS);
+      int s = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < n; ++i) {
+        if (--s < 0) { s = C::NS - 1; ph ^= 1u; }
+        if (!mbar_wait(&full[s], ph, a.err)) break;
+      }
+    }
+    return;
+  }
+
+  // --------------------------------- consumers ------------------------------------
+  const int h = warp % HKV, sub = warp / HKV;
+  const int g = lane >> 2, c = lane & 3;
+  const float ksc = a.k_scale[h];
+  const int hq = h * a.G + g;
+  const bool row_ok = g < a.G;
+
+  uint32_t q1lo[C::KSTEPS], q2lo[C::KSTEPS], q1hi[C::KSTEPS], q2hi[C::KSTEPS];
+  float qf = 0.f;  // 2^-a * k_scale * sm_scale * log2(e)
+  float m = -INFINITY, l = 0.f;
+  float acc[C::DB][4];
+
+  auto load_q = [&](int b) {
+    float v0[C::RL], v1[C::RL];
+    float amax = 0.f;
+    if (row_ok) {
+      const __nv_bfloat16* qr = a.q + (size_t)b * a.ldq + (size_t)hq * D;
+#pragma unroll
+      for (int i = 0; i < C::RL; i += 8) {
+        const uint4 r0 = *reinterpret_cast<const uint4*>(qr + C::RL * c + i);
+        const uint4 r1 = *reinterpret_cast<const uint4*>(qr + D / 2 + C::RL * c + i);
+        const uint32_t w0[4] = {r0.x, r0.y, r0.z, r0.w}, w1[4] = {r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v0[i + 2 * k] = bf16_lo(w0[k]);
+          v0[i + 2 * k + 1] = bf16_hi(w0[k]);
+          v1[i + 2 * k] = bf16_lo(w1[k]);
+          v1[i + 2 * k + 1] = bf16_hi(w1[k]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < C::RL; ++i) amax = fmaxf(amax, fmaxf(fabsf(v0[i]), fabsf(v1[i])));
+    } else {
+#pragma unroll
+      for (int i = 0; i < C::RL; ++i) v0[i] = v1[i] = 0.f;
+    }
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    // 2^ea with amax * 2^ea in [128, 256): the e4m3 terms keep their full precision
+    int ea = 0;
+    if (amax > 0.f) ea = 7 - (int)((__float_as_uint(amax) >> 23) & 0xff) + 127;
+    const float up = __uint_as_float((uint32_t)(127 + ea) << 23);
+    const float down = __uint_as_float((uint32_t)(127 - ea) << 23);
+    qf = down * ksc * a.sm_scale_log2;
+#pragma unroll
+    for (int s = 0; s < C::KSTEPS; ++s) {
+      uint32_t w1a = 0, w2a = 0, w1b = 0, w2b = 0;
+#pragma unroll
+      for (int pr = 0; pr < 2; ++pr) {
+        const int i = 4 * s + 2 * pr;
+        const float x0 = v0[i] * up, x1 = v0[i + 1] * up;
+        const float y0 = v1[i] * up, y1 = v1[i + 1] * up;
+        const uint16_t hx = f2_to_e4m3x2_sat(x0, x1), hy = f2_to_e4m3x2_sat(y0, y1);
+        const __half2 bx = __half2(__nv_cvt_fp8x2_to_halfraw2(hx, __NV_E4M3));
+        const __half2 by = __half2(__nv_cvt_fp8x2_to_halfraw2(hy, __NV_E4M3));
+        const uint16_t lx = f2_to_e4m3x2_sat((x0 - __low2float(bx)) * 16.f, (x1 - __high2float(bx)) * 16.f);
+        const uint16_t ly = f2_to_e4m3x2_sat((y0 - __low2float(by)) * 16.f, (y1 - __high2float(by)) * 16.f);
+        w1a |= (uint32_t)hx << (16 * pr);
+        w2a |= (uint32_t)lx << (16 * pr);
+        w1b |= (uint32_t)hy << (16 * pr);
+        w2b |= (uint32_t)ly << (16 * pr);
+      }
+      q1lo[s] = w1a; q2lo[s] = w2a; q1hi[s] = w1b; q2hi[s] = w2b;
+    }
+    m = -INFINITY;
+    l = 0.f;
+#pragma unroll
+    for (int i = 0; i < C::DB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  };
+
+  auto flush = [&](int b) {
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (!row_ok) return;
+    const int slot = blockIdx.x + b;
+    const size_t rowi = ((size_t)slot * C::NSUB + sub) * a.Hq + hq;
+    if (c == 0) {
+      a.ws_ml[rowi * 2] = m;
+      a.ws_ml[rowi * 2 + 1] = l;
+    }
+    float* dst = a.ws_acc + rowi * D + 2 * c * C::RL;
+    constexpr float kInv = 1.f / 256.f, kLo = 1.f / 4096.f;
+#pragma unroll
+    for (int i = 0; i < C::RL; i += 4) {
+      float4 o0, o1;
+      o0.x = acc[i][0] * kInv + acc[i][2] * kLo;
+      o0.y = acc[i + 1][0] * kInv + acc[i + 1][2] * kLo;
+      o0.z = acc[i + 2][0] * kInv + acc[i + 2][2] * kLo;
+      o0.w = acc[i + 3][0] * kInv + acc[i + 3][2] * kLo;
+      o1.x = acc[i][1] * kInv + acc[i][3] * kLo;
+      o1.y = acc[i + 1][1] * kInv + acc[i + 1][3] * kLo;
+      o1.z = acc[i + 2][1] * kInv + acc[i + 2][3] * kLo;
+      o1.w = acc[i + 3][1] * kInv + acc[i + 3][3] * kLo;
+      *reinterpret_cast<float4*>(dst + i) = o0;
+      *reinterpret_cast<float4*>(dst + C::RL + i) = o1;
+    }
+  };
+
+  int b = find_seq(prefix, a.B, u0);
+  int cur_b = -1;
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int u = u0; u < u1; ++u) {
+    while (prefix[b + 1] <= u) ++b;
+    if (b != cur_b) {
+      if (cur_b >= 0) flush(cur_b);
+      load_q(b);
+      cur_b = b;
+    }
+    const int len = a.seq_lens[b];
+    const int tb = (u - prefix[b]) * C::TS + sub * 32;
+    const int valid = min(32, max(0, len - tb));
+
+    bool ok = mbar_wait(&full[stage], phase, a.err);
+    if (!__all_sync(0xffffffffu, ok)) { *abort_flag = 1; return; }
+
+    if (valid > 0) {
+      const uint8_t* sk = stages + (size_t)stage * C::STAGE + (size_t)(sub * 32) * C::ROW + h * D;
+      const uint8_t* sv = sk + C::KV_BYTES;
+      // ---- S = Q K^T over 32 tokens: 4 n8 blocks ----
+      float S[4][4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.f;
+        const int tok = 16 * (j >> 1) + 4 * (g >> 1) + 2 * (j & 1) + (g & 1);
+        const uint8_t* kr = sk + (size_t)tok * C::ROW + C::RL * c;
+        uint32_t r0[C::KSTEPS], r1[C::KSTEPS];
+        if constexpr (D == 128) {
+          const uint4 x0 = *reinterpret_cast<const uint4*>(kr);
+          const uint4 x1 = *reinterpret_cast<const uint4*>(kr + 64);
+          r0[0] = x0.x; r0[1] = x0.y; r0[2] = x0.z; r0[3] = x0.w;
+          r1[0] = x1.x; r1[1] = x1.y; r1[2] = x1.z; r1[3] = x1.w;
+        } else {
+          const uint2 x0 = *reinterpret_cast<const uint2*>(kr);
+          const uint2 x1 = *reinterpret_cast<const uint2*>(kr + 32);
+          r0[0] = x0.x; r0[1] = x0.y;
+          r1[0] = x1.x; r1[1] = x1.y;
+        }
+#pragma unroll
+        for (int s = 0; s < C::KSTEPS; ++s)
+          mma_e4m3_16832(S[j], q1lo[s], q2lo[s], q1hi[s], q2hi[s], r0[s], r1[s]);
+      }
+      // ---- online softmax (log2 domain), rows g (q1 part) + g+8 (q2 part) ----
+      float sc[4][2];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int tok = 16 * (j >> 1) + 4 * c + 2 * (j & 1) + e;
+          float v = (S[j][e] + S[j][2 + e] * 0.0625f) * qf;
+          v = tok < valid ? v : -INFINITY;
+          sc[j][e] = v;
+          mx = fmaxf(mx, v);
+        }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = fast_exp2(m - m_use);
+      m = m_new;
+      float p[4][2];
+      float ps = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          p[j][e] = fast_exp2(sc[j][e] - m_use);
+          ps += p[j][e];
+        }
+      }
+      l = l * alpha + ps;
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+        for (int i = 0; i < C::DB; ++i) {
+          acc[i][0] *= alpha; acc[i][1] *= alpha; acc[i][2] *= alpha; acc[i][3] *= alpha;
+        }
+      }
+      // ---- P as two e4m3 terms: p*256 ~= p1 + p2/16 ----
+      uint32_t pa[4] = {0, 0, 0, 0};  // a0 (p1, tokens 4c..), a1 (p2), a2 (p1, 16+4c..), a3 (p2)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x0 = p[j][0] * 256.f, x1 = p[j][1] * 256.f;
+        const uint16_t h1 = f2_to_e4m3x2_sat(x0, x1);
+        const __half2 bk = __half2(__nv_cvt_fp8x2_to_halfraw2(h1, __NV_E4M3));
+        const uint16_t h2 = f2_to_e4m3x2_sat((x0 - __low2float(bk)) * 16.f, (x1 - __high2float(bk)) * 16.f);
+        const int reg = (j >> 1) * 2;       // j=0,1 -> a0/a1 ; j=2,3 -> a2/a3
+        const int sh = 16 * (j & 1);
+        pa[reg] |= (uint32_t)h1 << sh;
+        pa[reg + 1] |= (uint32_t)h2 << sh;
+      }
+      // ---- O += P V: V rows (4c+u) and (16+4c+u), columns [RL*g, RL*g + RL) ----
+      const bool tail = valid < 32;
+      uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
+      if (tail) {
+        mlo = 0; mhi = 0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (4 * c + u < valid) mlo |= 0xffu << (8 * u);
+          if (16 + 4 * c + u < valid) mhi |= 0xffu << (8 * u);
+        }
+      }
+      constexpr int VW = C::RL / 4;  // 32-bit words per V run
+      uint32_t vl[4][VW], vh[4][VW];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint8_t* r0p = sv + (size_t)(4 * c + u) * C::ROW + C::RL * g;
+        const uint8_t* r1p = sv + (size_t)(16 + 4 * c + u) * C::ROW + C::RL * g;
+        if constexpr (D == 128) {
+          const uint4 x0 = *reinterpret_cast<const uint4*>(r0p);
+          const uint4 x1 = *reinterpret_cast<const uint4*>(r1p);
+          vl[u][0] = x0.x; vl[u][1] = x0.y; vl[u][2] = x0.z; vl[u][3] = x0.w;
+          vh[u][0] = x1.x; vh[u][1] = x1.y; vh[u][2] = x1.z; vh[u][3] = x1.w;
+        } else {
+          const uint2 x0 = *reinterpret_cast<const uint2*>(r0p);
+          const uint2 x1 = *reinterpret_cast<const uint2*>(r1p);
+          vl[u][0] = x0.x; vl[u][1] = x0.y;
+          vh[u][0] = x1.x; vh[u][1] = x1.y;
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < VW; ++k) {
+        uint32_t b0[4], b1[4];
+        transpose4x4(vl[0][k], vl[1][k], vl[2][k], vl[3][k], b0[0], b0[1], b0[2], b0[3]);
+        transpose4x4(vh[0][k], vh[1][k], vh[2][k], vh[3][k], b1[0], b1[1], b1[2], b1[3]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          mma_e4m3_16832(acc[4 * k + i], pa[0], pa[1], pa[2], pa[3], b0[i] & mlo, b1[i] & mhi);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == C::NS) { stage = 0; phase ^= 1u; }
+  }
+  if (cur_b >= 0) flush(cur_b);
+}
+
+// ---------------------------------------------------------------------------------------
+// Merge: out[b, hq, :] = v_scale[h] * sum_parts 2^(m_i - M) acc_i / sum_parts 2^(m_i - M) l_i
+__global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int NSUB, int D) {
+  extern __shared__ int mprefix[];
+  const int b = blockIdx.x;
+  unit_prefix(a.seq_lens, a.B, TS, mprefix);
+  __syncthreads();
+  const int U = mprefix[a.B];
+  const int uf = mprefix[b], ul = mprefix[b + 1] - 1;
+  const int total = a.Hq * D;
+  if (ul < uf) {
+    for (int e = threadIdx.x; e < total; e += blockDim.x)
+      a.out[(size_t)b * a.ldo + e] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  const int cf = cta_of_unit(U, a.num_ctas, uf), cl = cta_of_unit(U, a.num_ctas, ul);
+  for (int e = threadIdx.x; e < total; e += blockDim.x) {
+    const int hq = e / D, d = e - hq * D;
+    float M = -INFINITY;
+    for (int cc = cf; cc <= cl; ++cc)
+      for (int s = 0; s < NSUB; ++s) {
+        const size_t rowi = ((size_t)(cc + b) * NSUB + s) * a.Hq + hq;
+        M = fmaxf(M, a.ws_ml[rowi * 2]);
+      }
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+      for (int cc = cf; cc <= cl; ++cc)
+        for (int s = 0; s < NSUB; ++s) {
+          const size_t rowi = ((size_t)(cc + b) * NSUB + s) * a.Hq + hq;
+          const float mi = a.ws_ml[rowi * 2];
+          if (mi == -INFINITY) continue;
+          const float w = exp2f(mi - M);
+          L += w * a.ws_ml[rowi * 2 + 1];
+          O += w * a.ws_acc[rowi * D + d];
+        }
+    }
+    const float vs = a.v_scale[hq / a.G];
+    const float r = L > 0.f ? O / L * vs : 0.f;
+    a.out[(size_t)b * a.ldo + e] = __float2bfloat16_rn(r);
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// RoPE + FP8 KV-append.  One CTA per sequence; items = (head, pair).
+__global__ void __launch_bounds__(256) rope_append_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int ldqkv, const int64_t* __restrict__ positions,
+    const int32_t* __restrict__ page_table, int table_ld, int max_pages,
+    const float* __restrict__ inv_freq, const float* __restrict__ k_scale,
+    const float* __restrict__ v_scale, __nv_bfloat16* __restrict__ q_out,
+    uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache, int64_t* __restrict__ slots_out,
+    int Hq, int Hkv, int D, int P, long long num_pages, int* err) {
+  const int b = blockIdx.x;
+  const long long pos = positions[b];
+  const long long lp = pos / P;
+  long long slot = -1;
+  if (pos >= 0 && lp < max_pages) {
+    const int page = page_table[(size_t)b * table_ld + lp];
+    if (page >= 0 && page < num_pages) slot = (long long)page * P + pos % P;
+  }
+  if (threadIdx.x == 0) {
+    if (slot < 0) atomicOr(err, OKC_DEVERR_PAGE);
+    if (slots_out) slots_out[b] = slot;
+  }
+  const int half = D / 2;
+  const int items = (Hq + 2 * Hkv) * half;
+  const __nv_bfloat16* row = qkv + (size_t)b * ldqkv;
+  const float posf = (float)pos;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    const int head = it / half, i = it - head * half;
+    const __nv_bfloat162 xv = *reinterpret_cast<const __nv_bfloat162*>(row + (size_t)head * D + 2 * i);
+    float x0 = __low2float(xv), x1 = __high2float(xv);
+    const bool is_v = head >= Hq + Hkv;
+    if (inv_freq && !is_v) {
+      float sn, cs;
+      sincosf(__fmul_rn(posf, inv_freq[i]), &sn, &cs);
+      const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+      const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
+      x0 = y0;
+      x1 = y1;
+    }
+    if (head < Hq) {
+      *reinterpret_cast<__nv_bfloat162*>(q_out + ((size_t)b * Hq + head) * D + 2 * i) =
+          __floats2bfloat162_rn(x0, x1);
+    } else if (slot >= 0) {
+      const int h = is_v ? head - Hq - Hkv : head - Hq;
+      const float s = is_v ? v_scale[h] : k_scale[h];
+      uint8_t* cache = is_v ? v_cache : k_cache;
+      const uint16_t two = (uint16_t)f_to_e4m3_nosat(__fdiv_rn(x0, s)) |
+                           ((uint16_t)f_to_e4m3_nosat(__fdiv_rn(x1, s)) << 8);
+      *reinterpret_cast<uint16_t*>(cache + ((size_t)slot * Hkv + h) * D + 2 * i) = two;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+template <int D, int HKV>
+static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
+  using C = AttnCfg<D, HKV>;
+  const size_t smem = (size_t)C::NS * C::STAGE + 2 * C::NS * sizeof(uint64_t) + 16 +
+                      (size_t)(a.B + 1) * sizeof(int);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(attn_decode_kernel<D, HKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem + 8192 * 4);
+    configured = true;
+  }
+  attn_decode_kernel<D, HKV><<<a.num_ctas, C::THREADS, smem, stream>>>(a);
+  int st = okc_host::launch_status();
+  if (st) return st;
+  attn_merge_kernel<<<a.B, 256, (size_t)(a.B + 1) * sizeof(int), stream>>>(a, C::TS, C::NSUB, D);
+  return okc_host::launch_status();
+}
+
+int launch_attn_decode(AttnArgs& a, int D, int Hkv, cudaStream_t stream) {
+  if (D == 128) {
+    switch (Hkv) {
+      case 1: return launch_attn_t<128, 1>(a, stream);
+      case 2: return launch_attn_t<128, 2>(a, stream);
+      case 4: return launch_attn_t<128, 4>(a, stream);
+      case 8: return launch_attn_t<128, 8>(a, stream);
+    }
+  } else if (D == 64) {
+    switch (Hkv) {
+      case 1: return launch_attn_t<64, 1>(a, stream);
+      case 2: return launch_attn_t<64, 2>(a, stream);
+      case 4: return launch_attn_t<64, 4>(a, stream);
+      case 8: return launch_attn_t<64, 8>(a, stream);
+    }
+  }
+  return OKC_ERR_INVALID;
+}
+
+int launch_rope_append(const void* qkv, int ldqkv, const int64_t* positions,
+                       const int32_t* page_table, int table_ld, int max_pages,
+                       const float* inv_freq, const float* k_scale, const float* v_scale,
+                       void* q_out, void* k_cache, void* v_cache, int64_t* slots_out, int B,
+                       int Hq, int Hkv, int D, int P, long long num_pages, int* err,
+                       cudaStream_t stream) {
+  rope_append_kernel<<<B, 256, 0, stream>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv), ldqkv, positions, page_table, table_ld, max_pages,
+      inv_freq, k_scale, v_scale, reinterpret_cast<__nv_bfloat16*>(q_out),
+      reinterpret_cast<uint8_t*>(k_cache), reinterpret_cast<uint8_t*>(v_cache), slots_out, Hq, Hkv,
+      D, P, num_pages, err);
+  return okc_host::launch_status();
+}
+
+}  // namespace okc

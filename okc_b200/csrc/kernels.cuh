@@ -1,0 +1,57 @@
+// Internal launcher declarations shared by the entry points (capi.cu) and the kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace okc {
+
+struct AttnArgs {
+  const __nv_bfloat16* q;
+  int ldq;
+  const uint8_t* k_cache;
+  const uint8_t* v_cache;
+  const int32_t* page_table;
+  int table_ld;
+  const int32_t* seq_lens;
+  const float* k_scale;
+  const float* v_scale;
+  __nv_bfloat16* out;
+  int ldo;
+  float* ws_ml;   // [slots][NSUB][Hq][2]: running max (log2 units), running sum
+  float* ws_acc;  // [slots][NSUB][Hq][D]: unnormalised output
+  int* err;
+  int B, Hq, G, P;
+  long long num_pages;
+  float sm_scale_log2;
+  int num_ctas;
+};
+
+int launch_skinny_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
+                       const void* residual, int M, int N, int K, int out_fp32, int splits,
+                       cudaStream_t stream);
+int launch_tc_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
+                   const void* residual, int M, int N, int K, int out_fp32, void* ws, size_t ws_bytes,
+                   cudaStream_t stream);
+size_t tc_gemm_ws_bytes(int M, int N, int K);
+bool tc_gemm_supported(int M, int N, int K, int ldx, int ldw);
+int launch_rmsnorm(const void* x, int ldx, const void* w, void* y, int ldy, int T, int H, float eps,
+                   int unit_offset, cudaStream_t stream);
+int launch_attn_decode(AttnArgs& a, int D, int Hkv, cudaStream_t stream);
+int launch_rope_append(const void* qkv, int ldqkv, const int64_t* positions,
+                       const int32_t* page_table, int table_ld, int max_pages, const float* inv_freq,
+                       const float* k_scale, const float* v_scale, void* q_out, void* k_cache,
+                       void* v_cache, int64_t* slots_out, int B, int Hq, int Hkv, int D, int P,
+                       long long num_pages, int* err, cudaStream_t stream);
+int launch_moe_route(const void* x, const void* wr, int32_t* ids, float* wts, float* logits, int T,
+                     int H, int E, int topk, int renormalize, cudaStream_t stream);
+int launch_moe_permute(const int32_t* ids, int n, int expert_lo, int E, int bm, int32_t* counts,
+                       int32_t* offsets, int32_t* pairs, int32_t* tiles, int max_tiles, int* err,
+                       cudaStream_t stream);
+size_t moe_experts_ws_bytes(int T, int topk, int H, int I);
+int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, const int32_t* counts,
+                       const int32_t* offsets, const int32_t* pairs, const void* w13,
+                       const void* w13_sf, const float* w13_gs, const void* w2, const void* w2_sf,
+                       const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
+                       int E, void* ws, cudaStream_t stream);
+
+}  // namespace okc

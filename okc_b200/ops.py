@@ -1,0 +1,234 @@
+"""Torch-facing wrappers of the okc_b200 C ABI.
+
+Each function validates dtypes/devices, allocates its outputs, passes raw pointers and
+``torch.cuda.current_stream()`` to libokc_b200.so and returns at once (no host sync), so
+every call can be captured in a CUDA graph.  Scratch memory comes from a per-device,
+zero-initialised workspace cache (the reference's `_counters` pattern,
+muse_attention_decode/submission.py:386-397).  There is no CPU path: a tensor that is
+not on a CUDA device raises.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._lib import check
+
+_lib.load()  # fail loudly at import if the native library is absent
+
+_WS: dict[tuple[int, str], torch.Tensor] = {}
+
+
+def _dev_index(t: torch.Tensor) -> int:
+    if not t.is_cuda:
+        raise _lib.OkcError("okc_b200 operators run on CUDA tensors only (no CPU fallback)")
+    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+
+
+def workspace(device: torch.device | int, tag: str, nbytes: int) -> torch.Tensor:
+    """Zero-filled scratch of at least `nbytes`, cached per (device, tag).  Grows (and is
+    re-zeroed) only when a larger size is asked for; allocate before graph capture."""
+    idx = device if isinstance(device, int) else (device.index or 0)
+    key = (idx, tag)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        size = max(int(nbytes), 4096)
+        buf = torch.zeros(size, dtype=torch.uint8, device=f"cuda:{idx}")
+        _WS[key] = buf
+    return buf
+
+
+def read_device_error(tag: str, device: int = 0) -> int:
+    """Reads and clears the device error word of workspace `tag` (synchronises)."""
+    buf = _WS.get((device, tag))
+    if buf is None:
+        return 0
+    with torch.cuda.device(device):
+        return int(_lib.load().okc_read_device_error(buf.data_ptr(), torch.cuda.current_stream(device).cuda_stream))
+
+
+def _stream(dev: int) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def _need(t: torch.Tensor, dtype: torch.dtype, name: str) -> None:
+    if t.dtype != dtype:
+        raise _lib.OkcError(f"{name}: expected {dtype}, got {t.dtype}")
+    if t.dim() >= 1 and t.stride(-1) != 1:
+        raise _lib.OkcError(f"{name}: innermost dimension must be contiguous")
+
+
+# ------------------------------------------------------------------------- projection
+def gemm(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor | None = None,
+         out: torch.Tensor | None = None, out_fp32: bool = False, family: int = 0,
+         splits: int = 0) -> torch.Tensor:
+    """y[M,N] = x[M,K] @ w[N,K]^T (+ residual), fp32 accumulate, one rounding."""
+    dev = _dev_index(x)
+    _need(x, torch.bfloat16, "x")
+    _need(w, torch.bfloat16, "w")
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise _lib.OkcError(f"shape mismatch x {tuple(x.shape)} w {tuple(w.shape)}")
+    if out is None:
+        out = torch.empty((M, N), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=x.device)
+    if residual is not None:
+        _need(residual, torch.bfloat16, "residual")
+        if residual.stride(0) != out.stride(0):
+            raise _lib.OkcError("residual must have the output's row stride")
+    lib = _lib.load()
+    ws = workspace(dev, "gemm", lib.okc_gemm_bf16_workspace_bytes(M, N, K))
+    st = lib.okc_gemm_bf16_ex(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
+                              out.stride(0), _ptr(residual), M, N, K, int(out_fp32), family, splits,
+                              ws.data_ptr(), ws.numel(), _stream(dev))
+    check(st, "okc_gemm_bf16")
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, unit_offset: bool = False,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _dev_index(x)
+    _need(x, torch.bfloat16, "x")
+    _need(w, torch.bfloat16, "w")
+    T, H = x.shape
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    st = _lib.load().okc_rmsnorm_bf16(x.data_ptr(), x.stride(0), w.data_ptr(), out.data_ptr(), out.stride(0),
+                                      T, H, float(eps), int(unit_offset), _stream(dev))
+    check(st, "okc_rmsnorm_bf16")
+    return out
+
+
+# ------------------------------------------------------------------------- attention
+def rope_inv_freq(theta: float, D: int, device) -> torch.Tensor:
+    """inv_freq[i] = 1 / theta^(2i/D) in fp32, computed exactly as the reference does
+    (muse_prefill_layer/submission.py:102)."""
+    return (1.0 / (theta ** (torch.arange(0, D, 2, device=device).float() / D))).contiguous()
+
+
+def rope_kv_append(qkv: torch.Tensor, positions: torch.Tensor, page_table: torch.Tensor,
+                   k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: torch.Tensor,
+                   v_scale: torch.Tensor, Hq: int, Hkv: int, D: int,
+                   inv_freq: torch.Tensor | None, q_out: torch.Tensor | None = None,
+                   slots_out: torch.Tensor | None = None) -> torch.Tensor:
+    """RoPE the new token's q and k, store e4m3 k/v at slot = table[b][pos//P]*P + pos%P.
+    Returns q_out bf16 [B, Hq, D]."""
+    dev = _dev_index(qkv)
+    _need(qkv, torch.bfloat16, "qkv")
+    B = qkv.shape[0]
+    qkv2 = qkv.reshape(B, -1)
+    if q_out is None:
+        q_out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=qkv.device)
+    lib = _lib.load()
+    ws = workspace(dev, "attn", 256)
+    P = k_cache.shape[1]
+    st = lib.okc_rope_kv_append(qkv2.data_ptr(), qkv2.stride(0), positions.data_ptr(), page_table.data_ptr(),
+                                page_table.stride(0), page_table.shape[1], _ptr(inv_freq),
+                                k_scale.data_ptr(), v_scale.data_ptr(), q_out.data_ptr(),
+                                k_cache.data_ptr(), v_cache.data_ptr(), _ptr(slots_out), B, Hq, Hkv, D, P,
+                                k_cache.shape[0], ws.data_ptr(), ws.numel(), _stream(dev))
+    check(st, "okc_rope_kv_append")
+    return q_out
+
+
+def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                page_table: torch.Tensor, seq_lens: torch.Tensor, k_scale: torch.Tensor,
+                v_scale: torch.Tensor, sm_scale: float, out: torch.Tensor | None = None,
+                num_ctas: int = 0) -> torch.Tensor:
+    """Paged FP8 decode attention.  q bf16 [B, Hq, D]; caches e4m3 [pages, P, Hkv, D];
+    page_table int32 [B, max_pages]; seq_lens int32 [B]; scales fp32 [Hkv]."""
+    dev = _dev_index(q)
+    _need(q, torch.bfloat16, "q")
+    B, Hq, D = q.shape
+    pages, P, Hkv, D2 = k_cache.shape
+    if D2 != D or v_cache.shape != k_cache.shape:
+        raise _lib.OkcError("cache shape mismatch")
+    if page_table.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise _lib.OkcError("page_table and seq_lens must be int32")
+    if out is None:
+        out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=q.device)
+    lib = _lib.load()
+    nbytes = lib.okc_attn_decode_workspace_bytes(B, Hq, Hkv, D, num_ctas)
+    ws = workspace(dev, "attn", nbytes)
+    st = lib.okc_attn_decode_fp8(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                 page_table.data_ptr(), page_table.stride(0), seq_lens.data_ptr(),
+                                 k_scale.data_ptr(), v_scale.data_ptr(), out.data_ptr(), out.stride(0),
+                                 B, Hq, Hkv, D, P, pages, float(sm_scale), num_ctas,
+                                 ws.data_ptr(), ws.numel(), _stream(dev))
+    check(st, "okc_attn_decode_fp8")
+    return out
+
+
+# ------------------------------------------------------------------------------- MoE
+def moe_route(x: torch.Tensor, wr: torch.Tensor, topk: int, renormalize: bool = True,
+              return_logits: bool = False):
+    dev = _dev_index(x)
+    _need(x, torch.bfloat16, "x")
+    _need(wr, torch.bfloat16, "router")
+    T, H = x.shape
+    E = wr.shape[0]
+    ids = torch.empty((T, topk), dtype=torch.int32, device=x.device)
+    wts = torch.empty((T, topk), dtype=torch.float32, device=x.device)
+    logits = torch.empty((T, E), dtype=torch.float32, device=x.device) if return_logits else None
+    st = _lib.load().okc_moe_route(x.data_ptr(), wr.data_ptr(), ids.data_ptr(), wts.data_ptr(), _ptr(logits),
+                                   T, H, E, topk, int(renormalize), _stream(dev))
+    check(st, "okc_moe_route")
+    return (ids, wts, logits) if return_logits else (ids, wts)
+
+
+def moe_max_tiles(T: int, topk: int, E_local: int, bm: int) -> int:
+    n = T * topk
+    return min(E_local, n) + (n + bm - 1) // bm
+
+
+def moe_permute(ids: torch.Tensor, expert_lo: int, E_local: int, bm: int = 8) -> dict:
+    dev = _dev_index(ids)
+    T, topk = ids.shape
+    mt = moe_max_tiles(T, topk, E_local, bm)
+    counts = torch.empty(E_local, dtype=torch.int32, device=ids.device)
+    offsets = torch.empty(E_local + 1, dtype=torch.int32, device=ids.device)
+    pairs = torch.empty(T * topk, dtype=torch.int32, device=ids.device)
+    tiles = torch.empty(1 + mt, dtype=torch.int32, device=ids.device)
+    ids_c = ids.contiguous()
+    st = _lib.load().okc_moe_permute(ids_c.data_ptr(), T, topk, expert_lo, E_local, bm, counts.data_ptr(),
+                                     offsets.data_ptr(), pairs.data_ptr(), tiles.data_ptr(), mt, _stream(dev))
+    check(st, "okc_moe_permute")
+    return {"counts": counts, "offsets": offsets, "pairs": pairs, "tiles": tiles}
+
+
+def moe_experts(x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, perm: dict,
+                w13: torch.Tensor, w13_sf: torch.Tensor, w13_gs: torch.Tensor,
+                w2: torch.Tensor, w2_sf: torch.Tensor, w2_gs: torch.Tensor, expert_lo: int,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _dev_index(x)
+    _need(x, torch.bfloat16, "x")
+    T, H = x.shape
+    topk = ids.shape[1]
+    E_local, two_i, _ = w13.shape
+    I = two_i // 2
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+    lib = _lib.load()
+    ws = workspace(dev, "moe", lib.okc_moe_experts_workspace_bytes(T, topk, H, I))
+    st = lib.okc_moe_experts_w4a16(x.data_ptr(), ids.data_ptr(), wts.data_ptr(), perm["counts"].data_ptr(),
+                                   perm["offsets"].data_ptr(), perm["pairs"].data_ptr(), w13.data_ptr(),
+                                   w13_sf.data_ptr(), w13_gs.data_ptr(), w2.data_ptr(), w2_sf.data_ptr(),
+                                   w2_gs.data_ptr(), out.data_ptr(), T, topk, H, I, expert_lo, E_local,
+                                   ws.data_ptr(), ws.numel(), _stream(dev))
+    check(st, "okc_moe_experts_w4a16")
+    return out
+
+
+def attn_workspace_bytes(B: int, Hq: int, Hkv: int, D: int, num_ctas: int = 0) -> int:
+    return int(_lib.load().okc_attn_decode_workspace_bytes(B, Hq, Hkv, D, num_ctas))
+
+
+def sm_scale_default(D: int) -> float:
+    return 1.0 / math.sqrt(D)
