@@ -59,8 +59,8 @@ int okc_read_device_error(const void* workspace, okc_stream_t stream);
  * Picks the split-K skinny kernel (M <= 32, cluster/DSMEM split-K reduction) or the
  * tcgen05 kernel (M >= 33) itself.  out_fp32 != 0 writes fp32 y (a row-parallel partial
  * that an all-reduce sums), else bf16.  residual (bf16, may be NULL) is added to the
- * fp32 accumulator before the single rounding.  K must be a multiple of 8, ldx/ldw/ldy
- * multiples of 8 elements, pointers 16-byte aligned.
+ * fp32 accumulator before the single rounding.  K must be a multiple of 8, ldx/ldw
+ * multiples of 8 elements, x and w 16-byte aligned (y and residual element-aligned).
  * ---------------------------------------------------------------------------------- */
 size_t okc_gemm_bf16_workspace_bytes(int M, int N, int K);
 int okc_gemm_bf16(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,

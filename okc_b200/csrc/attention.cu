@@ -535,11 +535,13 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
   using C = AttnCfg<D, HKV>;
   const size_t smem = (size_t)C::NS * C::STAGE + 2 * C::NS * sizeof(uint64_t) + 16 +
                       (size_t)(a.B + 1) * sizeof(int);
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(attn_decode_kernel<D, HKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem + 8192 * 4);
-    configured = true;
+  static size_t configured = 0;  // largest dynamic smem size set so far for this instance
+  if (smem > 232448) return OKC_ERR_INVALID;  // 227 KB per block on sm_100
+  if (smem > configured) {
+    if (cudaFuncSetAttribute(attn_decode_kernel<D, HKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return OKC_ERR_LAUNCH;
+    configured = smem;
   }
   attn_decode_kernel<D, HKV><<<a.num_ctas, C::THREADS, smem, stream>>>(a);
   int st = okc_host::launch_status();

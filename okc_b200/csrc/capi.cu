@@ -46,10 +46,11 @@ int okc_gemm_bf16_ex(const void* x, int ldx, const void* w, int ldw, void* y, in
                      const void* residual, int M, int N, int K, int out_fp32, int family, int splits,
                      void* workspace, size_t workspace_bytes, okc_stream_t stream) {
   if (!x || !w || !y || M <= 0 || N <= 0 || K <= 0) return OKC_ERR_INVALID;
-  if (K % 8 || ldx % 8 || ldw % 8 || ldy % 8 || ldx < K || ldw < K || ldy < N) return OKC_ERR_INVALID;
-  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (residual && !aligned16(residual)))
-    return OKC_ERR_ALIGNMENT;
-  if (family == 0) family = (M > 32 && okc::tc_gemm_supported(M, N, K, ldx, ldw)) ? 2 : 1;
+  if (K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K || ldy < N) return OKC_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(w)) return OKC_ERR_ALIGNMENT;
+  const uintptr_t ya = reinterpret_cast<uintptr_t>(y), ra = reinterpret_cast<uintptr_t>(residual);
+  if ((ya & (out_fp32 ? 3u : 1u)) || (ra & 1u)) return OKC_ERR_ALIGNMENT;
+  if (family == 0) family = (M > 32 && okc::tc_gemm_supported(M, N, K, ldx, ldw) && ldy % 8 == 0) ? 2 : 1;
   if (family == 2) {
     if (!okc::tc_gemm_supported(M, N, K, ldx, ldw)) return OKC_ERR_INVALID;
     if (!workspace || workspace_bytes < okc_gemm_bf16_workspace_bytes(M, N, K)) return OKC_ERR_WORKSPACE;

@@ -44,6 +44,7 @@ def test_validation_without_device(lib):
     assert lib.okc_gemm_bf16(None, 0, None, 0, None, 0, None, 1, 1, 1, 0, None, 0, None) == _lib.OKC_ERR_INVALID
     assert lib.okc_gemm_bf16(8, 8, 16, 8, 32, 8, None, 1, 8, 12, 0, None, 0, None) == _lib.OKC_ERR_INVALID  # K % 8
     assert lib.okc_gemm_bf16(8, 8, 16, 8, 32, 8, None, 1, 8, 8, 0, None, 0, None) == _lib.OKC_ERR_ALIGNMENT
+    assert lib.okc_gemm_bf16(16, 8, 16, 8, 33, 8, None, 1, 8, 8, 0, None, 0, None) == _lib.OKC_ERR_ALIGNMENT
     assert lib.okc_attn_decode_fp8(16, 64, 16, 16, 16, 4, 16, 16, 16, 16, 64, 1, 9, 8, 64, 16, 4, 0.1, 1,
                                    None, 0, None) == _lib.OKC_ERR_INVALID  # Hq % Hkv
     assert lib.okc_attn_decode_fp8(16, 64, 16, 16, 16, 4, 16, 16, 16, 16, 64, 1, 8, 8, 96, 16, 4, 0.1, 1,
