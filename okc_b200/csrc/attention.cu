@@ -315,29 +315,31 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
     if (valid > 0) {
       const uint8_t* sk = stages + (size_t)stage * C::STAGE + (size_t)(sub * 32) * C::ROW + h * D;
       const uint8_t* sv = sk + C::KV_BYTES;
-      // ---- S = Q K^T over 32 tokens: 4 n8 blocks ----
+      // ---- S = Q K^T over 32 tokens: 4 n8 blocks, k-steps interleaved across blocks ----
       float S[4][4];
+      uint32_t kr0[4][C::KSTEPS], kr1[4][C::KSTEPS];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         S[j][0] = S[j][1] = S[j][2] = S[j][3] = 0.f;
         const int tok = 16 * (j >> 1) + 4 * (g >> 1) + 2 * (j & 1) + (g & 1);
         const uint8_t* kr = sk + (size_t)tok * C::ROW + C::RL * c;
-        uint32_t r0[C::KSTEPS], r1[C::KSTEPS];
         if constexpr (D == 128) {
           const uint4 x0 = *reinterpret_cast<const uint4*>(kr);
           const uint4 x1 = *reinterpret_cast<const uint4*>(kr + 64);
-          r0[0] = x0.x; r0[1] = x0.y; r0[2] = x0.z; r0[3] = x0.w;
-          r1[0] = x1.x; r1[1] = x1.y; r1[2] = x1.z; r1[3] = x1.w;
+          kr0[j][0] = x0.x; kr0[j][1] = x0.y; kr0[j][2] = x0.z; kr0[j][3] = x0.w;
+          kr1[j][0] = x1.x; kr1[j][1] = x1.y; kr1[j][2] = x1.z; kr1[j][3] = x1.w;
         } else {
           const uint2 x0 = *reinterpret_cast<const uint2*>(kr);
           const uint2 x1 = *reinterpret_cast<const uint2*>(kr + 32);
-          r0[0] = x0.x; r0[1] = x0.y;
-          r1[0] = x1.x; r1[1] = x1.y;
+          kr0[j][0] = x0.x; kr0[j][1] = x0.y;
+          kr1[j][0] = x1.x; kr1[j][1] = x1.y;
         }
-#pragma unroll
-        for (int s = 0; s < C::KSTEPS; ++s)
-          mma_e4m3_16832(S[j], q1lo[s], q2lo[s], q1hi[s], q2hi[s], r0[s], r1[s]);
       }
+#pragma unroll
+      for (int s2 = 0; s2 < C::KSTEPS; ++s2)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          mma_e4m3_16832(S[j], q1lo[s2], q2lo[s2], q1hi[s2], q2hi[s2], kr0[j][s2], kr1[j][s2]);
       // ---- online softmax (log2 domain), rows g (q1 part) + g+8 (q2 part) ----
       float sc[4][2];
       float mx = -INFINITY;
@@ -347,7 +349,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
         for (int e = 0; e < 2; ++e) {
           const int tok = 16 * (j >> 1) + 4 * c + 2 * (j & 1) + e;
           float v = (S[j][e] + S[j][2 + e] * 0.0625f) * qf;
-          v = tok < valid ? v : -INFINITY;
+          if (valid < 32) v = tok < valid ? v : -INFINITY;  // warp-uniform: tail tiles only
           sc[j][e] = v;
           mx = fmaxf(mx, v);
         }
@@ -400,32 +402,24 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
         }
       }
       constexpr int VW = C::RL / 4;  // 32-bit words per V run
-      uint32_t vl[4][VW], vh[4][VW];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint8_t* r0p = sv + (size_t)(4 * c + u) * C::ROW + C::RL * g;
-        const uint8_t* r1p = sv + (size_t)(16 + 4 * c + u) * C::ROW + C::RL * g;
-        if constexpr (D == 128) {
-          const uint4 x0 = *reinterpret_cast<const uint4*>(r0p);
-          const uint4 x1 = *reinterpret_cast<const uint4*>(r1p);
-          vl[u][0] = x0.x; vl[u][1] = x0.y; vl[u][2] = x0.z; vl[u][3] = x0.w;
-          vh[u][0] = x1.x; vh[u][1] = x1.y; vh[u][2] = x1.z; vh[u][3] = x1.w;
-        } else {
-          const uint2 x0 = *reinterpret_cast<const uint2*>(r0p);
-          const uint2 x1 = *reinterpret_cast<const uint2*>(r1p);
-          vl[u][0] = x0.x; vl[u][1] = x0.y;
-          vh[u][0] = x1.x; vh[u][1] = x1.y;
+      for (int k = 0; k < VW; ++k) {  // one 4-byte column group (4 d-blocks) at a time
+        uint32_t vl[4], vh[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          vl[u] = *reinterpret_cast<const uint32_t*>(sv + (size_t)(4 * c + u) * C::ROW + C::RL * g + 4 * k);
+          vh[u] = *reinterpret_cast<const uint32_t*>(sv + (size_t)(16 + 4 * c + u) * C::ROW + C::RL * g + 4 * k);
         }
-      }
-#pragma unroll
-      for (int k = 0; k < VW; ++k) {
         uint32_t b0[4], b1[4];
-        transpose4x4(vl[0][k], vl[1][k], vl[2][k], vl[3][k], b0[0], b0[1], b0[2], b0[3]);
-        transpose4x4(vh[0][k], vh[1][k], vh[2][k], vh[3][k], b1[0], b1[1], b1[2], b1[3]);
+        transpose4x4(vl[0], vl[1], vl[2], vl[3], b0[0], b0[1], b0[2], b0[3]);
+        transpose4x4(vh[0], vh[1], vh[2], vh[3], b1[0], b1[1], b1[2], b1[3]);
+        if (tail) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          mma_e4m3_16832(acc[4 * k + i], pa[0], pa[1], pa[2], pa[3], b0[i] & mlo, b1[i] & mhi);
+          for (int i = 0; i < 4; ++i) { b0[i] &= mlo; b1[i] &= mhi; }
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          mma_e4m3_16832(acc[4 * k + i], pa[0], pa[1], pa[2], pa[3], b0[i], b1[i]);
       }
     }
     __syncwarp();

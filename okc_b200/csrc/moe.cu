@@ -30,7 +30,7 @@ namespace okc {
 
 // ---------------------------------------------------------------------------------------
 // Routing
-__global__ void __launch_bounds__(256) route_kernel(const __nv_bfloat16* __restrict__ x,
+__global__ void __launch_bounds__(1024) route_kernel(const __nv_bfloat16* __restrict__ x,
                                                     const __nv_bfloat16* __restrict__ wr,
                                                     int32_t* __restrict__ ids, float* __restrict__ wts,
                                                     float* __restrict__ logits_out, int H, int E,
@@ -44,18 +44,25 @@ __global__ void __launch_bounds__(256) route_kernel(const __nv_bfloat16* __restr
     *reinterpret_cast<uint4*>(xs + i) = *reinterpret_cast<const uint4*>(x + (size_t)t * H + i);
   __syncthreads();
   const int nj = H / 256;
-  for (int e = warp; e < E; e += 8) {
+  const int nwarps = blockDim.x >> 5;
+  for (int e = warp; e < E; e += nwarps) {
     const __nv_bfloat16* we = wr + (size_t)e * H;
     float acc = 0.f;
-    for (int j = 0; j < nj; ++j) {
-      const int k = 256 * j + 8 * lane;
-      const uint4 xv = *reinterpret_cast<const uint4*>(xs + k);
-      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(we + k));
-      const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+    for (int j0 = 0; j0 < nj; j0 += 8) {  // 8 row loads in flight before the first use
+      uint4 wv[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        acc = fmaf(bf16_lo(xa[q]), bf16_lo(wa[q]), acc);
-        acc = fmaf(bf16_hi(xa[q]), bf16_hi(wa[q]), acc);
+      for (int q = 0; q < 8; ++q)
+        if (j0 + q < nj) wv[q] = __ldg(reinterpret_cast<const uint4*>(we + 256 * (j0 + q) + 8 * lane));
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if (j0 + q >= nj) break;
+        const uint4 xv = *reinterpret_cast<const uint4*>(xs + 256 * (j0 + q) + 8 * lane);
+        const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          acc = fmaf(bf16_lo(xa[r]), bf16_lo(wa[r]), acc);
+          acc = fmaf(bf16_hi(xa[r]), bf16_hi(wa[r]), acc);
+        }
       }
     }
 #pragma unroll
@@ -294,10 +301,16 @@ __global__ void __launch_bounds__(kMoeWarps * 32) moe_expert_kernel(
 #pragma unroll
       for (int q = 0; q < 4; ++q) ag[t][q] = au[t][q] = 0.f;
 
+    WTile tg, tu, ng, nu;
+    if (kc0 < kc1) {
+      load_wtile(tg, wg_lo, wg_hi, sg_lo, sg_hi, kc0 * 64, kc0 * 8);
+      if (GATED) load_wtile(tu, wu_lo, wu_hi, su_lo, su_hi, kc0 * 64, kc0 * 8);
+    }
     for (int kc = kc0; kc < kc1; ++kc) {
-      WTile tg, tu;
-      load_wtile(tg, wg_lo, wg_hi, sg_lo, sg_hi, kc * 64, kc * 8);
-      if (GATED) load_wtile(tu, wu_lo, wu_hi, su_lo, su_hi, kc * 64, kc * 8);
+      if (kc + 1 < kc1) {  // next chunk's codes and scales in flight while this one computes
+        load_wtile(ng, wg_lo, wg_hi, sg_lo, sg_hi, (kc + 1) * 64, (kc + 1) * 8);
+        if (GATED) load_wtile(nu, wu_lo, wu_hi, su_lo, su_hi, (kc + 1) * 64, (kc + 1) * 8);
+      }
       const uint32_t sgl[2] = {sf_to_h2(tg.slo & 0xff), sf_to_h2(tg.slo >> 8)};
       const uint32_t sgh[2] = {sf_to_h2(tg.shi & 0xff), sf_to_h2(tg.shi >> 8)};
       uint32_t sul[2] = {0, 0}, suh[2] = {0, 0};
@@ -328,6 +341,8 @@ __global__ void __launch_bounds__(kMoeWarps * 32) moe_expert_kernel(
           }
         }
       }
+      tg = ng;
+      if (GATED) tu = nu;
     }
 
     // epilogue: (optional) cluster reduction, then scale / round / activation / store
@@ -420,7 +435,7 @@ int launch_moe_route(const void* x, const void* wr, int32_t* ids, float* wts, fl
   const size_t smem = (size_t)H * 2 + (size_t)E * 4;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  route_kernel<<<T, 256, smem, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x),
+  route_kernel<<<T, 1024, smem, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x),
                                          reinterpret_cast<const __nv_bfloat16*>(wr), ids, wts, logits,
                                          H, E, topk, renormalize);
   return okc_host::launch_status();

@@ -68,7 +68,7 @@ class DecodeLayer:
 
     def kernels_per_step(self, tokens: int) -> int:
         """Our kernel launches in one step (for the bench's gpu_launches)."""
-        passes = 1 if tokens <= 64 else (tokens + 63) // 64
+        passes = 1 if tokens <= 256 else (tokens + 255) // 256  # tcgen05 GEMM: 256 tokens a launch
         return 1 + passes + 1 + 2 + passes
 
     def step(self, x, positions, page_table, k_cache, v_cache, lens=None, out=None):

@@ -45,7 +45,11 @@ def cache_slots(page_table: torch.Tensor, positions: torch.Tensor, page: int) ->
 
 
 def split_qkv(qkv: torch.Tensor, hq: int, hkv: int, d: int):
-    q, k, v = qkv.float().split([hq * d, hkv * d, hkv * d], dim=-1)[:3]
+    """q | k | v (| Muse's output gate) columns of the fused projection output."""
+    f = qkv.float()
+    q = f[..., :hq * d]
+    k = f[..., hq * d:(hq + hkv) * d]
+    v = f[..., (hq + hkv) * d:(hq + 2 * hkv) * d]
     return q.reshape(-1, hq, d), k.reshape(-1, hkv, d), v.reshape(-1, hkv, d)
 
 

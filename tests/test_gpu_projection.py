@@ -76,3 +76,18 @@ def test_rmsnorm(ops):
         y = ops.rmsnorm(x, w, 1e-6, unit_offset=unit)
         torch.testing.assert_close(y.float().cpu(), ref.rmsnorm(x.cpu(), w.cpu(), 1e-6, unit).float(),
                                    rtol=2e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("M", [33, 48, 64, 65, 100, 128, 200, 256])
+@pytest.mark.parametrize("K,N", [(8192, 10240), (8192, 8192), (4096, 6144), (1000, 300)])
+def test_tcgen05_family(ops, M, K, N):
+    """The tcgen05 kernel (family 2) against the oracle and against the split-K CUDA-core path."""
+    from okc_b200 import synth
+    x, w = synth.projection_case(M, K, N, seed=M + N, device="cuda")
+    y = ops.gemm(x, w, family=2)
+    _close(y, ref.gemm(x.cpu(), w.cpu()), f"tc M{M} K{K} N{N}")
+    r = torch.randn((M, N), device="cuda").to(torch.bfloat16)
+    y2 = ops.gemm(x, w, residual=r, family=2)
+    _close(y2, ref.gemm(x.cpu(), w.cpu(), residual=r.cpu()), f"tc+res M{M}")
+    y3 = ops.gemm(x, w, out_fp32=True, family=2)
+    torch.testing.assert_close(y3.cpu(), ref.gemm(x.cpu(), w.cpu(), out_fp32=True), rtol=1e-3, atol=1e-3)

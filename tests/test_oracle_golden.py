@@ -1,0 +1,67 @@
+"""Pins the CPU oracle to fixtures produced by running the reference's own code
+(tests/golden/make_golden.py): the NVFP4 nibble decoder, the `_route` permutation kernel and
+the prefill layer's rms / rope / route / gated decode attention."""
+
+import json
+from pathlib import Path
+
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle import moe as omoe
+
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+def test_nvfp4_decode_matches_reference_decoder_bit_exactly():
+    table = json.loads((GOLD / "nvfp4_decode.json").read_text())
+    assert len(table["rows"]) == 16 * 7 * 3
+    for code, sf, gs, expected in table["rows"]:
+        packed = torch.tensor([[code | (code << 4)] * 8], dtype=torch.uint8)  # 16 values, one block
+        sfe = torch.tensor([[sf]], dtype=torch.float32).to(torch.float8_e4m3fn)
+        got = omoe.dequantize(packed, sfe, gs)[0, 0].float().item()
+        assert got == expected, (code, sf, gs, got, expected)
+
+
+@pytest.mark.parametrize("idx", range(6))
+def test_permutation_matches_reference_route_kernel(idx):
+    case = json.loads((GOLD / "route_perm.json").read_text())["cases"][idx]
+    ids = torch.tensor(case["ids"], dtype=torch.int32)
+    counts, offsets, pairs, tiles = omoe.permute(ids, case["local_start"], case["local_count"], case["bm"])
+    assert counts.tolist() == case["count"]
+    for e in range(case["local_count"]):
+        assert pairs[offsets[e]:offsets[e + 1]].tolist() == case["pairs"][e]
+    assert tiles.tolist() == case["tiles"]
+
+
+@pytest.fixture(scope="module")
+def pre():
+    return torch.load(GOLD / "prefill_ops.pt", weights_only=False)
+
+
+def test_rms_and_rope_bit_exact(pre):
+    assert torch.equal(oatt.rms(pre["rms_in"]), pre["rms_out"])
+    assert torch.equal(oatt.rope(pre["rope_in"], pre["rope_pos"], 500000.0), pre["rope_out_5e5"])
+    assert torch.equal(oatt.rope(pre["rope_in"], pre["rope_pos"], 10000.0), pre["rope_out_1e4"])
+
+
+def test_muse_route(pre):
+    ids, w = omoe.muse_route(pre["route_h"], pre["route_w"], pre["route_bias"], 8)
+    assert torch.equal(ids, pre["route_ids"])
+    assert torch.equal(w, pre["route_weights"])
+
+
+@pytest.mark.parametrize("i", range(3))
+def test_gated_attention_and_cache_append(pre, i):
+    c = pre["attention_cases"][i]
+    cfg = c["cfg"]
+    qkv = c["x"] @ c["wqkv"].T
+    kc, vc = c["k_cache_in"].clone(), c["v_cache_in"].clone()
+    s = torch.tensor(c["kv_scale"])
+    out = oatt.muse_attention(qkv, c["positions"], c["table"], kc, vc, s, s, cfg)
+    # the append writes the same e4m3 bytes at the same rows
+    assert torch.equal(kc.view(torch.uint8), c["k_cache_out"].view(torch.uint8))
+    assert torch.equal(vc.view(torch.uint8), c["v_cache_out"].view(torch.uint8))
+    assert torch.equal(oatt.cache_slots(c["table"], c["positions"], cfg["page_size"]), c["cache_loc"])
+    torch.testing.assert_close(out.float(), c["out"].float(), rtol=1e-2, atol=1e-2)
