@@ -77,7 +77,7 @@ int okc_gemm_bf16_ex(const void* x, int ldx, const void* w, int ldw, void* y, in
 /* ------------------------------------------------------------------------------------
  * RMSNorm: y[t] = bf16(x[t] * rsqrt(mean(x[t]^2) + eps) * g), g = w or (1 + w).
  * Replaces `_norm` muse_decode_layer/decode/boundaries.py:8-14 and `rms`/`gain`
- * muse_prefill_layer/submission.py:89-96.  x bf16 [T,H] (ldx), w bf16 [H].
+ * muse_prefill_layer/submission.py:89-96.  x bf16 [T,H] (ldx), w bf16 [H], H <= 16384.
  * ---------------------------------------------------------------------------------- */
 int okc_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, int ldy, int T, int H,
                      float eps, int unit_offset, okc_stream_t stream);
@@ -92,7 +92,8 @@ int okc_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, int ldy, in
  * [B, max_pages] (ld = table_ld).  Slot = page_table[b][pos / P] * P + pos % P.
  * Writes q_out bf16 [B, Hq, D] (rotated), k_cache/v_cache e4m3 [num_pages, P, Hkv, D] at
  * the slot (k rotated, / k_scale[h]; v / v_scale[h]; RNE, overflow -> NaN like torch),
- * and slots_out int64 [B] (may be NULL).  inv_freq fp32 [D/2] (NULL = no RoPE).
+ * and slots_out int64 [B] (may be NULL).  inv_freq fp32 [D/2] (NULL = no RoPE).  D % 8 == 0,
+ * D <= 512, ldqkv % 8 == 0, qkv / q_out 16-byte aligned, caches 8-byte aligned.
  * ---------------------------------------------------------------------------------- */
 int okc_rope_kv_append(const void* qkv, int ldqkv, const int64_t* positions,
                        const int32_t* page_table, int table_ld, int max_pages,

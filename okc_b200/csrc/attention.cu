@@ -430,49 +430,65 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
 }
 
 // ---------------------------------------------------------------------------------------
-// Merge: out[b, hq, :] = v_scale[h] * sum_parts 2^(m_i - M) acc_i / sum_parts 2^(m_i - M) l_i
+// Merge: out[b, hq, :] = v_scale[h] * sum_parts 2^(m_i - M) acc_i / sum_parts 2^(m_i - M) l_i.
+// One warp per (sequence, query head); lane owns D/32 consecutive d.  Parts are read in a
+// fixed order, so the result does not depend on which CTA finished first.
 __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int NSUB, int D) {
   extern __shared__ int mprefix[];
   const int b = blockIdx.x;
   unit_prefix(a.seq_lens, a.B, TS, mprefix);
   __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hq = blockIdx.y * 8 + warp;
+  if (hq >= a.Hq) return;
+  const int per = D / 32;  // 4 (D = 128) or 2 (D = 64)
+  __nv_bfloat16* dst = a.out + (size_t)b * a.ldo + (size_t)hq * D + lane * per;
   const int U = mprefix[a.B];
   const int uf = mprefix[b], ul = mprefix[b + 1] - 1;
-  const int total = a.Hq * D;
-  if (ul < uf) {
-    for (int e = threadIdx.x; e < total; e += blockDim.x)
-      a.out[(size_t)b * a.ldo + e] = __float2bfloat16_rn(0.f);
-    return;
-  }
-  const int cf = cta_of_unit(U, a.num_ctas, uf), cl = cta_of_unit(U, a.num_ctas, ul);
-  for (int e = threadIdx.x; e < total; e += blockDim.x) {
-    const int hq = e / D, d = e - hq * D;
+  float o[4] = {0.f, 0.f, 0.f, 0.f};
+  float L = 0.f;
+  if (ul >= uf) {
+    const int cf = cta_of_unit(U, a.num_ctas, uf), cl = cta_of_unit(U, a.num_ctas, ul);
+    const int nparts = (cl - cf + 1) * NSUB;
     float M = -INFINITY;
-    for (int cc = cf; cc <= cl; ++cc)
-      for (int s = 0; s < NSUB; ++s) {
-        const size_t rowi = ((size_t)(cc + b) * NSUB + s) * a.Hq + hq;
-        M = fmaxf(M, a.ws_ml[rowi * 2]);
-      }
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-      for (int cc = cf; cc <= cl; ++cc)
-        for (int s = 0; s < NSUB; ++s) {
-          const size_t rowi = ((size_t)(cc + b) * NSUB + s) * a.Hq + hq;
-          const float mi = a.ws_ml[rowi * 2];
-          if (mi == -INFINITY) continue;
-          const float w = exp2f(mi - M);
-          L += w * a.ws_ml[rowi * 2 + 1];
-          O += w * a.ws_acc[rowi * D + d];
-        }
+    for (int p = lane; p < nparts; p += 32) {
+      const size_t rowi = ((size_t)(cf + p / NSUB + b) * NSUB + p % NSUB) * a.Hq + hq;
+      M = fmaxf(M, a.ws_ml[rowi * 2]);
     }
-    const float vs = a.v_scale[hq / a.G];
-    const float r = L > 0.f ? O / L * vs : 0.f;
-    a.out[(size_t)b * a.ldo + e] = __float2bfloat16_rn(r);
+    M = warp_max(M);
+    if (M != -INFINITY) {
+#pragma unroll 4
+      for (int p = 0; p < nparts; ++p) {
+        const size_t rowi = ((size_t)(cf + p / NSUB + b) * NSUB + p % NSUB) * a.Hq + hq;
+        const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + rowi * 2);
+        if (ml.x == -INFINITY) continue;
+        const float w = exp2f(ml.x - M);
+        L += w * ml.y;
+        const float* src = a.ws_acc + rowi * D + lane * per;
+        if (per == 4) {
+          const float4 v = *reinterpret_cast<const float4*>(src);
+          o[0] += w * v.x; o[1] += w * v.y; o[2] += w * v.z; o[3] += w * v.w;
+        } else {
+          const float2 v = *reinterpret_cast<const float2*>(src);
+          o[0] += w * v.x; o[1] += w * v.y;
+        }
+      }
+    }
+  }
+  const float scale = L > 0.f ? a.v_scale[hq / a.G] / L : 0.f;
+  if (per == 4) {
+    uint2 r;
+    r.x = pack_bf16x2(o[0] * scale, o[1] * scale);
+    r.y = pack_bf16x2(o[2] * scale, o[3] * scale);
+    *reinterpret_cast<uint2*>(dst) = r;
+  } else {
+    *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0] * scale, o[1] * scale);
   }
 }
 
 // ---------------------------------------------------------------------------------------
-// RoPE + FP8 KV-append.  One CTA per sequence; items = (head, pair).
+// RoPE + FP8 KV-append.  grid (B, chunks): each thread owns 8 consecutive elements (4 pairs,
+// one 16-byte load) of the token's q | k | v row; sin/cos are computed once per token.
 __global__ void __launch_bounds__(256) rope_append_kernel(
     const __nv_bfloat16* __restrict__ qkv, int ldqkv, const int64_t* __restrict__ positions,
     const int32_t* __restrict__ page_table, int table_ld, int max_pages,
@@ -488,38 +504,54 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
     const int page = page_table[(size_t)b * table_ld + lp];
     if (page >= 0 && page < num_pages) slot = (long long)page * P + pos % P;
   }
-  if (threadIdx.x == 0) {
+  if (blockIdx.y == 0 && threadIdx.x == 0) {
     if (slot < 0) atomicOr(err, OKC_DEVERR_PAGE);
     if (slots_out) slots_out[b] = slot;
   }
   const int half = D / 2;
-  const int items = (Hq + 2 * Hkv) * half;
-  const __nv_bfloat16* row = qkv + (size_t)b * ldqkv;
-  const float posf = (float)pos;
-  for (int it = threadIdx.x; it < items; it += blockDim.x) {
-    const int head = it / half, i = it - head * half;
-    const __nv_bfloat162 xv = *reinterpret_cast<const __nv_bfloat162*>(row + (size_t)head * D + 2 * i);
-    float x0 = __low2float(xv), x1 = __high2float(xv);
-    const bool is_v = head >= Hq + Hkv;
-    if (inv_freq && !is_v) {
-      float sn, cs;
-      sincosf(__fmul_rn(posf, inv_freq[i]), &sn, &cs);
-      const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
-      const float y1 = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, cs));
-      x0 = y0;
-      x1 = y1;
+  __shared__ float sin_s[256], cos_s[256];  // D <= 512: the angles depend on (pos, pair) only
+  if (inv_freq) {
+    const float posf = (float)pos;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) sincosf(__fmul_rn(posf, inv_freq[i]), &sin_s[i], &cos_s[i]);
+  }
+  __syncthreads();
+  const int e0 = (blockIdx.y * blockDim.x + threadIdx.x) * 8;  // first element of this thread
+  const int total = (Hq + 2 * Hkv) * D;
+  if (e0 >= total) return;
+  const int head = e0 / D, d0 = e0 - head * D;  // D % 8 == 0: the 8 elements share one head
+  const uint4 raw = *reinterpret_cast<const uint4*>(qkv + (size_t)b * ldqkv + e0);
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  float x[8];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) { x[2 * k] = bf16_lo(w[k]); x[2 * k + 1] = bf16_hi(w[k]); }
+  const bool is_v = head >= Hq + Hkv;
+  if (inv_freq && !is_v) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int i = d0 / 2 + k;
+      const float sn = sin_s[i], cs = cos_s[i];
+      const float y0 = __fsub_rn(__fmul_rn(x[2 * k], cs), __fmul_rn(x[2 * k + 1], sn));
+      const float y1 = __fadd_rn(__fmul_rn(x[2 * k], sn), __fmul_rn(x[2 * k + 1], cs));
+      x[2 * k] = y0;
+      x[2 * k + 1] = y1;
     }
-    if (head < Hq) {
-      *reinterpret_cast<__nv_bfloat162*>(q_out + ((size_t)b * Hq + head) * D + 2 * i) =
-          __floats2bfloat162_rn(x0, x1);
-    } else if (slot >= 0) {
-      const int h = is_v ? head - Hq - Hkv : head - Hq;
-      const float s = is_v ? v_scale[h] : k_scale[h];
-      uint8_t* cache = is_v ? v_cache : k_cache;
-      const uint16_t two = (uint16_t)f_to_e4m3_nosat(__fdiv_rn(x0, s)) |
-                           ((uint16_t)f_to_e4m3_nosat(__fdiv_rn(x1, s)) << 8);
-      *reinterpret_cast<uint16_t*>(cache + ((size_t)slot * Hkv + h) * D + 2 * i) = two;
+  }
+  if (head < Hq) {
+    uint4 o;
+    o.x = pack_bf16x2(x[0], x[1]); o.y = pack_bf16x2(x[2], x[3]);
+    o.z = pack_bf16x2(x[4], x[5]); o.w = pack_bf16x2(x[6], x[7]);
+    *reinterpret_cast<uint4*>(q_out + ((size_t)b * Hq + head) * D + d0) = o;
+  } else if (slot >= 0) {
+    const int h = is_v ? head - Hq - Hkv : head - Hq;
+    const float sc = is_v ? v_scale[h] : k_scale[h];
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      lo |= (uint32_t)f_to_e4m3_nosat(__fdiv_rn(x[k], sc)) << (8 * k);
+      hi |= (uint32_t)f_to_e4m3_nosat(__fdiv_rn(x[4 + k], sc)) << (8 * k);
     }
+    uint8_t* cache = is_v ? v_cache : k_cache;
+    *reinterpret_cast<uint2*>(cache + ((size_t)slot * Hkv + h) * D + d0) = make_uint2(lo, hi);
   }
 }
 
@@ -540,7 +572,7 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
   attn_decode_kernel<D, HKV><<<a.num_ctas, C::THREADS, smem, stream>>>(a);
   int st = okc_host::launch_status();
   if (st) return st;
-  attn_merge_kernel<<<a.B, 256, (size_t)(a.B + 1) * sizeof(int), stream>>>(a, C::TS, C::NSUB, D);
+  attn_merge_kernel<<<dim3(a.B, (a.Hq + 7) / 8), 256, (size_t)(a.B + 1) * sizeof(int), stream>>>(a, C::TS, C::NSUB, D);
   return okc_host::launch_status();
 }
 
@@ -569,7 +601,8 @@ int launch_rope_append(const void* qkv, int ldqkv, const int64_t* positions,
                        void* q_out, void* k_cache, void* v_cache, int64_t* slots_out, int B,
                        int Hq, int Hkv, int D, int P, long long num_pages, int* err,
                        cudaStream_t stream) {
-  rope_append_kernel<<<B, 256, 0, stream>>>(
+  const int chunks = ((Hq + 2 * Hkv) * D / 8 + 255) / 256;
+  rope_append_kernel<<<dim3(B, chunks), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), ldqkv, positions, page_table, table_ld, max_pages,
       inv_freq, k_scale, v_scale, reinterpret_cast<__nv_bfloat16*>(q_out),
       reinterpret_cast<uint8_t*>(k_cache), reinterpret_cast<uint8_t*>(v_cache), slots_out, Hq, Hkv,

@@ -82,7 +82,7 @@ int okc_gemm_bf16(const void* x, int ldx, const void* w, int ldw, void* y, int l
 // --------------------------------------------------------------------------- RMSNorm
 int okc_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, int ldy, int T, int H, float eps,
                      int unit_offset, okc_stream_t stream) {
-  if (!x || !w || !y || T <= 0 || H <= 0 || H % 8 || ldx % 8 || ldy % 8) return OKC_ERR_INVALID;
+  if (!x || !w || !y || T <= 0 || H <= 0 || H % 8 || H > 16384 || ldx % 8 || ldy % 8) return OKC_ERR_INVALID;
   if (!aligned16(x) || !aligned16(w) || !aligned16(y)) return OKC_ERR_ALIGNMENT;
   return okc::launch_rmsnorm(x, ldx, w, y, ldy, T, H, eps, unit_offset, stream);
 }
@@ -97,7 +97,10 @@ int okc_rope_kv_append(const void* qkv, int ldqkv, const int64_t* positions, con
   if (!qkv || !positions || !page_table || !k_scale || !v_scale || !q_out || !k_cache || !v_cache)
     return OKC_ERR_INVALID;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || D % 2 || page_size <= 0 || num_pages <= 0 ||
-      max_pages <= 0 || table_ld < max_pages || ldqkv < (Hq + 2 * Hkv) * D || ldqkv % 2)
+      max_pages <= 0 || table_ld < max_pages || ldqkv < (Hq + 2 * Hkv) * D || ldqkv % 8 || D % 8 || D > 512)
+    return OKC_ERR_INVALID;
+  if (!aligned16(qkv) || !aligned16(q_out) || (reinterpret_cast<uintptr_t>(k_cache) & 7) ||
+      (reinterpret_cast<uintptr_t>(v_cache) & 7))
     return OKC_ERR_INVALID;
   if (!workspace || workspace_bytes < 256) return OKC_ERR_WORKSPACE;
   return okc::launch_rope_append(qkv, ldqkv, positions, page_table, table_ld, max_pages, inv_freq,

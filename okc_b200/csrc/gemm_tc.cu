@@ -12,17 +12,15 @@
 //    warp 1 (one thread) issues tcgen05.mma kind::f16 (K = 16 per instruction) with the
 //    accumulator in TMEM and frees each stage with tcgen05.commit;
 //  * all 4 warps drain TMEM with tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = weight
-//    rows) and store y; with split-K the S CTAs of a cluster reduce their partial tiles
-//    through distributed shared memory in a fixed order (deterministic, no workspace).
+//    rows) and store y; with split-K every split stores an fp32 partial tile and the last
+//    CTA of the tile to arrive (self-resetting counter) sums them in split order
+//    (deterministic) — no thread-block clusters, so all CTAs of the grid stay co-resident.
 // Every mbarrier wait is bounded (common.cuh); TMEM is always released before exit.
 // Mirrors the M >= 32 tensor-core path of muse_bf16_proj/projection/kernels/{tma,
 // hopper_ws}.py and muse_decode_layer/decode/projections.py:75-77 (there: cuBLAS / wgmma).
-#include <cooperative_groups.h>
 #include <cudaTypedefs.h>
 
 #include "kernels.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace okc {
 
@@ -34,6 +32,8 @@ struct TcParams {
   void* y;
   const __nv_bfloat16* residual;
   int* err;
+  float* part;    // split-K partial tiles [tiles][splits][128][BN] (workspace)
+  int* counters;  // per-tile arrival counters, zero between calls (the last arriver resets)
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -86,10 +86,7 @@ struct TcCfg {
   static constexpr int A_BYTES = TC_BM * TC_BK * 2;
   static constexpr int B_BYTES = BN * TC_BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
-  static constexpr int RED_LD = BN + 1;
-  static constexpr int RED_BYTES = TC_BM * RED_LD * 4;
-  static constexpr int PIPE = STAGE * STAGES;
-  static constexpr int BODY = PIPE > RED_BYTES ? PIPE : RED_BYTES;
+  static constexpr int BODY = STAGE * STAGES;
   static constexpr int SMEM = 1024 + BODY + 256;  // alignment slack + body + barriers
   static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
 };
@@ -196,33 +193,50 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
       }
     }
   } else {
-    float* red = reinterpret_cast<float*>(smem);  // pipeline buffers are idle now
+    // Split-K: every split stores its fp32 partial tile; the last CTA of the tile to arrive
+    // (self-resetting counter) sums the partials in split order — deterministic — and stores y.
+    float* mine = p.part + ((size_t)tile * p.splits + split) * TC_BM * BN + (size_t)row * BN;
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 16) {
       float v[16];
       tmem_ld16(taddr + c0, v);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) red[row * C::RED_LD + c0 + j] = empty_split ? 0.f : v[j];
+      for (int j = 0; j < 16; j += 4)
+        *reinterpret_cast<float4*>(mine + c0 + j) =
+            empty_split ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     }
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    const int mv = min(p.M, BN);
-    const int total = TC_BM * mv;
-    const int per = (total + p.splits - 1) / p.splits;
-    const int e1 = min(total, (split + 1) * per);
-    for (int e = split * per + (int)threadIdx.x; e < e1; e += blockDim.x) {
-      const int m = e / TC_BM, nl = e % TC_BM;
-      const int nn = n0 + nl;
-      if (nn >= p.N) continue;
-      float r = 0.f;
-      for (int q = 0; q < p.splits; ++q) r += cluster.map_shared_rank(red, q)[nl * C::RED_LD + m];
-      if (p.residual) r += __bfloat162float(p.residual[(size_t)m * p.ldy + nn]);
-      if (p.out_fp32)
-        reinterpret_cast<float*>(p.y)[(size_t)m * p.ldy + nn] = r;
-      else
-        reinterpret_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + nn] = __float2bfloat16_rn(r);
+    __threadfence();
+    __syncthreads();
+    int* last = reinterpret_cast<int*>(const_cast<int*>(abort_flag)) + 1;
+    if (threadIdx.x == 0) *last = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
+    __syncthreads();
+    if (*last) {
+      __threadfence();
+      const int mv = min(p.M, BN);
+      const float* base = p.part + (size_t)tile * p.splits * TC_BM * BN + (size_t)row * BN;
+#pragma unroll 1
+      for (int c0 = 0; c0 < mv; c0 += 4) {
+        float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < p.splits; ++q) {
+          const float4 t4 = __ldcg(reinterpret_cast<const float4*>(base + (size_t)q * TC_BM * BN + c0));
+          acc4.x += t4.x; acc4.y += t4.y; acc4.z += t4.z; acc4.w += t4.w;
+        }
+        const float r4[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
+        if (!ok || n >= p.N) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int m = c0 + j;
+          if (m >= mv) break;
+          float r = r4[j];
+          if (p.residual) r += __bfloat162float(p.residual[(size_t)m * p.ldy + n]);
+          if (p.out_fp32)
+            reinterpret_cast<float*>(p.y)[(size_t)m * p.ldy + n] = r;
+          else
+            reinterpret_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + n] = __float2bfloat16_rn(r);
+        }
+      }
+      if (threadIdx.x == 0) p.counters[tile] = 0;
     }
-    cluster.sync();
   }
 
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -263,11 +277,44 @@ bool tc_gemm_supported(int M, int N, int K, int ldx, int ldw) {
          encode_fn() != nullptr;
 }
 
-size_t tc_gemm_ws_bytes(int, int, int) { return 0; }
+struct TcPlan {
+  int bn, ctas_per_sm, tiles, nkb, splits, kb_per_split;
+};
+
+// Split K so that tiles x splits fills the resident CTA slots of every SM (all CTAs co-resident).
+static TcPlan tc_plan(int M, int N, int K) {
+  TcPlan pl;
+  pl.bn = M <= 64 ? 64 : (M <= 128 ? 128 : 256);
+  pl.ctas_per_sm = pl.bn <= 128 ? 2 : 1;
+  pl.tiles = (N + TC_BM - 1) / TC_BM;
+  pl.nkb = (K + TC_BK - 1) / TC_BK;
+  int s = okc_host::num_sms() * pl.ctas_per_sm / pl.tiles;
+  s = s < 1 ? 1 : (s > 16 ? 16 : s);
+  while (s > 1 && pl.nkb / s < 2) --s;
+  int kbps = (pl.nkb + s - 1) / s;
+  while (s > 1 && (s - 1) * kbps >= pl.nkb) {  // every split owns at least one K block
+    --s;
+    kbps = (pl.nkb + s - 1) / s;
+  }
+  pl.splits = s;
+  pl.kb_per_split = kbps;
+  return pl;
+}
+
+// Workspace: [kTcCounterBytes of per-tile counters at a FIXED offset, so that they stay zero
+// from call to call whatever the shape][fp32 partial tiles].
+constexpr size_t kTcCounterBytes = 16384;  // 4096 tiles of 128 rows: N <= 524288
+
+size_t tc_gemm_ws_bytes(int M, int N, int K) {
+  if (M < 1 || M > 256 || N < 1 || K < 1) return 0;
+  const TcPlan pl = tc_plan(M, N, K);
+  if (pl.splits == 1) return 0;
+  return kTcCounterBytes + (size_t)pl.tiles * pl.splits * TC_BM * pl.bn * 4;
+}
 
 template <int BN, int STAGES>
-static int launch_tc_t(const void* x, int ldx, const void* w, int ldw, TcParams& p, cudaStream_t stream,
-                       int ctas_per_sm) {
+static int launch_tc_t(const void* x, int ldx, const void* w, int ldw, TcParams& p, const TcPlan& pl,
+                       void* ws, size_t ws_bytes, cudaStream_t stream) {
   using C = TcCfg<BN, STAGES>;
   CUtensorMap mw, mx;
   if (!make_map(&mw, w, p.K, p.N, ldw, TC_BM) || !make_map(&mx, x, p.K, p.M, ldx, BN)) return OKC_ERR_INVALID;
@@ -278,36 +325,23 @@ static int launch_tc_t(const void* x, int ldx, const void* w, int ldw, TcParams&
       return OKC_ERR_LAUNCH;
     configured = true;
   }
-  const int tiles = (p.N + TC_BM - 1) / TC_BM;
-  const int nkb = (p.K + TC_BK - 1) / TC_BK;
-  int splits = okc_host::num_sms() * ctas_per_sm / tiles;
-  splits = splits < 1 ? 1 : (splits > 8 ? 8 : splits);
-  while (splits > 1 && nkb / splits < 2) --splits;
-  p.splits = splits;
-  p.kb_per_split = (nkb + splits - 1) / splits;
-  // every split must own at least one K block
-  while (p.splits > 1 && (p.splits - 1) * p.kb_per_split >= nkb) {
-    --p.splits;
-    p.kb_per_split = (nkb + p.splits - 1) / p.splits;
+  p.splits = pl.splits;
+  p.kb_per_split = pl.kb_per_split;
+  p.part = nullptr;
+  p.counters = nullptr;
+  if (pl.splits > 1) {
+    const size_t part_bytes = (size_t)pl.tiles * pl.splits * TC_BM * BN * 4;
+    if (!ws || ws_bytes < kTcCounterBytes + part_bytes || (size_t)pl.tiles * 4 > kTcCounterBytes)
+      return OKC_ERR_WORKSPACE;
+    p.counters = reinterpret_cast<int*>(ws);
+    p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kTcCounterBytes);
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles * p.splits, 1, 1);
-  cfg.blockDim = dim3(128, 1, 1);
-  cfg.dynamicSmemBytes = C::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = p.splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, tc_gemm_kernel<BN, STAGES>, mw, mx, p);
+  tc_gemm_kernel<BN, STAGES><<<pl.tiles * pl.splits, 128, C::SMEM, stream>>>(mw, mx, p);
   return okc_host::launch_status();
 }
 
 int launch_tc_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy, const void* residual, int M,
-                   int N, int K, int out_fp32, void* ws, size_t, cudaStream_t stream) {
+                   int N, int K, int out_fp32, void* ws, size_t ws_bytes, cudaStream_t stream) {
   TcParams p;
   p.M = M;
   p.N = N;
@@ -317,10 +351,10 @@ int launch_tc_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int 
   p.y = y;
   p.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
   p.err = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) - 256);  // the caller's error word
-  if (M <= 64) return launch_tc_t<64, 4>(x, ldx, w, ldw, p, stream, 2);
-  if (M <= 128) return launch_tc_t<128, 3>(x, ldx, w, ldw, p, stream, 2);
-  if (M <= 256) return launch_tc_t<256, 4>(x, ldx, w, ldw, p, stream, 1);
-  return OKC_ERR_INVALID;
+  const TcPlan pl = tc_plan(M, N, K);
+  if (pl.bn == 64) return launch_tc_t<64, 4>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
+  if (pl.bn == 128) return launch_tc_t<128, 3>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
+  return launch_tc_t<256, 4>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
 }
 
 }  // namespace okc

@@ -409,24 +409,32 @@ __global__ void __launch_bounds__(256) to_f16_kernel(const __nv_bfloat16* __rest
   }
 }
 
-__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ y,
-                                                      const int32_t* __restrict__ ids,
-                                                      const float* __restrict__ wts,
-                                                      __nv_bfloat16* __restrict__ out, int topk, int H,
-                                                      int expert_lo, int E) {
+__global__ void __launch_bounds__(64) combine_kernel(const __nv_bfloat16* __restrict__ y,
+                                                     const int32_t* __restrict__ ids,
+                                                     const float* __restrict__ wts,
+                                                     __nv_bfloat16* __restrict__ out, int topk, int H,
+                                                     int expert_lo, int E) {
+  // grid (T, H / 512): 64 threads x 8 elements (one 16-byte load per slot)
   const int t = blockIdx.x;
-  for (int d = threadIdx.x * 2; d < H; d += blockDim.x * 2) {
-    float a0 = 0.f, a1 = 0.f;
-    for (int s = 0; s < topk; ++s) {
-      const int e = ids[(size_t)t * topk + s] - expert_lo;
-      if (e < 0 || e >= E) continue;
-      const float wv = wts[(size_t)t * topk + s];
-      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + ((size_t)t * topk + s) * H + d);
-      a0 = fmaf(wv, __low2float(v), a0);
-      a1 = fmaf(wv, __high2float(v), a1);
+  const int d = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (d >= H) return;
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < topk; ++s) {
+    const int e = ids[(size_t)t * topk + s] - expert_lo;
+    if (e < 0 || e >= E) continue;  // slots routed to other ranks were never written
+    const float wv = wts[(size_t)t * topk + s];
+    const uint4 v = *reinterpret_cast<const uint4*>(y + ((size_t)t * topk + s) * H + d);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      a[2 * k] = fmaf(wv, bf16_lo(u[k]), a[2 * k]);
+      a[2 * k + 1] = fmaf(wv, bf16_hi(u[k]), a[2 * k + 1]);
     }
-    *reinterpret_cast<__nv_bfloat162*>(out + (size_t)t * H + d) = __floats2bfloat162_rn(a0, a1);
   }
+  uint4 o;
+  o.x = pack_bf16x2(a[0], a[1]); o.y = pack_bf16x2(a[2], a[3]);
+  o.z = pack_bf16x2(a[4], a[5]); o.w = pack_bf16x2(a[6], a[7]);
+  *reinterpret_cast<uint4*>(out + (size_t)t * H + d) = o;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -533,8 +541,8 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
   st = launch_expert<false>(T, inter, counts, offsets, pairs, w2, w2_sf, w2_gs, nullptr, y, topk, I, H,
                             I, E, sp2, expert_lo, stream);
   if (st) return st;
-  combine_kernel<<<T, 256, 0, stream>>>(y, ids, wts, reinterpret_cast<__nv_bfloat16*>(out), topk, H,
-                                        expert_lo, E);
+  combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, reinterpret_cast<__nv_bfloat16*>(out),
+                                                               topk, H, expert_lo, E);
   return okc_host::launch_status();
 }
 

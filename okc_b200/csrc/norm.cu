@@ -6,6 +6,9 @@
 
 namespace okc {
 
+constexpr int kNormMaxVec = 8;  // 16-byte vectors per thread: H <= 256 * 8 * 8 = 16384
+
+// Single pass: the row stays in registers between the sum of squares and the scaling.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                                       const __nv_bfloat16* __restrict__ w,
                                                       __nv_bfloat16* __restrict__ y, int ldy, int H,
@@ -14,10 +17,13 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
   const __nv_bfloat16* xr = x + (size_t)t * ldx;
   __nv_bfloat16* yr = y + (size_t)t * ldy;
   __shared__ float red[8];
+  uint4 v[kNormMaxVec];
   float ss = 0.f;
-  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
-    const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
-    const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int i = (j * blockDim.x + threadIdx.x) * 8;
+    v[j] = i < H ? *reinterpret_cast<const uint4*>(xr + i) : make_uint4(0, 0, 0, 0);
+    const uint32_t wv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const float a = bf16_lo(wv[k]), b = bf16_hi(wv[k]);
@@ -30,10 +36,12 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
   float tot = 0.f;
   for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
   const float inv = rsqrtf(tot / (float)H + eps);
-  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
-    const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+#pragma unroll
+  for (int j = 0; j < kNormMaxVec; ++j) {
+    const int i = (j * blockDim.x + threadIdx.x) * 8;
+    if (i >= H) break;
     const uint4 gw = *reinterpret_cast<const uint4*>(w + i);
-    const uint32_t xv[4] = {v.x, v.y, v.z, v.w}, gv[4] = {gw.x, gw.y, gw.z, gw.w};
+    const uint32_t xv[4] = {v[j].x, v[j].y, v[j].z, v[j].w}, gv[4] = {gw.x, gw.y, gw.z, gw.w};
     uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
