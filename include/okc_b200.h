@@ -36,6 +36,7 @@ enum {
   OKC_ERR_WORKSPACE = -3,   /* workspace too small */
   OKC_ERR_LAUNCH = -4,      /* the CUDA launch itself failed */
   OKC_ERR_DEVICE = -5,      /* no sm_100 device / kernel image */
+  OKC_ERR_TOO_LARGE = -6,   /* the request needs more than the fixed scratch of a no-alloc entry point */
 };
 
 enum {
@@ -121,6 +122,21 @@ int okc_attn_decode_fp8(const void* q, int ldq, const void* k_cache, const void*
                         int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
                         float sm_scale, int num_ctas,
                         void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
+/* Same computation as okc_attn_decode_fp8, for callers that cannot allocate device memory
+ * (no counterpart in the reference, whose operators allocate their scratch per call).  The
+ * split-KV partials live in a fixed 16 MiB array inside the library, so the caller passes only
+ * inputs and outputs.  A request whose partials need more than that (okc_attn_decode_workspace_
+ * bytes(B, Hq, Hkv, D, num_ctas) > 16 MiB) returns OKC_ERR_TOO_LARGE.  The array is shared by
+ * every call on a device and keeps the last call's contents: calls that may overlap on the GPU
+ * (streams without ordering between them) race and must not be issued.  The first call on each
+ * device looks up the array's device address (with that device current); make it before any
+ * stream capture.  Device-side error bits are cleared by each call and not reported here. */
+int okc_attn_decode_fp8_noalloc(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                                const int32_t* page_table, int table_ld, const int32_t* seq_lens,
+                                const float* k_scale, const float* v_scale, void* out, int ldo,
+                                int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
+                                float sm_scale, int num_ctas, okc_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
  * MoE routing: logits = bf16(x · Wr^T) (fixed fp32 summation order, see DESIGN),

@@ -20,12 +20,14 @@ OKC_ERR_ALIGNMENT = -2
 OKC_ERR_WORKSPACE = -3
 OKC_ERR_LAUNCH = -4
 OKC_ERR_DEVICE = -5
+OKC_ERR_TOO_LARGE = -6
 ERR_NAMES = {
     OKC_ERR_INVALID: "invalid argument or unsupported shape",
     OKC_ERR_ALIGNMENT: "pointer or leading dimension not 16-byte aligned",
     OKC_ERR_WORKSPACE: "workspace too small",
     OKC_ERR_LAUNCH: "CUDA launch failed",
     OKC_ERR_DEVICE: "no sm_100a device or kernel image",
+    OKC_ERR_TOO_LARGE: "request exceeds the fixed scratch of the no-alloc entry point",
 }
 DEVERR_TIMEOUT, DEVERR_PAGE, DEVERR_INDEX = 1, 2, 4
 
@@ -44,6 +46,8 @@ SIGNATURES: dict[str, tuple] = {
     "okc_attn_decode_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "okc_attn_decode_fp8": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
                                  _i, _i, _i, _i, _i, _i64, _f, _i, _p, _sz, _p]),
+    "okc_attn_decode_fp8_noalloc": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
+                                         _i, _i, _i, _i, _i, _i64, _f, _i, _p]),
     "okc_moe_route": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),
     "okc_moe_permute": (_i, [_p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _i, _p]),
     "okc_moe_experts_workspace_bytes": (_sz, [_i, _i, _i, _i]),
