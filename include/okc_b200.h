@@ -103,6 +103,19 @@ int okc_rope_kv_append(const void* qkv, int ldqkv, const int64_t* positions,
                        int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
                        void* workspace, size_t workspace_bytes, okc_stream_t stream);
 
+/* okc_rope_kv_append plus Muse's query/key treatment (the reference problem's own semantics,
+ * muse_prefill_layer/submission.py:141-147 and muse_attention_decode/submission.py:57-69,252-257):
+ * qk_norm != 0 applies a per-head RMSNorm without weight (eps norm_eps) to q and k before RoPE,
+ * and q is multiplied by q_scale (the qk_scale_factor) before its bf16 rounding.  With
+ * q_scale = 1, qk_norm = 0 it is okc_rope_kv_append.  qk_norm needs D a power of two <= 256. */
+int okc_rope_kv_append_ex(const void* qkv, int ldqkv, const int64_t* positions,
+                          const int32_t* page_table, int table_ld, int max_pages,
+                          const float* inv_freq, const float* k_scale, const float* v_scale,
+                          void* q_out, void* k_cache, void* v_cache, int64_t* slots_out,
+                          int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
+                          float q_scale, int qk_norm, float norm_eps,
+                          void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
 /* ------------------------------------------------------------------------------------
  * Paged FP8 attention decode (q_len = 1), split-KV with a log-sum-exp merge.
  * Replaces `_fused_attn` muse_attention_decode/submission.py:191-351 (its cached-context
@@ -122,6 +135,19 @@ int okc_attn_decode_fp8(const void* q, int ldq, const void* k_cache, const void*
                         int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
                         float sm_scale, int num_ctas,
                         void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
+/* okc_attn_decode_fp8 followed by Muse's output gate (muse_prefill_layer/submission.py:176;
+ * `_epilogue` muse_attention_decode/submission.py:366-383): out = bf16(rms(o) * sigmoid(gate))
+ * with a per-head RMSNorm of the fp32 attention output o (eps out_eps).  gate bf16 [B, Hq*D]
+ * with row stride ld_gate (the gate columns of the fused projection output).  gate = NULL
+ * gives okc_attn_decode_fp8. */
+int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                              const int32_t* page_table, int table_ld, const int32_t* seq_lens,
+                              const float* k_scale, const float* v_scale, void* out, int ldo,
+                              int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
+                              float sm_scale, int num_ctas, const void* gate, int ld_gate,
+                              float out_eps, void* workspace, size_t workspace_bytes,
+                              okc_stream_t stream);
 
 /* Same computation as okc_attn_decode_fp8, for callers that cannot allocate device memory
  * (no counterpart in the reference, whose operators allocate their scratch per call).  The

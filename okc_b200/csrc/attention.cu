@@ -476,13 +476,26 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int
     }
   }
   const float scale = L > 0.f ? a.v_scale[hq / a.G] / L : 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) o[i] *= scale;
+  if (a.gate) {
+    // Muse output gate (muse_prefill_layer/submission.py:176): rms(o) * sigmoid(gate), per head
+    float ss = 0.f;
+    for (int i = 0; i < per; ++i) ss += o[i] * o[i];
+    const float inv = rsqrtf(warp_sum(ss) / (float)D + a.out_eps);
+    const __nv_bfloat16* g = a.gate + (size_t)b * a.ld_gate + (size_t)hq * D + lane * per;
+    for (int i = 0; i < per; ++i) {
+      const float gv = __bfloat162float(g[i]);
+      o[i] = o[i] * inv * (1.f / (1.f + expf(-gv)));
+    }
+  }
   if (per == 4) {
     uint2 r;
-    r.x = pack_bf16x2(o[0] * scale, o[1] * scale);
-    r.y = pack_bf16x2(o[2] * scale, o[3] * scale);
+    r.x = pack_bf16x2(o[0], o[1]);
+    r.y = pack_bf16x2(o[2], o[3]);
     *reinterpret_cast<uint2*>(dst) = r;
   } else {
-    *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0] * scale, o[1] * scale);
+    *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
   }
 }
 
@@ -495,7 +508,7 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
     const float* __restrict__ inv_freq, const float* __restrict__ k_scale,
     const float* __restrict__ v_scale, __nv_bfloat16* __restrict__ q_out,
     uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache, int64_t* __restrict__ slots_out,
-    int Hq, int Hkv, int D, int P, long long num_pages, int* err) {
+    int Hq, int Hkv, int D, int P, long long num_pages, float q_scale, int qk_norm, float norm_eps, int* err) {
   const int b = blockIdx.x;
   const long long pos = positions[b];
   const long long lp = pos / P;
@@ -517,14 +530,30 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
   __syncthreads();
   const int e0 = (blockIdx.y * blockDim.x + threadIdx.x) * 8;  // first element of this thread
   const int total = (Hq + 2 * Hkv) * D;
-  if (e0 >= total) return;
+  const bool active = e0 < total;
   const int head = e0 / D, d0 = e0 - head * D;  // D % 8 == 0: the 8 elements share one head
-  const uint4 raw = *reinterpret_cast<const uint4*>(qkv + (size_t)b * ldqkv + e0);
-  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-  float x[8];
+  float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (active) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(qkv + (size_t)b * ldqkv + e0);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-  for (int k = 0; k < 4; ++k) { x[2 * k] = bf16_lo(w[k]); x[2 * k + 1] = bf16_hi(w[k]); }
+    for (int k = 0; k < 4; ++k) { x[2 * k] = bf16_lo(w[k]); x[2 * k + 1] = bf16_hi(w[k]); }
+  }
   const bool is_v = head >= Hq + Hkv;
+  if (qk_norm) {
+    // Muse's per-head RMSNorm of q and k (muse_prefill_layer/submission.py:144-145): the D/8
+    // threads of a head are consecutive lanes of one warp, reduced with xor shuffles.
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += x[k] * x[k];
+    for (int o = 1; o < D / 8; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (!is_v) {
+      const float inv = rsqrtf(ss / (float)D + norm_eps);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] *= inv;
+    }
+  }
+  if (!active) return;
   if (inv_freq && !is_v) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -537,6 +566,10 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
     }
   }
   if (head < Hq) {
+    if (q_scale != 1.f) {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) x[k] *= q_scale;  // the query scale factor before bf16
+    }
     uint4 o;
     o.x = pack_bf16x2(x[0], x[1]); o.y = pack_bf16x2(x[2], x[3]);
     o.z = pack_bf16x2(x[4], x[5]); o.w = pack_bf16x2(x[6], x[7]);
@@ -599,14 +632,14 @@ int launch_rope_append(const void* qkv, int ldqkv, const int64_t* positions,
                        const int32_t* page_table, int table_ld, int max_pages,
                        const float* inv_freq, const float* k_scale, const float* v_scale,
                        void* q_out, void* k_cache, void* v_cache, int64_t* slots_out, int B,
-                       int Hq, int Hkv, int D, int P, long long num_pages, int* err,
-                       cudaStream_t stream) {
+                       int Hq, int Hkv, int D, int P, long long num_pages, float q_scale, int qk_norm,
+                       float norm_eps, int* err, cudaStream_t stream) {
   const int chunks = ((Hq + 2 * Hkv) * D / 8 + 255) / 256;
   rope_append_kernel<<<dim3(B, chunks), 256, 0, stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(qkv), ldqkv, positions, page_table, table_ld, max_pages,
       inv_freq, k_scale, v_scale, reinterpret_cast<__nv_bfloat16*>(q_out),
       reinterpret_cast<uint8_t*>(k_cache), reinterpret_cast<uint8_t*>(v_cache), slots_out, Hq, Hkv,
-      D, P, num_pages, err);
+      D, P, num_pages, q_scale, qk_norm, norm_eps, err);
   return okc_host::launch_status();
 }
 

@@ -88,24 +88,37 @@ int okc_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, int ldy, in
 }
 
 // ------------------------------------------------------------------- RoPE + append
+int okc_rope_kv_append_ex(const void* qkv, int ldqkv, const int64_t* positions, const int32_t* page_table,
+                          int table_ld, int max_pages, const float* inv_freq, const float* k_scale,
+                          const float* v_scale, void* q_out, void* k_cache, void* v_cache, int64_t* slots_out,
+                          int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages, float q_scale,
+                          int qk_norm, float norm_eps, void* workspace, size_t workspace_bytes,
+                          okc_stream_t stream) {
+  if (!qkv || !positions || !page_table || !k_scale || !v_scale || !q_out || !k_cache || !v_cache)
+    return OKC_ERR_INVALID;
+  if (B <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || D % 2 || page_size <= 0 || num_pages <= 0 ||
+      max_pages <= 0 || table_ld < max_pages || ldqkv < (Hq + 2 * Hkv) * D || ldqkv % 8 || D % 8 || D > 512)
+    return OKC_ERR_INVALID;
+  if (qk_norm && (D > 256 || (D & (D - 1)))) return OKC_ERR_INVALID;  // a head's lanes fit one warp
+  if (!aligned16(qkv) || !aligned16(q_out) || (reinterpret_cast<uintptr_t>(k_cache) & 7) ||
+      (reinterpret_cast<uintptr_t>(v_cache) & 7))
+    return OKC_ERR_ALIGNMENT;
+  if (!workspace || workspace_bytes < 256) return OKC_ERR_WORKSPACE;
+  return okc::launch_rope_append(qkv, ldqkv, positions, page_table, table_ld, max_pages, inv_freq, k_scale,
+                                 v_scale, q_out, k_cache, v_cache, slots_out, B, Hq, Hkv, D, page_size,
+                                 num_pages, q_scale, qk_norm, norm_eps, reinterpret_cast<int*>(workspace),
+                                 stream);
+}
+
 int okc_rope_kv_append(const void* qkv, int ldqkv, const int64_t* positions, const int32_t* page_table,
                        int table_ld, int max_pages, const float* inv_freq, const float* k_scale,
                        const float* v_scale, void* q_out, void* k_cache, void* v_cache,
                        int64_t* slots_out, int B, int Hq, int Hkv, int D, int page_size,
                        int64_t num_pages, void* workspace, size_t workspace_bytes,
                        okc_stream_t stream) {
-  if (!qkv || !positions || !page_table || !k_scale || !v_scale || !q_out || !k_cache || !v_cache)
-    return OKC_ERR_INVALID;
-  if (B <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || D % 2 || page_size <= 0 || num_pages <= 0 ||
-      max_pages <= 0 || table_ld < max_pages || ldqkv < (Hq + 2 * Hkv) * D || ldqkv % 8 || D % 8 || D > 512)
-    return OKC_ERR_INVALID;
-  if (!aligned16(qkv) || !aligned16(q_out) || (reinterpret_cast<uintptr_t>(k_cache) & 7) ||
-      (reinterpret_cast<uintptr_t>(v_cache) & 7))
-    return OKC_ERR_INVALID;
-  if (!workspace || workspace_bytes < 256) return OKC_ERR_WORKSPACE;
-  return okc::launch_rope_append(qkv, ldqkv, positions, page_table, table_ld, max_pages, inv_freq,
-                                 k_scale, v_scale, q_out, k_cache, v_cache, slots_out, B, Hq, Hkv, D,
-                                 page_size, num_pages, reinterpret_cast<int*>(workspace), stream);
+  return okc_rope_kv_append_ex(qkv, ldqkv, positions, page_table, table_ld, max_pages, inv_freq, k_scale,
+                               v_scale, q_out, k_cache, v_cache, slots_out, B, Hq, Hkv, D, page_size, num_pages,
+                               1.0f, 0, 0.0f, workspace, workspace_bytes, stream);
 }
 
 // ------------------------------------------------------------------------ attention
@@ -117,11 +130,13 @@ size_t okc_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int num_ct
   return 256 + ((rows * 2 * 4 + 255) / 256) * 256 + rows * D * 4;
 }
 
-int okc_attn_decode_fp8(const void* q, int ldq, const void* k_cache, const void* v_cache,
-                        const int32_t* page_table, int table_ld, const int32_t* seq_lens,
-                        const float* k_scale, const float* v_scale, void* out, int ldo, int B, int Hq,
-                        int Hkv, int D, int page_size, int64_t num_pages, float sm_scale, int num_ctas,
-                        void* workspace, size_t workspace_bytes, okc_stream_t stream) {
+int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                              const int32_t* page_table, int table_ld, const int32_t* seq_lens,
+                              const float* k_scale, const float* v_scale, void* out, int ldo, int B, int Hq,
+                              int Hkv, int D, int page_size, int64_t num_pages, float sm_scale, int num_ctas,
+                              const void* gate, int ld_gate, float out_eps, void* workspace,
+                              size_t workspace_bytes, okc_stream_t stream) {
+  if (gate && (ld_gate < Hq * D || (reinterpret_cast<uintptr_t>(gate) & 1))) return OKC_ERR_INVALID;
   if (!q || !k_cache || !v_cache || !page_table || !seq_lens || !k_scale || !v_scale || !out)
     return OKC_ERR_INVALID;
   if (B <= 0 || B > 4096 || Hkv <= 0 || Hq % Hkv || Hq / Hkv > 8 || table_ld <= 0 || num_pages <= 0)
@@ -159,7 +174,20 @@ int okc_attn_decode_fp8(const void* q, int ldq, const void* k_cache, const void*
   a.num_pages = num_pages;
   a.sm_scale_log2 = sm_scale * 1.4426950408889634f;
   a.num_ctas = num_ctas;
+  a.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
+  a.ld_gate = ld_gate;
+  a.out_eps = out_eps;
   return okc::launch_attn_decode(a, D, Hkv, stream);
+}
+
+int okc_attn_decode_fp8(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                        const int32_t* page_table, int table_ld, const int32_t* seq_lens,
+                        const float* k_scale, const float* v_scale, void* out, int ldo, int B, int Hq,
+                        int Hkv, int D, int page_size, int64_t num_pages, float sm_scale, int num_ctas,
+                        void* workspace, size_t workspace_bytes, okc_stream_t stream) {
+  return okc_attn_decode_fp8_gated(q, ldq, k_cache, v_cache, page_table, table_ld, seq_lens, k_scale, v_scale,
+                                   out, ldo, B, Hq, Hkv, D, page_size, num_pages, sm_scale, num_ctas, nullptr, 0,
+                                   0.0f, workspace, workspace_bytes, stream);
 }
 
 // ------------------------------------------------------------------------------ MoE

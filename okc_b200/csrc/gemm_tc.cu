@@ -11,14 +11,17 @@
 //    (SWIZZLE_128B, the canonical K-major UMMA layout) into a STAGES-deep mbarrier ring;
 //    warp 1 (one thread) issues tcgen05.mma kind::f16 (K = 16 per instruction) with the
 //    accumulator in TMEM and frees each stage with tcgen05.commit;
-//  * all 4 warps drain TMEM with tcgen05.ld (warp w owns TMEM lanes 32w..32w+31 = weight
-//    rows) and store y; with split-K every split stores an fp32 partial tile and the last
-//    CTA of the tile to arrive (self-resetting counter) sums them in split order
-//    (deterministic) — no thread-block clusters, so all CTAs of the grid stay co-resident.
+//  * persistent stream-K grid (one CTA per SM): the (tile, K-block) units are split evenly
+//    over the CTAs, so every SM streams the same number of bytes whatever N and K are;
+//  * 4 epilogue warps drain the double-buffered TMEM accumulator with tcgen05.ld (warp w owns
+//    TMEM lanes 32(w%4)..+31 = weight rows) while the next segment's MMAs run; a tile split
+//    between CTAs is finished by its last arriving CTA, which sums the fp32 partial slots in
+//    slot order (deterministic; self-resetting per-tile counter).
 // Every mbarrier wait is bounded (common.cuh); TMEM is always released before exit.
 // Mirrors the M >= 32 tensor-core path of muse_bf16_proj/projection/kernels/{tma,
 // hopper_ws}.py and muse_decode_layer/decode/projections.py:75-77 (there: cuBLAS / wgmma).
 #include <cudaTypedefs.h>
+#include <stdlib.h>
 
 #include "kernels.cuh"
 
@@ -28,11 +31,11 @@ constexpr int TC_BM = 128;  // weight rows per tile (MMA M)
 constexpr int TC_BK = 64;   // K elements per stage (128 bytes: one swizzle atom row)
 
 struct TcParams {
-  int M, N, K, ldy, out_fp32, splits, kb_per_split;
+  int M, N, K, ldy, out_fp32, tiles;
   void* y;
   const __nv_bfloat16* residual;
   int* err;
-  float* part;    // split-K partial tiles [tiles][splits][128][BN] (workspace)
+  float* part;    // stream-K partial slots [ctas + tiles][BN][128] (workspace)
   int* counters;  // per-tile arrival counters, zero between calls (the last arriver resets)
 };
 
@@ -81,43 +84,67 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KS = 1>
 struct TcCfg {
-  static constexpr int A_BYTES = TC_BM * TC_BK * 2;
-  static constexpr int B_BYTES = BN * TC_BK * 2;
+  static constexpr int A_BOX = TC_BM * TC_BK * 2;  // one 128 x 64 W box
+  static constexpr int B_BOX = BN * TC_BK * 2;     // one BN x 64 x box
+  static constexpr int A_BYTES = A_BOX * KS;       // KS adjacent K boxes per stage
+  static constexpr int B_BYTES = B_BOX * KS;
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int BODY = STAGE * STAGES;
   static constexpr int SMEM = 1024 + BODY + 256;  // alignment slack + body + barriers
-  static constexpr int TMEM_COLS = BN <= 32 ? 32 : BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr int TMEM_COLS = 2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512));
 };
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_w,
+__host__ __device__ __forceinline__ void sk_range(int U, int C, int c, int& u0, int& u1) {
+  const int q = U / C, r = U % C;
+  u0 = c * q + (c < r ? c : r);
+  u1 = u0 + q + (c < r ? 1 : 0);
+}
+__host__ __device__ __forceinline__ int sk_owner(int U, int C, int u) {
+  const int q = U / C, r = U % C;
+  const int big = r * (q + 1);
+  return u < big ? u / (q + 1) : r + (u - big) / q;
+}
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Persistent stream-K: the (tile, K-block) units of the whole GEMM are split evenly over the
+// grid; a CTA's consecutive units form at most a few segments, one per weight tile it touches.
+// Warp 0: TMA producer.  Warp 1: MMA issuer (double-buffered TMEM accumulator).  Warps 2..5:
+// epilogue (TMEM lane quarter = warp % 4).  A segment that covers its whole tile stores y
+// directly; otherwise it stores an fp32 partial (m-major, coalesced) into slot (CTA + tile) and
+// the last segment of the tile to arrive sums the tile's slots in slot order (deterministic).
+template <int BN, int STAGES, int KS>
+__global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_w,
                                                          const __grid_constant__ CUtensorMap tma_x,
                                                          TcParams p) {
-  using C = TcCfg<BN, STAGES>;
+  using C = TcCfg<BN, STAGES, KS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::BODY);
   uint64_t* empty = full + STAGES;
-  uint64_t* accf = empty + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* accf = empty + STAGES;  // [2] accumulator buffer ready for the epilogue
+  uint64_t* acce = accf + 2;        // [2] accumulator buffer drained by the epilogue
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int split = p.splits > 1 ? (int)(blockIdx.x % p.splits) : 0;
-  const int tile = blockIdx.x / p.splits;
-  const int n0 = tile * TC_BM;
-  const int nkb = (p.K + TC_BK - 1) / TC_BK;
-  const int kb0 = split * p.kb_per_split;
-  const int kb1 = min(nkb, kb0 + p.kb_per_split);
+  const int nkb = (p.K + TC_BK * KS - 1) / (TC_BK * KS);  // stages (units) per tile
+  const int U = p.tiles * nkb;
+  int u0, u1;
+  sk_range(U, gridDim.x, blockIdx.x, u0, u1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(accf, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], 4);  // one arrival per epilogue warp
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -131,111 +158,166 @@ __global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const __grid_constant__
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // ---------------------------- TMA producer ----------------------------
-    int issued = 0;
-    for (int kb = kb0; kb < kb1; ++kb, ++issued) {
-      const int s = issued % STAGES;
-      const uint32_t ph = (uint32_t)(issued / STAGES) & 1u;
-      if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u, p.err)) { *abort_flag = 1; break; }
-      mbar_arrive_expect_tx(&full[s], C::STAGE);
-      uint8_t* sa = smem + s * C::STAGE;
-      tma_load_2d(sa, &tma_w, kb * TC_BK, n0, &full[s]);
-      tma_load_2d(sa + C::A_BYTES, &tma_x, kb * TC_BK, 0, &full[s]);
-    }
-    // make sure this thread's last loads have landed before anyone can leave
-    for (int i = max(0, issued - STAGES); i < issued; ++i)
-      if (!mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, p.err)) break;
-  } else if (warp == 1 && lane == 0) {
-    // ---------------------------- MMA issuer -------------------------------
-    const uint32_t idesc = umma_idesc_bf16(BN);
-    int done = 0;
-    for (int kb = kb0; kb < kb1; ++kb, ++done) {
-      const int s = done % STAGES;
-      const uint32_t ph = (uint32_t)(done / STAGES) & 1u;
-      if (*abort_flag || !mbar_wait(&full[s], ph, p.err)) { *abort_flag = 1; break; }
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t sa = smem_u32(smem + s * C::STAGE);
-      const uint64_t da = umma_desc_sw128(sa), db = umma_desc_sw128(sa + C::A_BYTES);
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------- TMA producer ----------------------------
+      int issued = 0;
+      for (int u = u0; u < u1; ++u, ++issued) {
+        const int s = issued % STAGES;
+        const uint32_t ph = (uint32_t)(issued / STAGES) & 1u;
+        if (*abort_flag || !mbar_wait(&empty[s], ph ^ 1u, p.err)) { *abort_flag = 1; break; }
+        const int tile = u / nkb, kb = u - tile * nkb;
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
+        uint8_t* sa = smem + s * C::STAGE;
 #pragma unroll
-      for (int j = 0; j < TC_BK / 16; ++j)  // +32 bytes per K=16 step inside the swizzle atom
-        umma_bf16(tmem, da + 2 * j, db + 2 * j, idesc, (kb > kb0 || j > 0) ? 1u : 0u);
-      umma_commit(&empty[s]);
-    }
-    umma_commit(accf);  // fires when every MMA above has completed
-  }
-  __syncwarp();
-
-  // ------------------------------ epilogue --------------------------------
-  const bool ok = mbar_wait(accf, 0, p.err);
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const int row = warp * 32 + lane;  // TMEM lane = weight row within the tile
-  const int n = n0 + row;
-  const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-  const bool empty_split = kb1 <= kb0;
-
-  if (p.splits == 1) {
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
-      if (!ok || n >= p.N) continue;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int m = c0 + j;
-        if (m >= p.M) break;
-        float r = empty_split ? 0.f : v[j];
-        if (p.residual) r += __bfloat162float(p.residual[(size_t)m * p.ldy + n]);
-        if (p.out_fp32)
-          reinterpret_cast<float*>(p.y)[(size_t)m * p.ldy + n] = r;
-        else
-          reinterpret_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + n] = __float2bfloat16_rn(r);
+        for (int i = 0; i < KS; ++i) {  // adjacent K boxes back to back: longer DRAM bursts per row
+          tma_load_2d(sa + i * C::A_BOX, &tma_w, (kb * KS + i) * TC_BK, tile * TC_BM, &full[s]);
+          tma_load_2d(sa + C::A_BYTES + i * C::B_BOX, &tma_x, (kb * KS + i) * TC_BK, 0, &full[s]);
+        }
       }
+      for (int i = max(0, issued - STAGES); i < issued; ++i)
+        if (!mbar_wait(&full[i % STAGES], (uint32_t)(i / STAGES) & 1u, p.err)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------- MMA issuer -------------------------------
+      const uint32_t idesc = umma_idesc_bf16(BN);
+      int done = 0, seg = 0;
+      bool first = true;
+      for (int u = u0; u < u1; ++u, ++done) {
+        const int tile = u / nkb, kb = u - tile * nkb;
+        const int buf = seg & 1;
+        if (u == u0 || kb == 0) {  // a new segment: wait until the epilogue freed this buffer
+          if (*abort_flag || !mbar_wait(&acce[buf], ((uint32_t)(seg >> 1) & 1u) ^ 1u, p.err)) {
+            *abort_flag = 1;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          first = true;
+        }
+        const int s = done % STAGES;
+        if (*abort_flag || !mbar_wait(&full[s], (uint32_t)(done / STAGES) & 1u, p.err)) { *abort_flag = 1; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t sa = smem_u32(smem + s * C::STAGE);
+#pragma unroll
+        for (int i = 0; i < KS; ++i) {
+          const uint64_t da = umma_desc_sw128(sa + i * C::A_BOX), db = umma_desc_sw128(sa + C::A_BYTES + i * C::B_BOX);
+#pragma unroll
+          for (int j = 0; j < TC_BK / 16; ++j)
+            umma_bf16(tmem + buf * BN, da + 2 * j, db + 2 * j, idesc, (first && i == 0 && j == 0) ? 0u : 1u);
+        }
+        first = false;
+        umma_commit(&empty[s]);
+        if (u == u1 - 1 || kb == nkb - 1) {  // segment complete: hand the buffer to the epilogue
+          umma_commit(&accf[buf]);
+          ++seg;
+        }
+      }
+      // on abort, release every epilogue wait that can still be pending
+      if (*abort_flag)
+        for (int i = 0; i < 2; ++i) umma_commit(&accf[i]);
     }
   } else {
-    // Split-K: every split stores its fp32 partial tile; the last CTA of the tile to arrive
-    // (self-resetting counter) sums the partials in split order — deterministic — and stores y.
-    float* mine = p.part + ((size_t)tile * p.splits + split) * TC_BM * BN + (size_t)row * BN;
+    // ------------------------------ epilogue -------------------------------
+    const int q4 = warp & 3;
+    const int row = q4 * 32 + lane;  // TMEM lane = weight row within the tile
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const int et = threadIdx.x - 64;  // 0..127 inside the epilogue group
+    const int mv = min(p.M, BN);
+    int seg = 0;
+    for (int u = u0; u < u1; ++seg) {
+      const int tile = u / nkb, kb_first = u - tile * nkb;
+      const int seg_end = min(u1, (tile + 1) * nkb);
+      const bool whole = kb_first == 0 && seg_end == (tile + 1) * nkb;
+      const int buf = seg & 1;
+      const bool ok = mbar_wait(&accf[buf], (uint32_t)(seg >> 1) & 1u, p.err) && !*abort_flag;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int n = tile * TC_BM + row;
+      const uint32_t taddr = tmem + lane_base + buf * BN;
+      if (whole) {
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      float v[16];
-      tmem_ld16(taddr + c0, v);
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(taddr + c0, v);
+          if (!ok || n >= p.N) continue;
 #pragma unroll
-      for (int j = 0; j < 16; j += 4)
-        *reinterpret_cast<float4*>(mine + c0 + j) =
-            empty_split ? make_float4(0.f, 0.f, 0.f, 0.f) : make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-    }
-    __threadfence();
-    __syncthreads();
-    int* last = reinterpret_cast<int*>(const_cast<int*>(abort_flag)) + 1;
-    if (threadIdx.x == 0) *last = atomicAdd(&p.counters[tile], 1) == p.splits - 1;
-    __syncthreads();
-    if (*last) {
-      __threadfence();
-      const int mv = min(p.M, BN);
-      const float* base = p.part + (size_t)tile * p.splits * TC_BM * BN + (size_t)row * BN;
-#pragma unroll 1
-      for (int c0 = 0; c0 < mv; c0 += 4) {
-        float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int q = 0; q < p.splits; ++q) {
-          const float4 t4 = __ldcg(reinterpret_cast<const float4*>(base + (size_t)q * TC_BM * BN + c0));
-          acc4.x += t4.x; acc4.y += t4.y; acc4.z += t4.z; acc4.w += t4.w;
+          for (int j = 0; j < 16; ++j) {
+            const int m = c0 + j;
+            if (m >= p.M) break;
+            float r = v[j];
+            if (p.residual) r += __bfloat162float(p.residual[(size_t)m * p.ldy + n]);
+            if (p.out_fp32)
+              reinterpret_cast<float*>(p.y)[(size_t)m * p.ldy + n] = r;
+            else
+              reinterpret_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + n] = __float2bfloat16_rn(r);
+          }
         }
-        const float r4[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
-        if (!ok || n >= p.N) continue;
+      } else {
+        float* mine = p.part + (size_t)(blockIdx.x + tile) * BN * TC_BM;  // [m][row] for this slot
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[16];
+          tmem_ld16(taddr + c0, v);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int m = c0 + j;
-          if (m >= mv) break;
-          float r = r4[j];
-          if (p.residual) r += __bfloat162float(p.residual[(size_t)m * p.ldy + n]);
-          if (p.out_fp32)
-            reinterpret_cast<float*>(p.y)[(size_t)m * p.ldy + n] = r;
-          else
-            reinterpret_cast<__nv_bfloat16*>(p.y)[(size_t)m * p.ldy + n] = __float2bfloat16_rn(r);
+          for (int j = 0; j < 16; ++j) mine[(size_t)(c0 + j) * TC_BM + row] = v[j];
         }
       }
-      if (threadIdx.x == 0) p.counters[tile] = 0;
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[buf]);  // the MMA warp may reuse this buffer now
+      if (!whole) {
+        const int c_first = sk_owner(U, gridDim.x, tile * nkb);
+        const int c_last = sk_owner(U, gridDim.x, (tile + 1) * nkb - 1);
+        __threadfence();
+        epi_bar();
+        if (et == 0) *last_flag = atomicAdd(&p.counters[tile], 1) == c_last - c_first;
+        epi_bar();
+        if (*last_flag) {
+          __threadfence();
+          // Fixup, bandwidth-bound: thread et owns rows [4*(et%32), +4) of every 4th token m; each
+          // step has one float4 load per slot in flight for 4 tokens (unrolled), and stores a
+          // coalesced quad of 4 consecutive outputs.
+          const int r4 = 4 * (et & 31);
+          const int n4 = tile * TC_BM + r4;
+          const int nslot = c_last - c_first + 1;
+          const float* base = p.part + (size_t)(c_first + tile) * BN * TC_BM + r4;
+#pragma unroll 4
+          for (int m = et >> 5; m < mv; m += 4) {
+            float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q = 0; q < nslot; ++q) {
+              const float4 t4 = __ldcg(reinterpret_cast<const float4*>(base + ((size_t)q * BN + m) * TC_BM));
+              acc4.x += t4.x; acc4.y += t4.y; acc4.z += t4.z; acc4.w += t4.w;
+            }
+            if (!ok) continue;
+            float r[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
+            const size_t o = (size_t)m * p.ldy + n4;
+            if (n4 + 3 < p.N && (o & 3) == 0) {
+              if (p.residual) {
+                const uint2 rv = *reinterpret_cast<const uint2*>(p.residual + o);
+                r[0] += bf16_lo(rv.x); r[1] += bf16_hi(rv.x); r[2] += bf16_lo(rv.y); r[3] += bf16_hi(rv.y);
+              }
+              if (p.out_fp32)
+                *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + o) = make_float4(r[0], r[1], r[2], r[3]);
+              else
+                *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.y) + o) =
+                    make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+            } else {
+              for (int j = 0; j < 4; ++j) {
+                if (n4 + j >= p.N) break;
+                float rv = r[j];
+                if (p.residual) rv += __bfloat162float(p.residual[o + j]);
+                if (p.out_fp32)
+                  reinterpret_cast<float*>(p.y)[o + j] = rv;
+                else
+                  reinterpret_cast<__nv_bfloat16*>(p.y)[o + j] = __float2bfloat16_rn(rv);
+              }
+            }
+          }
+          if (et == 0) p.counters[tile] = 0;
+        }
+        epi_bar();  // last_flag is reused by the next segment
+      }
+      u = seg_end;
     }
   }
 
@@ -278,65 +360,66 @@ bool tc_gemm_supported(int M, int N, int K, int ldx, int ldw) {
 }
 
 struct TcPlan {
-  int bn, ctas_per_sm, tiles, nkb, splits, kb_per_split;
+  int bn, tiles, nkb, ctas, per_sm, ks;
 };
 
-// Split K so that tiles x splits fills the resident CTA slots of every SM (all CTAs co-resident).
+// Variant: "1" = one CTA per SM with 64-wide K stages, "2" = two CTAs per SM, "w" (default) =
+// one CTA per SM with two adjacent 64-wide K boxes per stage (256-byte DRAM bursts per row).
+// OKC_TC_VARIANT selects another one for tuning sweeps.
+static char tc_variant() {
+  static char v = 0;
+  if (!v) {
+    const char* e = getenv("OKC_TC_VARIANT");
+    v = (e && (e[0] == '1' || e[0] == '2' || e[0] == 'w')) ? e[0] : 'w';
+  }
+  return v;
+}
+
+// Persistent grid of (CTAs per SM) x SMs; at most one CTA per (tile, K block) unit.
 static TcPlan tc_plan(int M, int N, int K) {
   TcPlan pl;
   pl.bn = M <= 64 ? 64 : (M <= 128 ? 128 : 256);
-  pl.ctas_per_sm = pl.bn <= 128 ? 2 : 1;
+  const char v = pl.bn == 256 ? '1' : tc_variant();
+  pl.per_sm = v == '2' ? 2 : 1;
+  pl.ks = v == 'w' ? 2 : 1;
   pl.tiles = (N + TC_BM - 1) / TC_BM;
-  pl.nkb = (K + TC_BK - 1) / TC_BK;
-  int s = okc_host::num_sms() * pl.ctas_per_sm / pl.tiles;
-  s = s < 1 ? 1 : (s > 16 ? 16 : s);
-  while (s > 1 && pl.nkb / s < 2) --s;
-  int kbps = (pl.nkb + s - 1) / s;
-  while (s > 1 && (s - 1) * kbps >= pl.nkb) {  // every split owns at least one K block
-    --s;
-    kbps = (pl.nkb + s - 1) / s;
-  }
-  pl.splits = s;
-  pl.kb_per_split = kbps;
+  pl.nkb = (K + TC_BK * pl.ks - 1) / (TC_BK * pl.ks);
+  const long long units = (long long)pl.tiles * pl.nkb;
+  const long long slots = (long long)okc_host::num_sms() * pl.per_sm;
+  pl.ctas = (int)(units < slots ? units : slots);
   return pl;
 }
 
 // Workspace: [kTcCounterBytes of per-tile counters at a FIXED offset, so that they stay zero
-// from call to call whatever the shape][fp32 partial tiles].
+// from call to call whatever the shape][fp32 partial slots: (ctas + tiles) x BN x 128].
 constexpr size_t kTcCounterBytes = 16384;  // 4096 tiles of 128 rows: N <= 524288
 
 size_t tc_gemm_ws_bytes(int M, int N, int K) {
   if (M < 1 || M > 256 || N < 1 || K < 1) return 0;
   const TcPlan pl = tc_plan(M, N, K);
-  if (pl.splits == 1) return 0;
-  return kTcCounterBytes + (size_t)pl.tiles * pl.splits * TC_BM * pl.bn * 4;
+  return kTcCounterBytes + (size_t)(pl.ctas + pl.tiles) * pl.bn * TC_BM * 4;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int KS = 1>
 static int launch_tc_t(const void* x, int ldx, const void* w, int ldw, TcParams& p, const TcPlan& pl,
                        void* ws, size_t ws_bytes, cudaStream_t stream) {
-  using C = TcCfg<BN, STAGES>;
+  using C = TcCfg<BN, STAGES, KS>;
   CUtensorMap mw, mx;
   if (!make_map(&mw, w, p.K, p.N, ldw, TC_BM) || !make_map(&mx, x, p.K, p.M, ldx, BN)) return OKC_ERR_INVALID;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(tc_gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(tc_gemm_kernel<BN, STAGES, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM) != cudaSuccess)
       return OKC_ERR_LAUNCH;
     configured = true;
   }
-  p.splits = pl.splits;
-  p.kb_per_split = pl.kb_per_split;
-  p.part = nullptr;
-  p.counters = nullptr;
-  if (pl.splits > 1) {
-    const size_t part_bytes = (size_t)pl.tiles * pl.splits * TC_BM * BN * 4;
-    if (!ws || ws_bytes < kTcCounterBytes + part_bytes || (size_t)pl.tiles * 4 > kTcCounterBytes)
-      return OKC_ERR_WORKSPACE;
-    p.counters = reinterpret_cast<int*>(ws);
-    p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kTcCounterBytes);
-  }
-  tc_gemm_kernel<BN, STAGES><<<pl.tiles * pl.splits, 128, C::SMEM, stream>>>(mw, mx, p);
+  const size_t part_bytes = (size_t)(pl.ctas + pl.tiles) * BN * TC_BM * 4;
+  if (!ws || ws_bytes < kTcCounterBytes + part_bytes || (size_t)pl.tiles * 4 > kTcCounterBytes)
+    return OKC_ERR_WORKSPACE;
+  p.tiles = pl.tiles;
+  p.counters = reinterpret_cast<int*>(ws);
+  p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kTcCounterBytes);
+  tc_gemm_kernel<BN, STAGES, KS><<<pl.ctas, 192, C::SMEM, stream>>>(mw, mx, p);
   return okc_host::launch_status();
 }
 
@@ -352,8 +435,16 @@ int launch_tc_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int 
   p.residual = reinterpret_cast<const __nv_bfloat16*>(residual);
   p.err = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(ws) - 256);  // the caller's error word
   const TcPlan pl = tc_plan(M, N, K);
-  if (pl.bn == 64) return launch_tc_t<64, 4>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
-  if (pl.bn == 128) return launch_tc_t<128, 3>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
+  if (pl.bn == 64) {
+    if (pl.ks == 2) return launch_tc_t<64, 4, 2>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
+    return pl.per_sm == 2 ? launch_tc_t<64, 4>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream)
+                          : launch_tc_t<64, 8>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
+  }
+  if (pl.bn == 128) {
+    if (pl.ks == 2) return launch_tc_t<128, 3, 2>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
+    return pl.per_sm == 2 ? launch_tc_t<128, 3>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream)
+                          : launch_tc_t<128, 6>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
+  }
   return launch_tc_t<256, 4>(x, ldx, w, ldw, p, pl, ws, ws_bytes, stream);
 }
 

@@ -24,6 +24,9 @@ struct AttnArgs {
   long long num_pages;
   float sm_scale_log2;
   int num_ctas;
+  const __nv_bfloat16* gate;  // optional output gate (Muse): out = rms(o) * sigmoid(gate)
+  int ld_gate;
+  float out_eps;
 };
 
 int launch_skinny_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
@@ -41,7 +44,8 @@ int launch_rope_append(const void* qkv, int ldqkv, const int64_t* positions,
                        const int32_t* page_table, int table_ld, int max_pages, const float* inv_freq,
                        const float* k_scale, const float* v_scale, void* q_out, void* k_cache,
                        void* v_cache, int64_t* slots_out, int B, int Hq, int Hkv, int D, int P,
-                       long long num_pages, int* err, cudaStream_t stream);
+                       long long num_pages, float q_scale, int qk_norm, float norm_eps, int* err,
+                       cudaStream_t stream);
 int launch_moe_route(const void* x, const void* wr, int32_t* ids, float* wts, float* logits, int T,
                      int H, int E, int topk, int renormalize, cudaStream_t stream);
 int launch_moe_permute(const int32_t* ids, int n, int expert_lo, int E, int bm, int32_t* counts,

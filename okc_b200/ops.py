@@ -117,8 +117,10 @@ def rope_kv_append(qkv: torch.Tensor, positions: torch.Tensor, page_table: torch
                    k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: torch.Tensor,
                    v_scale: torch.Tensor, Hq: int, Hkv: int, D: int,
                    inv_freq: torch.Tensor | None, q_out: torch.Tensor | None = None,
-                   slots_out: torch.Tensor | None = None) -> torch.Tensor:
+                   slots_out: torch.Tensor | None = None, q_scale: float = 1.0,
+                   qk_norm: bool = False, norm_eps: float = 1e-5) -> torch.Tensor:
     """RoPE the new token's q and k, store e4m3 k/v at slot = table[b][pos//P]*P + pos%P.
+    qk_norm / q_scale add Muse's per-head QK RMSNorm and query scale factor.
     Returns q_out bf16 [B, Hq, D]."""
     dev = _dev_index(qkv)
     _need(qkv, torch.bfloat16, "qkv")
@@ -129,21 +131,24 @@ def rope_kv_append(qkv: torch.Tensor, positions: torch.Tensor, page_table: torch
     lib = _lib.load()
     ws = workspace(dev, "attn", 256)
     P = k_cache.shape[1]
-    st = lib.okc_rope_kv_append(qkv2.data_ptr(), qkv2.stride(0), positions.data_ptr(), page_table.data_ptr(),
-                                page_table.stride(0), page_table.shape[1], _ptr(inv_freq),
-                                k_scale.data_ptr(), v_scale.data_ptr(), q_out.data_ptr(),
-                                k_cache.data_ptr(), v_cache.data_ptr(), _ptr(slots_out), B, Hq, Hkv, D, P,
-                                k_cache.shape[0], ws.data_ptr(), ws.numel(), _stream(dev))
-    check(st, "okc_rope_kv_append")
+    st = lib.okc_rope_kv_append_ex(qkv2.data_ptr(), qkv2.stride(0), positions.data_ptr(), page_table.data_ptr(),
+                                   page_table.stride(0), page_table.shape[1], _ptr(inv_freq),
+                                   k_scale.data_ptr(), v_scale.data_ptr(), q_out.data_ptr(),
+                                   k_cache.data_ptr(), v_cache.data_ptr(), _ptr(slots_out), B, Hq, Hkv, D, P,
+                                   k_cache.shape[0], float(q_scale), int(qk_norm), float(norm_eps),
+                                   ws.data_ptr(), ws.numel(), _stream(dev))
+    check(st, "okc_rope_kv_append_ex")
     return q_out
 
 
 def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                 page_table: torch.Tensor, seq_lens: torch.Tensor, k_scale: torch.Tensor,
                 v_scale: torch.Tensor, sm_scale: float, out: torch.Tensor | None = None,
-                num_ctas: int = 0) -> torch.Tensor:
+                num_ctas: int = 0, gate: torch.Tensor | None = None,
+                out_eps: float = 1e-5) -> torch.Tensor:
     """Paged FP8 decode attention.  q bf16 [B, Hq, D]; caches e4m3 [pages, P, Hkv, D];
-    page_table int32 [B, max_pages]; seq_lens int32 [B]; scales fp32 [Hkv]."""
+    page_table int32 [B, max_pages]; seq_lens int32 [B]; scales fp32 [Hkv].  With `gate`
+    (bf16 [B, >= Hq*D], Muse's output gate) the result is rms(o) * sigmoid(gate) per head."""
     dev = _dev_index(q)
     _need(q, torch.bfloat16, "q")
     B, Hq, D = q.shape
@@ -152,16 +157,19 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
         raise _lib.OkcError("cache shape mismatch")
     if page_table.dtype != torch.int32 or seq_lens.dtype != torch.int32:
         raise _lib.OkcError("page_table and seq_lens must be int32")
+    if gate is not None:
+        _need(gate, torch.bfloat16, "gate")
     if out is None:
         out = torch.empty((B, Hq, D), dtype=torch.bfloat16, device=q.device)
     lib = _lib.load()
     nbytes = lib.okc_attn_decode_workspace_bytes(B, Hq, Hkv, D, num_ctas)
     ws = workspace(dev, "attn", nbytes)
-    st = lib.okc_attn_decode_fp8(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
-                                 page_table.data_ptr(), page_table.stride(0), seq_lens.data_ptr(),
-                                 k_scale.data_ptr(), v_scale.data_ptr(), out.data_ptr(), out.stride(0),
-                                 B, Hq, Hkv, D, P, pages, float(sm_scale), num_ctas,
-                                 ws.data_ptr(), ws.numel(), _stream(dev))
+    st = lib.okc_attn_decode_fp8_gated(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                       page_table.data_ptr(), page_table.stride(0), seq_lens.data_ptr(),
+                                       k_scale.data_ptr(), v_scale.data_ptr(), out.data_ptr(), out.stride(0),
+                                       B, Hq, Hkv, D, P, pages, float(sm_scale), num_ctas, _ptr(gate),
+                                       0 if gate is None else gate.stride(0), float(out_eps),
+                                       ws.data_ptr(), ws.numel(), _stream(dev))
     check(st, "okc_attn_decode_fp8")
     return out
 
