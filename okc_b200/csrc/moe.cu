@@ -21,6 +21,7 @@
 // Roofline: HBM, algorithmic bytes = (#experts hit) * (W13 + sf + W2 + sf) bytes + activations.
 // Mirrors muse_moe_w4a16/submission.py:163-308 and muse_decode_layer/decode/nvfp4_gemv.py:9-75.
 #include <cooperative_groups.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 
@@ -210,6 +211,15 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   return r;
 }
 
+// One 32-bit word of packed codes (8 values, bytes b0..b3) -> four f16x2 (byte i -> hi, lo pair).
+__device__ __forceinline__ void e2m1_word_to_f16x2(uint32_t w, uint32_t& h0, uint32_t& h1, uint32_t& h2, uint32_t& h3) {
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(h0), "=r"(h1), "=r"(h2), "=r"(h3)
+      : "r"(w));
+}
+
 __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
   __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
   return *reinterpret_cast<uint32_t*>(&r);
@@ -248,7 +258,7 @@ __device__ __forceinline__ uint32_t code_byte(const uint4& v, int i) {
 // GATED: inter = bf16(silu(g) * u) over rows [0, I) (gate) and [I, 2I) (up) of W13;
 // else y rows of W2.  x16: f16 activations [rows][K] (K = H for GATED, I for down).
 template <int MT, bool GATED>
-__global__ void __launch_bounds__(kMoeWarps * 32) moe_expert_kernel(
+__global__ void __launch_bounds__(kMoeWarps * 32, 1) moe_expert_kernel(
     const __half* __restrict__ xin, const int32_t* __restrict__ counts,
     const int32_t* __restrict__ offsets, const int32_t* __restrict__ pairs,
     const uint8_t* __restrict__ w, const uint8_t* __restrict__ sf, const float* __restrict__ gs,
@@ -321,16 +331,22 @@ __global__ void __launch_bounds__(kMoeWarps * 32) moe_expert_kernel(
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
         const int grp = s >> 2;
-        const uint32_t a0 = hmul2u(e2m1x2_to_f16x2(code_byte(tg.lo, 2 * s)), sgl[grp]);
-        const uint32_t a1 = hmul2u(e2m1x2_to_f16x2(code_byte(tg.hi, 2 * s)), sgh[grp]);
-        const uint32_t a2 = hmul2u(e2m1x2_to_f16x2(code_byte(tg.lo, 2 * s + 1)), sgl[grp]);
-        const uint32_t a3 = hmul2u(e2m1x2_to_f16x2(code_byte(tg.hi, 2 * s + 1)), sgh[grp]);
+        const bool odd = s & 1;
+        uint32_t q0, q1, q2, q3, r0, r1, r2, r3;
+        e2m1_word_to_f16x2((&tg.lo.x)[s >> 1], q0, q1, q2, q3);
+        e2m1_word_to_f16x2((&tg.hi.x)[s >> 1], r0, r1, r2, r3);
+        const uint32_t a0 = hmul2u(odd ? q2 : q0, sgl[grp]);
+        const uint32_t a1 = hmul2u(odd ? r2 : r0, sgh[grp]);
+        const uint32_t a2 = hmul2u(odd ? q3 : q1, sgl[grp]);
+        const uint32_t a3 = hmul2u(odd ? r3 : r1, sgh[grp]);
         uint32_t u0 = 0, u1 = 0, u2 = 0, u3 = 0;
         if (GATED) {
-          u0 = hmul2u(e2m1x2_to_f16x2(code_byte(tu.lo, 2 * s)), sul[grp]);
-          u1 = hmul2u(e2m1x2_to_f16x2(code_byte(tu.hi, 2 * s)), suh[grp]);
-          u2 = hmul2u(e2m1x2_to_f16x2(code_byte(tu.lo, 2 * s + 1)), sul[grp]);
-          u3 = hmul2u(e2m1x2_to_f16x2(code_byte(tu.hi, 2 * s + 1)), suh[grp]);
+          e2m1_word_to_f16x2((&tu.lo.x)[s >> 1], q0, q1, q2, q3);
+          e2m1_word_to_f16x2((&tu.hi.x)[s >> 1], r0, r1, r2, r3);
+          u0 = hmul2u(odd ? q2 : q0, sul[grp]);
+          u1 = hmul2u(odd ? r2 : r0, suh[grp]);
+          u2 = hmul2u(odd ? q3 : q1, sul[grp]);
+          u3 = hmul2u(odd ? r3 : r1, suh[grp]);
         }
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
@@ -391,6 +407,294 @@ __global__ void __launch_bounds__(kMoeWarps * 32) moe_expert_kernel(
       cluster.sync();
     }
   }
+}
+
+// ---------------------------------------------------------------------------------------
+// Pipelined expert kernel.  A unit = RT*16 consecutive output rows of one active expert over the
+// full K: for GATED the gate rows [r0, r0 + RT*16) and the up rows I + [r0, ...), each one
+// contiguous span of codes and one of scales in HBM, moved by cp.async.bulk (1 or 2 matrices x
+// (codes + scales)) into an NS-deep shared-memory ring by warp 8.  Warps 0..7 = RT m-tiles x WK
+// K-slices: each decodes its rows' codes from shared memory (cvt.rn.f16x2.e2m1x2, x e4m3 scale)
+// and runs f16 mma.sync against the expert's token rows of x (L1/L2); the WK partial sums meet in
+// shared memory, are scaled by gs, rounded, activated (GATED: silu(g) * u) and stored.
+// Persistent grid: every CTA derives the active-expert list from `counts` and takes an equal
+// contiguous range of units, so only experts that received tokens are streamed.
+template <bool GATED, int RT, int WK, int MT, int NS>
+struct MoeCfg {
+  static constexpr int ROWS = RT * 16;
+  static constexpr int MATS = GATED ? 2 : 1;
+  static constexpr int MTOK = MT * 8;
+};
+
+template <bool GATED, int RT, int WK, int MT, int NS>
+__global__ void __launch_bounds__(288, 1) moe_pipe_kernel(
+    const __half* __restrict__ xin, const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ pairs, const uint8_t* __restrict__ w, const uint8_t* __restrict__ sf,
+    const float* __restrict__ gs, __half* __restrict__ inter_out, __nv_bfloat16* __restrict__ y_out, int topk,
+    int K, int NR, int I, int E, int* err) {
+  using C = MoeCfg<GATED, RT, WK, MT, NS>;
+  extern __shared__ __align__(128) uint8_t msm[];
+  const int code_row = K / 2, sf_row = K / 16;
+  const int mat_bytes = C::ROWS * (code_row + sf_row);          // codes then scales of one matrix
+  const int stage_bytes = (C::MATS * mat_bytes + 127) / 128 * 128;
+  uint8_t* stages = msm;
+  float* red = reinterpret_cast<float*>(msm + (size_t)NS * stage_bytes);  // [8 warps][ROWS/RT=16][MTOK][2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(red + 8 * 16 * C::MTOK * 2);
+  uint64_t* empty = full + NS;
+  int* act = reinterpret_cast<int*>(empty + NS);  // [E + 1]: active expert list, act[E] = count
+  volatile int* abort_flag = act + E + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {  // ordered list of experts with tokens
+    int base = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const bool on = e < E && counts[e] > 0;
+      const unsigned bal = __ballot_sync(0xffffffffu, on);
+      if (on) act[base + __popc(bal & ((1u << lane) - 1u))] = e;
+      base += __popc(bal);
+    }
+    if (lane == 0) act[E] = base;
+  }
+  __syncthreads();
+  const int rb_per_expert = NR / C::ROWS;
+  const int U = act[E] * rb_per_expert;
+  const int q = U / (int)gridDim.x, r = U % (int)gridDim.x;
+  const int u0 = blockIdx.x * q + min((int)blockIdx.x, r);
+  const int u1 = u0 + q + ((int)blockIdx.x < r ? 1 : 0);
+  if (u0 >= u1) return;
+  const int rows_w = GATED ? 2 * I : NR;
+
+  if (warp == 8) {
+    // ------------------------------- producer -------------------------------
+    const uint64_t pol = l2_evict_first_policy();
+    int stage = 0;
+    uint32_t phase = 0;
+    int issued = 0;
+    for (int u = u0; u < u1; ++u) {
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait(&empty[stage], phase ^ 1u, err) && !*abort_flag;
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) { *abort_flag = 1; break; }
+      const int e = act[u / rb_per_expert];
+      const int r0 = (u % rb_per_expert) * C::ROWS;
+      if (lane == 0) mbar_arrive_expect_tx(&full[stage], (uint32_t)(C::MATS * mat_bytes));
+      __syncwarp();
+      uint8_t* dst = stages + (size_t)stage * stage_bytes;
+      if (lane < 2 * C::MATS) {
+        const int m = lane >> 1, part = lane & 1;  // (matrix, codes|scales)
+        const size_t row = (size_t)e * rows_w + r0 + (m ? I : 0);
+        const uint8_t* src = part == 0 ? w + row * code_row : sf + row * sf_row;
+        const uint32_t bytes = (uint32_t)(C::ROWS * (part == 0 ? code_row : sf_row));
+        uint8_t* d = dst + m * mat_bytes + (part == 0 ? 0 : C::ROWS * code_row);
+        bulk_g2s(d, src, bytes, &full[stage], pol);
+      }
+      ++issued;
+      if (++stage == NS) { stage = 0; phase ^= 1u; }
+    }
+    if (lane == 0) {  // make sure this warp's copies have landed before leaving
+      int s = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < min(issued, NS); ++i) {
+        if (--s < 0) { s = NS - 1; ph ^= 1u; }
+        if (!mbar_wait(&full[s], ph, err)) break;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------- consumers --------------------------------
+  const int g = lane >> 2, c = lane & 3;
+  const int mt = warp / WK, ks = warp % WK;       // m-tile of the unit, K slice
+  const int kslice = K / WK;                      // multiple of 128
+  const int nck = kslice / 128;
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int u = u0; u < u1; ++u) {
+    const int e = act[u / rb_per_expert];
+    const int r0 = (u % rb_per_expert) * C::ROWS;
+    const int n_e = counts[e], off = offsets[e];
+    const float gsc = gs[e];
+    // No early return: after a timed-out wait this warp skips the math but still takes every
+    // named barrier below (their count depends only on n_e, the same for all 8 warps).
+    const bool ok = *abort_flag ? false : mbar_wait(&full[stage], phase, err);
+    const bool skip = !__all_sync(0xffffffffu, ok);
+    if (skip) *abort_flag = 1;
+    const uint8_t* sbase = stages + (size_t)stage * stage_bytes;
+    for (int pc = 0; pc < n_e; pc += C::MTOK) {
+      const int ntile = min(MT, (n_e - pc + 7) / 8);
+      const __half* xrow[MT];
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        const int i = pc + 8 * t + g;
+        int xr = 0;
+        if (i < n_e) xr = GATED ? pairs[off + i] / topk : off + i;
+        xrow[t] = xin + (size_t)xr * K + ks * kslice + 32 * c;
+      }
+      float ag[MT][4], au[MT][4];
+#pragma unroll
+      for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int z = 0; z < 4; ++z) ag[t][z] = au[t][z] = 0.f;
+      // x fragments of a whole 128-chunk (8 MMA steps) come in one batch of 16-byte loads; with
+      // MT <= 2 the next chunk's batch is in flight while this chunk computes.
+      constexpr bool kPrefetch = MT <= 2;
+      uint4 xcur[MT][4], xnext[MT][4];
+      auto load_x = [&](uint4 (&dst)[MT][4], int ck) {
+#pragma unroll
+        for (int t = 0; t < MT; ++t)
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            dst[t][v] = t < ntile ? *reinterpret_cast<const uint4*>(xrow[t] + ck * 128 + 8 * v)
+                                  : make_uint4(0, 0, 0, 0);
+      };
+      if (!skip && nck > 0) load_x(xcur, 0);
+      for (int ck = 0; ck < (skip ? 0 : nck); ++ck) {
+        const int kb = ks * kslice + ck * 128;   // first k of this 128-chunk
+        if (kPrefetch && ck + 1 < nck) load_x(xnext, ck + 1);
+        uint4 clo[C::MATS], chi[C::MATS];
+        uint32_t slo[C::MATS], shi[C::MATS];
+#pragma unroll
+        for (int m = 0; m < C::MATS; ++m) {
+          const uint8_t* cb = sbase + m * mat_bytes;
+          const uint8_t* sb = cb + C::ROWS * code_row;
+          const int rl = mt * 16 + g;
+          clo[m] = *reinterpret_cast<const uint4*>(cb + (size_t)rl * code_row + kb / 2 + 16 * c);
+          chi[m] = *reinterpret_cast<const uint4*>(cb + (size_t)(rl + 8) * code_row + kb / 2 + 16 * c);
+          slo[m] = *reinterpret_cast<const uint16_t*>(sb + (size_t)rl * sf_row + kb / 16 + 2 * c);
+          shi[m] = *reinterpret_cast<const uint16_t*>(sb + (size_t)(rl + 8) * sf_row + kb / 16 + 2 * c);
+        }
+        uint32_t sl[C::MATS][2], sh[C::MATS][2];
+#pragma unroll
+        for (int m = 0; m < C::MATS; ++m) {
+          sl[m][0] = sf_to_h2(slo[m] & 0xff); sl[m][1] = sf_to_h2(slo[m] >> 8);
+          sh[m][0] = sf_to_h2(shi[m] & 0xff); sh[m][1] = sf_to_h2(shi[m] >> 8);
+        }
+#pragma unroll
+        for (int s8 = 0; s8 < 8; ++s8) {
+          const int grp = s8 >> 2;
+          uint32_t a[C::MATS][4];
+#pragma unroll
+          for (int m = 0; m < C::MATS; ++m) {
+            // word s8/2 of each row holds steps s8 (bytes 0,1) and s8+1 (bytes 2,3)
+            const uint32_t wl = (&clo[m].x)[s8 >> 1], wh = (&chi[m].x)[s8 >> 1];
+            uint32_t l0, l1, l2, l3, u0_, u1_, u2_, u3_;
+            e2m1_word_to_f16x2(wl, l0, l1, l2, l3);
+            e2m1_word_to_f16x2(wh, u0_, u1_, u2_, u3_);
+            const bool odd = s8 & 1;
+            a[m][0] = hmul2u(odd ? l2 : l0, sl[m][grp]);
+            a[m][1] = hmul2u(odd ? u2_ : u0_, sh[m][grp]);
+            a[m][2] = hmul2u(odd ? l3 : l1, sl[m][grp]);
+            a[m][3] = hmul2u(odd ? u3_ : u1_, sh[m][grp]);
+          }
+#pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            if (t < ntile) {
+              const uint4 xq = xcur[t][s8 >> 1];  // halves 8*(s8/2) .. +7 of this thread's 32
+              const uint32_t b0 = (s8 & 1) ? xq.z : xq.x, b1 = (s8 & 1) ? xq.w : xq.y;
+              mma_f16_16816(ag[t], a[0][0], a[0][1], a[0][2], a[0][3], b0, b1);
+              if (GATED) mma_f16_16816(au[t], a[C::MATS - 1][0], a[C::MATS - 1][1], a[C::MATS - 1][2],
+                                       a[C::MATS - 1][3], b0, b1);
+            }
+          }
+        }
+        if (ck + 1 < nck) {
+          if (kPrefetch) {
+#pragma unroll
+            for (int t = 0; t < MT; ++t)
+#pragma unroll
+              for (int v = 0; v < 4; ++v) xcur[t][v] = xnext[t][v];
+          } else {
+            load_x(xcur, ck + 1);
+          }
+        }
+      }
+      // K-slice partials -> shared memory -> the ks == 0 warp of each m-tile finishes
+      float* myred = red + ((size_t)warp * 16) * C::MTOK * 2;
+#pragma unroll
+      for (int t = 0; t < MT; ++t)
+#pragma unroll
+        for (int z = 0; z < 4; ++z) {
+          const int rr = g + ((z >> 1) << 3), mm = 8 * t + 2 * c + (z & 1);
+          myred[(rr * C::MTOK + mm) * 2] = ag[t][z];
+          myred[(rr * C::MTOK + mm) * 2 + 1] = au[t][z];
+        }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (ks == 0 && !skip) {
+        for (int idx = lane; idx < 16 * C::MTOK; idx += 32) {
+          const int rr = idx / C::MTOK, mm = idx % C::MTOK;
+          const int i = pc + mm;
+          if (i >= n_e) continue;
+          float vg = 0.f, vu = 0.f;
+          for (int kw = 0; kw < WK; ++kw) {
+            const float* o = red + ((size_t)(mt * WK + kw) * 16 + rr) * C::MTOK * 2 + mm * 2;
+            vg += o[0];
+            vu += o[1];
+          }
+          const int rowo = r0 + mt * 16 + rr;
+          if (GATED) {
+            const float hg = __bfloat162float(__float2bfloat16_rn(vg * gsc));
+            const float hu = __bfloat162float(__float2bfloat16_rn(vu * gsc));
+            const float act_v = hg / (1.f + expf(-hg)) * hu;
+            inter_out[(size_t)(off + i) * I + rowo] = __float2half_rn(__bfloat162float(__float2bfloat16_rn(act_v)));
+          } else {
+            y_out[(size_t)pairs[off + i] * NR + rowo] = __float2bfloat16_rn(vg * gsc);
+          }
+        }
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // red is reused by the next pair chunk
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (++stage == NS) { stage = 0; phase ^= 1u; }
+  }
+}
+
+template <bool GATED, int RT, int WK, int MT, int NS>
+static int launch_moe_pipe_t(const __half* xin, const int32_t* counts, const int32_t* offsets, const int32_t* pairs,
+                             const void* w, const void* sf, const float* gs, __half* inter, __nv_bfloat16* y,
+                             int topk, int K, int NR, int I, int E, int* err, cudaStream_t stream) {
+  using C = MoeCfg<GATED, RT, WK, MT, NS>;
+  const int mat_bytes = C::ROWS * (K / 2 + K / 16);
+  const int stage_bytes = (C::MATS * mat_bytes + 127) / 128 * 128;
+  const size_t smem = (size_t)NS * stage_bytes + 8 * 16 * C::MTOK * 2 * 4 + 2 * NS * 8 + (size_t)(E + 2) * 4;
+  if (smem > 232448) return OKC_ERR_INVALID;
+  static size_t configured = 0;
+  if (smem > configured) {
+    if (cudaFuncSetAttribute(moe_pipe_kernel<GATED, RT, WK, MT, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return OKC_ERR_LAUNCH;
+    configured = smem;
+  }
+  const int grid = okc_host::num_sms();
+  moe_pipe_kernel<GATED, RT, WK, MT, NS><<<grid, 288, smem, stream>>>(
+      xin, counts, offsets, pairs, reinterpret_cast<const uint8_t*>(w), reinterpret_cast<const uint8_t*>(sf), gs,
+      inter, y, topk, K, NR, I, E, err);
+  return okc_host::launch_status();
+}
+
+// GATED: unit = 16 rows x (gate + up), warps split K in 8 (K % 1024 == 0).  Down: unit = 32 rows,
+// 2 m-tiles x 4 K slices (K % 512 == 0).  MT from the token count (a chunk of 8*MT pairs per pass).
+template <bool GATED>
+static int launch_moe_pipe(int T, const __half* xin, const int32_t* counts, const int32_t* offsets,
+                           const int32_t* pairs, const void* w, const void* sf, const float* gs, __half* inter,
+                           __nv_bfloat16* y, int topk, int K, int NR, int I, int E, int* err, cudaStream_t stream) {
+  if (GATED) {
+    if (T <= 8) return launch_moe_pipe_t<true, 1, 8, 1, 2>(xin, counts, offsets, pairs, w, sf, gs, inter, y, topk, K, NR, I, E, err, stream);
+    if (T <= 16) return launch_moe_pipe_t<true, 1, 8, 2, 2>(xin, counts, offsets, pairs, w, sf, gs, inter, y, topk, K, NR, I, E, err, stream);
+    return launch_moe_pipe_t<true, 1, 8, 4, 2>(xin, counts, offsets, pairs, w, sf, gs, inter, y, topk, K, NR, I, E, err, stream);
+  }
+  if (T <= 8) return launch_moe_pipe_t<false, 2, 4, 1, 4>(xin, counts, offsets, pairs, w, sf, gs, inter, y, topk, K, NR, I, E, err, stream);
+  if (T <= 16) return launch_moe_pipe_t<false, 2, 4, 2, 4>(xin, counts, offsets, pairs, w, sf, gs, inter, y, topk, K, NR, I, E, err, stream);
+  return launch_moe_pipe_t<false, 2, 4, 4, 4>(xin, counts, offsets, pairs, w, sf, gs, inter, y, topk, K, NR, I, E, err, stream);
 }
 
 __global__ void __launch_bounds__(256) to_f16_kernel(const __nv_bfloat16* __restrict__ x,
@@ -532,15 +836,29 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
   to_f16_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), xh, n);
   int st = okc_host::launch_status();
   if (st) return st;
-  // Few active experts (small T): split K over a cluster so that all SMs stream weights.
-  const int sp1 = T <= 4 ? 4 : (T <= 16 ? 2 : 1);
-  st = launch_expert<true>(T, xh, counts, offsets, pairs, w13, w13_sf, w13_gs, inter, nullptr, topk, H,
-                           I, I, E, sp1, expert_lo, stream);
-  if (st) return st;
-  const int sp2 = T <= 4 ? 2 : 1;
-  st = launch_expert<false>(T, inter, counts, offsets, pairs, w2, w2_sf, w2_gs, nullptr, y, topk, I, H,
-                            I, E, sp2, expert_lo, stream);
-  if (st) return st;
+  int* err = reinterpret_cast<int*>(ws);
+  const int pipe_env = getenv("OKC_MOE_PIPE") ? atoi(getenv("OKC_MOE_PIPE")) : 1;
+  // Measured on B200: the pipelined kernel wins up to 64 tokens, the per-expert kernel above.
+  const bool pipe_ok = pipe_env && T <= 64 && H % 1024 == 0 && I % 512 == 0 && I % 16 == 0 && H % 32 == 0 &&
+                       (size_t)16 * 2 * (H / 2 + H / 16) * 2 < 200000;
+  if (pipe_ok) {
+    st = launch_moe_pipe<true>(T, xh, counts, offsets, pairs, w13, w13_sf, w13_gs, inter, nullptr, topk, H, I, I, E,
+                               err, stream);
+    if (st) return st;
+    st = launch_moe_pipe<false>(T, inter, counts, offsets, pairs, w2, w2_sf, w2_gs, nullptr, y, topk, I, H, I, E,
+                                err, stream);
+    if (st) return st;
+  } else {
+    // Few active experts (small T): split K over a cluster so that all SMs stream weights.
+    const int sp1 = T <= 4 ? 4 : (T <= 16 ? 2 : 1);
+    st = launch_expert<true>(T, xh, counts, offsets, pairs, w13, w13_sf, w13_gs, inter, nullptr, topk, H,
+                             I, I, E, sp1, expert_lo, stream);
+    if (st) return st;
+    const int sp2 = T <= 4 ? 2 : 1;
+    st = launch_expert<false>(T, inter, counts, offsets, pairs, w2, w2_sf, w2_gs, nullptr, y, topk, I, H,
+                              I, E, sp2, expert_lo, stream);
+    if (st) return st;
+  }
   combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, reinterpret_cast<__nv_bfloat16*>(out),
                                                                topk, H, expert_lo, E);
   return okc_host::launch_status();
