@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Decode-layer benchmark (BASELINE.json configs[3]): one decode step of a layer with hidden
+"""Decode-layer benchmark: one decode step of a layer with hidden
 8192, 64 query / 8 KV heads, head_dim 128, batch 128, context lengths U[1024, 8192], page 16.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl okc|reference]
@@ -326,7 +326,7 @@ def run_okc(args):
             "metric": METRIC, "value": round(us, 2), "unit": "us/step", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1000, 4),
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded; BASELINE configs[3] shapes)",
+            "data": "synthetic (seeded; decode-layer workload shapes)",
             "config": dict(WORKLOAD, parallelism=f"tp{world}"),
             "e2e": {"value": round(e2e_us, 2), "unit": "us/step", "h2d_bytes_per_step": B * H * 2 + B * 8,
                     "d2h_bytes_per_step": B * H * 2},

@@ -165,13 +165,15 @@ int okc_attn_decode_fp8_noalloc(const void* q, int ldq, const void* k_cache, con
                                 float sm_scale, int num_ctas, okc_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
- * MoE routing: logits = bf16(x · Wr^T) (fixed fp32 summation order, see DESIGN),
+ * MoE routing: logits = bf16(x · Wr^T) (fp32 sums in a fixed order: lane l of a warp sums
+ * elements 256j + 8l + i over j then i, then an xor butterfly over the 32 lanes, so
+ * the logits are reproducible bit for bit on the CPU),
  * ids = top-k of the logits (ties -> lower expert id), weights = softmax over the
  * chosen logits (renormalize != 0) or the full-softmax probabilities of the chosen
  * experts (renormalize == 0).  x bf16 [T,H], wr bf16 [E,H]; ids int32 [T,k];
  * weights fp32 [T,k]; logits_out fp32 [T,E] (may be NULL).  E <= 256, k <= 16.
  * Replaces `route` muse_prefill_layer/submission.py:179-184 and the routing call of
- * muse_decode_layer/decode/runtime.py:55-63 (softmax top-k per the BASELINE contract).
+ * muse_decode_layer/decode/runtime.py:55-63 (softmax top-k of the bf16 logits).
  * ---------------------------------------------------------------------------------- */
 int okc_moe_route(const void* x, const void* wr, int32_t* ids, float* weights,
                   float* logits_out, int T, int H, int E, int topk, int renormalize,

@@ -274,42 +274,67 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
         epi_bar();
         if (*last_flag) {
           __threadfence();
-          // Fixup, bandwidth-bound: thread et owns rows [4*(et%32), +4) of every 4th token m; each
-          // step has one float4 load per slot in flight for 4 tokens (unrolled), and stores a
-          // coalesced quad of 4 consecutive outputs.
+          // Fixup: thread et owns rows [4*(et%32), +4) of tokens m0 + 4i (i < 8) per chunk.  All
+          // float4 loads of 4 slots x 8 tokens are issued before any is consumed (32 in flight per
+          // thread) so that the tail is not bound by L2 latency; slots are still added in slot
+          // order (deterministic).
           const int r4 = 4 * (et & 31);
           const int n4 = tile * TC_BM + r4;
           const int nslot = c_last - c_first + 1;
           const float* base = p.part + (size_t)(c_first + tile) * BN * TC_BM + r4;
-#pragma unroll 4
-          for (int m = et >> 5; m < mv; m += 4) {
-            float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int q = 0; q < nslot; ++q) {
-              const float4 t4 = __ldcg(reinterpret_cast<const float4*>(base + ((size_t)q * BN + m) * TC_BM));
-              acc4.x += t4.x; acc4.y += t4.y; acc4.z += t4.z; acc4.w += t4.w;
+#pragma unroll 1
+          for (int m0 = et >> 5; m0 < mv; m0 += 32) {
+            float4 acc[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+            for (int q0 = 0; q0 < nslot; q0 += 4) {
+              float4 t4[4][8];
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const int q = q0 + qq, m = m0 + 4 * i;
+                  t4[qq][i] = (q < nslot && m < mv)
+                                  ? __ldcg(reinterpret_cast<const float4*>(base + ((size_t)q * BN + m) * TC_BM))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  acc[i].x += t4[qq][i].x; acc[i].y += t4[qq][i].y;
+                  acc[i].z += t4[qq][i].z; acc[i].w += t4[qq][i].w;
+                }
             }
             if (!ok) continue;
-            float r[4] = {acc4.x, acc4.y, acc4.z, acc4.w};
-            const size_t o = (size_t)m * p.ldy + n4;
-            if (n4 + 3 < p.N && (o & 3) == 0) {
-              if (p.residual) {
-                const uint2 rv = *reinterpret_cast<const uint2*>(p.residual + o);
-                r[0] += bf16_lo(rv.x); r[1] += bf16_hi(rv.x); r[2] += bf16_lo(rv.y); r[3] += bf16_hi(rv.y);
-              }
-              if (p.out_fp32)
-                *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + o) = make_float4(r[0], r[1], r[2], r[3]);
-              else
-                *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.y) + o) =
-                    make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
-            } else {
-              for (int j = 0; j < 4; ++j) {
-                if (n4 + j >= p.N) break;
-                float rv = r[j];
-                if (p.residual) rv += __bfloat162float(p.residual[o + j]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int m = m0 + 4 * i;
+              if (m >= mv) break;
+              float r[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
+              const size_t o = (size_t)m * p.ldy + n4;
+              if (n4 + 3 < p.N && (o & 3) == 0) {
+                if (p.residual) {
+                  const uint2 rv = *reinterpret_cast<const uint2*>(p.residual + o);
+                  r[0] += bf16_lo(rv.x); r[1] += bf16_hi(rv.x); r[2] += bf16_lo(rv.y); r[3] += bf16_hi(rv.y);
+                }
                 if (p.out_fp32)
-                  reinterpret_cast<float*>(p.y)[o + j] = rv;
+                  *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + o) = make_float4(r[0], r[1], r[2], r[3]);
                 else
-                  reinterpret_cast<__nv_bfloat16*>(p.y)[o + j] = __float2bfloat16_rn(rv);
+                  *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.y) + o) =
+                      make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+              } else {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  if (n4 + j >= p.N) break;
+                  float rv = r[j];
+                  if (p.residual) rv += __bfloat162float(p.residual[o + j]);
+                  if (p.out_fp32)
+                    reinterpret_cast<float*>(p.y)[o + j] = rv;
+                  else
+                    reinterpret_cast<__nv_bfloat16*>(p.y)[o + j] = __float2bfloat16_rn(rv);
+                }
               }
             }
           }
@@ -385,7 +410,17 @@ static TcPlan tc_plan(int M, int N, int K) {
   pl.tiles = (N + TC_BM - 1) / TC_BM;
   pl.nkb = (K + TC_BK * pl.ks - 1) / (TC_BK * pl.ks);
   const long long units = (long long)pl.tiles * pl.nkb;
-  const long long slots = (long long)okc_host::num_sms() * pl.per_sm;
+  long long slots = (long long)okc_host::num_sms() * pl.per_sm;
+  static int cap = -1;  // OKC_TC_MAX_CTAS: grid cap for tuning sweeps (0 = none)
+  if (cap < 0) {
+    const char* e = getenv("OKC_TC_MAX_CTAS");
+    cap = e ? atoi(e) : 0;
+  }
+  if (cap > 0 && slots > cap) slots = cap;
+  // Few tiles (small N): split each tile over at most 4 CTAs.  The last arriver of a tile sums
+  // one fp32 slot per contributor, so wider splits make that serial fixup the critical path
+  // (N = 1280, K = 8192 on B200: 148 CTAs 35-41 us, 40 CTAs 23 us).
+  if (slots > 4LL * pl.tiles) slots = 4LL * pl.tiles;
   pl.ctas = (int)(units < slots ? units : slots);
   return pl;
 }

@@ -3,7 +3,7 @@
 (muse_moe_w4a16/submission.py:22-49, 352-398): `prepare(weights)` keeps the bank as stored
 (no repack), `kernel_fn(data, state)` takes hidden_states [M, H] bf16, topk_ids [M, k] int32
 (global ids) and topk_weights [M, k] fp32 and returns bf16 [M, H]: the routing-weighted sum of
-the local experts' SwiGLU MLP outputs.  BASELINE's MoE has no post-expert RMSNorm, so the Muse
+the local experts' SwiGLU MLP outputs.  The plain W4A16 MoE contract has no post-expert RMSNorm, so the Muse
 `post_norm_w` is not applied (it is the reference's `_finalize` extra, submission.py:295-308)."""
 
 from __future__ import annotations

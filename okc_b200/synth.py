@@ -1,5 +1,5 @@
-"""Seeded synthetic workloads with the shapes and value distributions of BASELINE.json's
-configs (there is no public dataset on this path; every input is synthetic).
+"""Seeded synthetic workloads with the shapes and value distributions of the decode-path
+workloads (there is no public dataset on this path; every input is synthetic).
 
 All generators take a torch device and a seed and use a generator on that device, so the
 large paged caches are produced directly in HBM.  The same seed gives the same tensors
@@ -53,7 +53,7 @@ def paged_layout(seq_lens: list[int], page: int, pool_pages: int, g: torch.Gener
 
 def attention_case(B=64, Hq=64, Hkv=8, D=128, ctx=(512, 32768), page=16, pool_pages=1 << 17,
                    seed=0, device="cuda", scale_range=(0.5, 2.0), extra_tokens=0, fill=True):
-    """q bf16 ~N(0,1) [B, Hq, D]; ctx ~U[lo, hi]; e4m3 caches
+    """Attention-decode workload: q bf16 ~N(0,1) [B, Hq, D]; ctx ~U[lo, hi]; e4m3 caches
     [pool, P, Hkv, D] of N(0,1)/scale_h codes; per-head scales ~U[0.5, 2]; sm_scale 1/sqrt(D)."""
     g = _gen(device, seed)
     lo, hi = ctx
@@ -77,7 +77,7 @@ def attention_case(B=64, Hq=64, Hkv=8, D=128, ctx=(512, 32768), page=16, pool_pa
 
 
 def projection_case(M, K, N, seed=0, device="cuda"):
-    """x [M,K] ~N(0,1), W [N,K] ~N(0, 0.02), bf16."""
+    """Projection workload: x [M,K] ~N(0,1), W [N,K] ~N(0, 0.02), bf16."""
     g = _gen(device, seed)
     x = torch.randn((M, K), generator=g, device=device).to(torch.bfloat16)
     w = (torch.randn((N, K), generator=g, device=device) * 0.02).to(torch.bfloat16)
@@ -86,7 +86,7 @@ def projection_case(M, K, N, seed=0, device="cuda"):
 
 def moe_case(T, E=64, H=4096, I=1536, topk=8, seed=0, device="cuda", gs13=(0.006, 0.010),
              gs2=(0.02, 0.03)):
-    """router Wr [E,H] ~N(0,0.02) bf16; uniformly random E2M1 codes
+    """W4A16 MoE workload: router Wr [E,H] ~N(0,0.02) bf16; uniformly random E2M1 codes
     (random bytes) for W13 [E, 2I, H/2] and W2 [E, H, I/2]; e4m3 block scales ~U[0.25, 1]
     per 16-element K-group; one fp32 global scale per expert (its value is not given by the
     config: W13 ~U[0.006, 0.010], W2 ~U[0.02, 0.03], which keep h, inter and y O(1) at
@@ -107,7 +107,7 @@ def moe_case(T, E=64, H=4096, I=1536, topk=8, seed=0, device="cuda", gs13=(0.006
 
 def layer_case(B=128, H=8192, Hq=64, Hkv=8, D=128, ctx=(1024, 8192), page=16, pool_pages=1 << 17,
                theta=5e5, eps=1e-6, seed=0, device="cuda", fill=True):
-    """one decode step of a layer: x [B, H] ~N(0,1) bf16; RMSNorm weight
+    """Decode-layer workload: one decode step of a layer: x [B, H] ~N(0,1) bf16; RMSNorm weight
     (plain, ~1 + N(0, 0.02)); Wqkv [(Hq + 2Hkv) D, H] and Wo [H, Hq D] ~N(0, 0.02) bf16; paged
     FP8 cache holding ctx ~U[1024, 8192] tokens per sequence (+1 page of room for the append)."""
     att = attention_case(B, Hq, Hkv, D, ctx, page, pool_pages, seed, device, extra_tokens=1, fill=fill)

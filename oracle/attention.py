@@ -2,7 +2,7 @@
 
 Follows muse_prefill_layer/submission.py:89-176 (`rms`, `rope`, `round_queries`,
 `attention`) and muse_attention_decode/tools/bench_tail.py:79-108 (`_ref`), generalised
-to BASELINE's shapes: per-KV-head scales k_scale[h] / v_scale[h], any head_dim, page size
+to the decode-path shapes: per-KV-head scales k_scale[h] / v_scale[h], any head_dim, page size
 and GQA ratio.  The Muse-only pieces (per-head QK RMSNorm, query scale factor, RMSNorm x
 sigmoid output gate) are kept behind `muse=True` so the reference's own shapes stay
 checkable against its code.

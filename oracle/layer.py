@@ -1,9 +1,9 @@
-"""Decode-layer oracle for BASELINE configs[0] / configs[3] (test infrastructure only).
+"""Decode-layer oracle for the small and the full decode-layer workloads (test infrastructure only).
 
 RMSNorm -> QKV projection -> RoPE -> FP8 KV-append -> paged attention -> O projection ->
 residual add, with the bf16 boundaries of the reference layer
 (muse_prefill_layer/submission.py:137-176, 201-207; muse_decode_layer/decode/runtime.py:47-50),
-without Muse's QK-norm, output gate and gated residual (BASELINE asks for plain RMSNorm,
+without Muse's QK-norm, output gate and gated residual (the plain layer is RMSNorm,
 eps 1e-6, and x + O).
 """
 

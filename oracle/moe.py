@@ -7,7 +7,7 @@
 * Experts: h = bf16(x @ W13^T), inter = bf16(silu(h_gate) * h_up), y = bf16(inter @ W2^T)
   with bf16 boundaries as muse_moe_w4a16/submission.py:236-242 and
   muse_prefill_layer/submission.py:187-198 (bf16 weights, fp32 accumulate).
-* Routing (BASELINE contract: softmax top-k of bf16 router logits): logits summed in the
+* Routing (the contract: softmax top-k of bf16 router logits): logits summed in the
   fixed order the CUDA kernel uses (so ids are reproduced exactly), ties -> lower id.
 * Permutation: per local expert the pair ids t*topk + slot in ascending order, counts and
   (expert << 16 | first) tiles of `bm` pairs (muse_moe_w4a16/submission.py:274-291).

@@ -1,6 +1,6 @@
 """Generates the golden fixtures of tests/golden/ by running the reference's OWN code here.
 
-Needs the reference checkout (default /root/reference, or $OKC_REFERENCE) and runs on CPU:
+Needs a checkout of the reference, named by $OKC_REFERENCE, and runs on CPU:
 
   nvfp4_decode.json  the NVFP4 nibble decoder `_decode_nvfp4` of
                      muse_decode_layer/decode/nvfp4_gemv.py:9-18, executed with scalar fp32/bf16
@@ -28,7 +28,7 @@ import types
 from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("OKC_REFERENCE", "/root/reference"))
+REF = Path(os.environ.get("OKC_REFERENCE", "reference-checkout-not-set"))
 
 
 # ------------------------------------------------------------------------ NVFP4 decode

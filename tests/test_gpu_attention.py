@@ -1,6 +1,6 @@
 """GPU parity of paged FP8 attention decode and the RoPE + FP8 KV-append against the oracle.
 
-Attention tolerance: bf16 output within rtol 2e-2 / atol 2e-2 and a
+Attention tolerance: bf16 output within rtol 2e-2 / atol 2e-2 (the path's stated tolerance) and a
 relative-L2 error below 1e-2.  KV-append: slot indices and every untouched cache byte
 bit-exact; written e4m3 bytes may differ by one e4m3 step where the rotated value sits on a
 rounding boundary (sin/cos differ in the last fp32 bit between CPU and GPU).
@@ -97,7 +97,7 @@ def test_peaked_scores_and_graph_replay(ops):
 
 
 def test_baseline_c3_subset(ops):
-    """BASELINE configs[2] at full size (B64, 64q/8kv, D128, ctx U[512, 32768], P16, pool 2^17);
+    """The attention-decode workload at full size (B64, 64q/8kv, D128, ctx U[512, 32768], P16, pool 2^17);
     the oracle checks a subset of the sequences (CPU time), the rest through a property:
     every output row is a convex combination of V rows, so |out| <= max|V| * v_scale."""
     from okc_b200 import synth

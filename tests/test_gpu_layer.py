@@ -1,5 +1,5 @@
 """GPU parity of one decode step of the layer (okc_b200.layer.DecodeLayer) against the CPU
-oracle (oracle.layer.decode_layer): BASELINE configs[0] exactly, a mid-size case, and a
+oracle (oracle.layer.decode_layer): the small decode-layer config exactly, a mid-size case, and a
 CUDA-graph replay of the step.  Tolerance: rtol 2e-2 / atol 2e-2 on the bf16 output, cache
 append slots bit-exact."""
 
@@ -22,7 +22,7 @@ def _run(B, H, Hq, Hkv, D, lens, page, pool, theta, seed):
     vc = torch.empty_like(kc)
     ks = (torch.rand(Hkv, generator=g, device="cuda") * 1.5 + 0.5).float()
     vs = (torch.rand(Hkv, generator=g, device="cuda") * 1.5 + 0.5).float()
-    synth.fill_e4m3_normal(kc, g, ks)   # e4m3(N(0,1) / scale_h)
+    synth.fill_e4m3_normal(kc, g, ks)   # e4m3(N(0,1) / scale_h), as the small config
     synth.fill_e4m3_normal(vc, g, vs)
     x = torch.randn((B, H), generator=g, device="cuda").to(torch.bfloat16)
     nw = (1 + 0.02 * torch.randn(H, generator=g, device="cuda")).to(torch.bfloat16)
@@ -47,7 +47,7 @@ def _check(out, exp, what):
 
 
 def test_baseline_config0_smoke():
-    """batch 2, hidden 1024, 8q/2kv, D128, theta 1e4, eps 1e-6, P16, 64 pages,
+    """Small decode-layer config: batch 2, hidden 1024, 8q/2kv, D128, theta 1e4, eps 1e-6, P16, 64 pages,
     ctx {37, 200}, weights ~N(0, 0.02), x ~N(0, 1)."""
     layer, ins, out, exp, slots, caches = _run(2, 1024, 8, 2, 128, [37, 200], 16, 64, 1e4, 0)
     _check(out, exp, "configs[0]")

@@ -1,5 +1,5 @@
 """GPU parity of the W4A16 MoE path: routing ids and permutation bit-exact, expert outputs
-within rtol 2e-2 / atol 2e-2 and relative-L2 below 1e-2.
+within rtol 2e-2 / atol 2e-2 (the path's stated tolerance) and relative-L2 below 1e-2.
 
 The oracle dequantises weights as bf16(e2m1 * f32(sf * gs)) (the reference's nibble decoder);
 the kernel multiplies the exact e2m1 * sf product by gs on the fp32 accumulator — the two

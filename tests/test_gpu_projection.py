@@ -1,6 +1,6 @@
 """GPU parity of the projection kernels (C ABI okc_gemm_bf16) against the CPU oracle.
 
-Tolerance: bf16 outputs within rtol 2e-2 / atol 2e-2 of the fp32-
+Tolerance (the path's stated tolerance): bf16 outputs within rtol 2e-2 / atol 2e-2 of the fp32-
 accumulated reference, plus a relative-L2 bound of 5e-3 (one bf16 rounding of the output
 is ~2e-3 relative).
 """
