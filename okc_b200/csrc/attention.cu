@@ -105,6 +105,21 @@ __device__ __forceinline__ void transpose4x4(uint32_t w0, uint32_t w1, uint32_t 
   o3 = prmt(t2, t3, 0x7632);
 }
 
+// RL bytes (8, 16 or 32) of one token row from shared memory as 32-bit words, 8/16-byte loads.
+template <int RL>
+__device__ __forceinline__ void ld_run(const uint8_t* p, uint32_t (&w)[RL / 4]) {
+  if constexpr (RL == 8) {
+    const uint2 x = *reinterpret_cast<const uint2*>(p);
+    w[0] = x.x; w[1] = x.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < RL / 16; ++i) {
+      const uint4 x = *reinterpret_cast<const uint4*>(p + 16 * i);
+      w[4 * i] = x.x; w[4 * i + 1] = x.y; w[4 * i + 2] = x.z; w[4 * i + 3] = x.w;
+    }
+  }
+}
+
 template <int D, int HKV>
 __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kernel(AttnArgs a) {
   using C = AttnCfg<D, HKV>;
@@ -340,6 +355,13 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
 #pragma unroll
         for (int j = 0; j < 4; ++j)
           mma_e4m3_16832(S[j], q1lo[s2], q2lo[s2], q1hi[s2], q2hi[s2], kr0[j][s2], kr1[j][s2]);
+      constexpr int VW = C::RL / 4;  // 32-bit words per V run
+      uint32_t vlw[4][VW], vhw[4][VW];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        ld_run<C::RL>(sv + (size_t)(4 * c + u) * C::ROW + C::RL * g, vlw[u]);
+        ld_run<C::RL>(sv + (size_t)(16 + 4 * c + u) * C::ROW + C::RL * g, vhw[u]);
+      }
       // ---- online softmax (log2 domain), rows g (q1 part) + g+8 (q2 part) ----
       float sc[4][2];
       float mx = -INFINITY;
@@ -401,18 +423,11 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
           if (16 + 4 * c + u < valid) mhi |= 0xffu << (8 * u);
         }
       }
-      constexpr int VW = C::RL / 4;  // 32-bit words per V run
 #pragma unroll
       for (int k = 0; k < VW; ++k) {  // one 4-byte column group (4 d-blocks) at a time
-        uint32_t vl[4], vh[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          vl[u] = *reinterpret_cast<const uint32_t*>(sv + (size_t)(4 * c + u) * C::ROW + C::RL * g + 4 * k);
-          vh[u] = *reinterpret_cast<const uint32_t*>(sv + (size_t)(16 + 4 * c + u) * C::ROW + C::RL * g + 4 * k);
-        }
         uint32_t b0[4], b1[4];
-        transpose4x4(vl[0], vl[1], vl[2], vl[3], b0[0], b0[1], b0[2], b0[3]);
-        transpose4x4(vh[0], vh[1], vh[2], vh[3], b1[0], b1[1], b1[2], b1[3]);
+        transpose4x4(vlw[0][k], vlw[1][k], vlw[2][k], vlw[3][k], b0[0], b0[1], b0[2], b0[3]);
+        transpose4x4(vhw[0][k], vhw[1][k], vhw[2][k], vhw[3][k], b1[0], b1[1], b1[2], b1[3]);
         if (tail) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) { b0[i] &= mlo; b1[i] &= mhi; }
