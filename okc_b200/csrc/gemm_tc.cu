@@ -14,9 +14,12 @@
 //  * persistent stream-K grid (one CTA per SM): the (tile, K-block) units are split evenly
 //    over the CTAs, so every SM streams the same number of bytes whatever N and K are;
 //  * 4 epilogue warps drain the double-buffered TMEM accumulator with tcgen05.ld (warp w owns
-//    TMEM lanes 32(w%4)..+31 = weight rows) while the next segment's MMAs run; a tile split
-//    between CTAs is finished by its last arriving CTA, which sums the fp32 partial slots in
-//    slot order (deterministic; self-resetting per-tile counter).
+//    TMEM lanes 32(w%4)..+31 = weight rows) while the next segment's MMAs run.  A tile that
+//    one CTA covers whole is written directly; a split tile leaves one fp32 partial slot per
+//    contributing CTA, and tc_reduce_kernel (all SMs, launched as a programmatic dependent of
+//    the GEMM) sums each tile's slots in slot order (deterministic).  A last-arriver fixup
+//    inside the GEMM put up to 4 x 64 KB of L2 reads on one SM at the end of the stream
+//    (11-13 us on B200 with the HBM still saturated); spread over every SM it takes ~2 us.
 // Every mbarrier wait is bounded (common.cuh); TMEM is always released before exit.
 // Mirrors the M >= 32 tensor-core path of muse_bf16_proj/projection/kernels/{tma,
 // hopper_ws}.py and muse_decode_layer/decode/projections.py:75-77 (there: cuBLAS / wgmma).
@@ -36,7 +39,6 @@ struct TcParams {
   const __nv_bfloat16* residual;
   int* err;
   float* part;    // stream-K partial slots [ctas + tiles][BN][128] (workspace)
-  int* counters;  // per-tile arrival counters, zero between calls (the last arriver resets)
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -113,8 +115,7 @@ __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: 
 // grid; a CTA's consecutive units form at most a few segments, one per weight tile it touches.
 // Warp 0: TMA producer.  Warp 1: MMA issuer (double-buffered TMEM accumulator).  Warps 2..5:
 // epilogue (TMEM lane quarter = warp % 4).  A segment that covers its whole tile stores y
-// directly; otherwise it stores an fp32 partial (m-major, coalesced) into slot (CTA + tile) and
-// the last segment of the tile to arrive sums the tile's slots in slot order (deterministic).
+// directly; otherwise it stores an fp32 partial (m-major, coalesced) into slot (CTA + tile).
 template <int BN, int STAGES, int KS>
 __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_w,
                                                          const __grid_constant__ CUtensorMap tma_x,
@@ -128,9 +129,10 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
   uint64_t* acce = accf + 2;        // [2] accumulator buffer drained by the epilogue
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  volatile int* last_flag = abort_flag + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the dependent reduce kernel may launch now: it waits for this grid before reading
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int nkb = (p.K + TC_BK * KS - 1) / (TC_BK * KS);  // stages (units) per tile
   const int U = p.tiles * nkb;
   int u0, u1;
@@ -222,8 +224,6 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
     const int q4 = warp & 3;
     const int row = q4 * 32 + lane;  // TMEM lane = weight row within the tile
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    const int et = threadIdx.x - 64;  // 0..127 inside the epilogue group
-    const int mv = min(p.M, BN);
     int seg = 0;
     for (int u = u0; u < u1; ++seg) {
       const int tile = u / nkb, kb_first = u - tile * nkb;
@@ -265,83 +265,6 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[buf]);  // the MMA warp may reuse this buffer now
-      if (!whole) {
-        const int c_first = sk_owner(U, gridDim.x, tile * nkb);
-        const int c_last = sk_owner(U, gridDim.x, (tile + 1) * nkb - 1);
-        __threadfence();
-        epi_bar();
-        if (et == 0) *last_flag = atomicAdd(&p.counters[tile], 1) == c_last - c_first;
-        epi_bar();
-        if (*last_flag) {
-          __threadfence();
-          // Fixup: thread et owns rows [4*(et%32), +4) of tokens m0 + 4i (i < 8) per chunk.  All
-          // float4 loads of 4 slots x 8 tokens are issued before any is consumed (32 in flight per
-          // thread) so that the tail is not bound by L2 latency; slots are still added in slot
-          // order (deterministic).
-          const int r4 = 4 * (et & 31);
-          const int n4 = tile * TC_BM + r4;
-          const int nslot = c_last - c_first + 1;
-          const float* base = p.part + (size_t)(c_first + tile) * BN * TC_BM + r4;
-#pragma unroll 1
-          for (int m0 = et >> 5; m0 < mv; m0 += 32) {
-            float4 acc[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 1
-            for (int q0 = 0; q0 < nslot; q0 += 4) {
-              float4 t4[4][8];
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  const int q = q0 + qq, m = m0 + 4 * i;
-                  t4[qq][i] = (q < nslot && m < mv)
-                                  ? __ldcg(reinterpret_cast<const float4*>(base + ((size_t)q * BN + m) * TC_BM))
-                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq)
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  acc[i].x += t4[qq][i].x; acc[i].y += t4[qq][i].y;
-                  acc[i].z += t4[qq][i].z; acc[i].w += t4[qq][i].w;
-                }
-            }
-            if (!ok) continue;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int m = m0 + 4 * i;
-              if (m >= mv) break;
-              float r[4] = {acc[i].x, acc[i].y, acc[i].z, acc[i].w};
-              const size_t o = (size_t)m * p.ldy + n4;
-              if (n4 + 3 < p.N && (o & 3) == 0) {
-                if (p.residual) {
-                  const uint2 rv = *reinterpret_cast<const uint2*>(p.residual + o);
-                  r[0] += bf16_lo(rv.x); r[1] += bf16_hi(rv.x); r[2] += bf16_lo(rv.y); r[3] += bf16_hi(rv.y);
-                }
-                if (p.out_fp32)
-                  *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + o) = make_float4(r[0], r[1], r[2], r[3]);
-                else
-                  *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.y) + o) =
-                      make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
-              } else {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  if (n4 + j >= p.N) break;
-                  float rv = r[j];
-                  if (p.residual) rv += __bfloat162float(p.residual[o + j]);
-                  if (p.out_fp32)
-                    reinterpret_cast<float*>(p.y)[o + j] = rv;
-                  else
-                    reinterpret_cast<__nv_bfloat16*>(p.y)[o + j] = __float2bfloat16_rn(rv);
-                }
-              }
-            }
-          }
-          if (et == 0) p.counters[tile] = 0;
-        }
-        epi_bar();  // last_flag is reused by the next segment
-      }
       u = seg_end;
     }
   }
@@ -351,6 +274,59 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
   if (warp == 0) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
+  }
+}
+
+// Split-tile reduction: y[m, tile*128 + r] = sum over the tile's slots (in slot order) of the
+// partials (+ residual).  Block (x, tile) covers tokens [8x, 8x + 8) x 128 rows; thread t owns 4
+// consecutive rows of one token (float4 loads, all slots' loads issued before the sum).
+template <int BN>
+__global__ void __launch_bounds__(256) tc_reduce_kernel(TcParams p, int U, int C, int nkb) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // the GEMM grid is complete and visible
+  const int tile = blockIdx.y;
+  const int c_first = sk_owner(U, C, tile * nkb), c_last = sk_owner(U, C, (tile + 1) * nkb - 1);
+  if (c_first == c_last) return;  // one CTA covered the tile: written directly
+  const int m = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (m >= p.M) return;
+  const int r4 = 4 * (threadIdx.x & 31);
+  const int n4 = tile * TC_BM + r4;
+  const int nslot = c_last - c_first + 1;
+  const float* base = p.part + (size_t)(c_first + tile) * BN * TC_BM + (size_t)m * TC_BM + r4;
+  const size_t slot_stride = (size_t)BN * TC_BM;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+  for (int q0 = 0; q0 < nslot; q0 += 8) {
+    float4 t4[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      t4[i] = q0 + i < nslot ? __ldcg(reinterpret_cast<const float4*>(base + (q0 + i) * slot_stride))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { acc.x += t4[i].x; acc.y += t4[i].y; acc.z += t4[i].z; acc.w += t4[i].w; }
+  }
+  float r[4] = {acc.x, acc.y, acc.z, acc.w};
+  const size_t o = (size_t)m * p.ldy + n4;
+  if (n4 + 3 < p.N && (o & 3) == 0) {
+    if (p.residual) {
+      const uint2 rv = *reinterpret_cast<const uint2*>(p.residual + o);
+      r[0] += bf16_lo(rv.x); r[1] += bf16_hi(rv.x); r[2] += bf16_lo(rv.y); r[3] += bf16_hi(rv.y);
+    }
+    if (p.out_fp32)
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.y) + o) = make_float4(r[0], r[1], r[2], r[3]);
+    else
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.y) + o) =
+          make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (n4 + j >= p.N) break;
+      float rv = r[j];
+      if (p.residual) rv += __bfloat162float(p.residual[o + j]);
+      if (p.out_fp32)
+        reinterpret_cast<float*>(p.y)[o + j] = rv;
+      else
+        reinterpret_cast<__nv_bfloat16*>(p.y)[o + j] = __float2bfloat16_rn(rv);
+    }
   }
 }
 
@@ -425,9 +401,8 @@ static TcPlan tc_plan(int M, int N, int K) {
   return pl;
 }
 
-// Workspace: [kTcCounterBytes of per-tile counters at a FIXED offset, so that they stay zero
-// from call to call whatever the shape][fp32 partial slots: (ctas + tiles) x BN x 128].
-constexpr size_t kTcCounterBytes = 16384;  // 4096 tiles of 128 rows: N <= 524288
+// Workspace: [kTcCounterBytes reserved][fp32 partial slots: (ctas + tiles) x BN x 128].
+constexpr size_t kTcCounterBytes = 16384;  // reserved (N <= 524288: 4096 tiles of 128 rows)
 
 size_t tc_gemm_ws_bytes(int M, int N, int K) {
   if (M < 1 || M > 256 || N < 1 || K < 1) return 0;
@@ -450,11 +425,27 @@ static int launch_tc_t(const void* x, int ldx, const void* w, int ldw, TcParams&
   }
   const size_t part_bytes = (size_t)(pl.ctas + pl.tiles) * BN * TC_BM * 4;
   if (!ws || ws_bytes < kTcCounterBytes + part_bytes || (size_t)pl.tiles * 4 > kTcCounterBytes)
-    return OKC_ERR_WORKSPACE;
+    return OKC_ERR_WORKSPACE;  // (the tile-count bound keeps the documented N limit)
   p.tiles = pl.tiles;
-  p.counters = reinterpret_cast<int*>(ws);
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kTcCounterBytes);
   tc_gemm_kernel<BN, STAGES, KS><<<pl.ctas, 192, C::SMEM, stream>>>(mw, mx, p);
+  int st = okc_host::launch_status();
+  if (st) return st;
+  // Reduce of the split tiles, as a programmatic dependent launch: its blocks may be scheduled
+  // while the GEMM drains and wait in griddepcontrol.wait until the GEMM grid has completed.
+  if ((long long)pl.tiles * pl.nkb <= pl.ctas && pl.nkb == 1) return OKC_OK;  // no split tile
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((min(p.M, BN) + 7) / 8), (unsigned)pl.tiles, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int U = pl.tiles * pl.nkb;
+  if (cudaLaunchKernelEx(&cfg, tc_reduce_kernel<BN>, p, U, pl.ctas, pl.nkb) != cudaSuccess) return OKC_ERR_LAUNCH;
   return okc_host::launch_status();
 }
 

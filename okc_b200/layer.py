@@ -69,7 +69,8 @@ class DecodeLayer:
     def kernels_per_step(self, tokens: int) -> int:
         """Our kernel launches in one step (for the bench's gpu_launches)."""
         passes = 1 if tokens <= 256 else (tokens + 255) // 256  # tcgen05 GEMM: 256 tokens a launch
-        return 1 + passes + 1 + 2 + passes
+        per_gemm = 2 * passes if tokens > 32 else 1  # tcgen05 stream-K + split-tile reduce
+        return 1 + per_gemm + 1 + 2 + per_gemm
 
     def step(self, x, positions, page_table, k_cache, v_cache, lens=None, out=None):
         """x bf16 [B, H]; positions int64 [B] (= tokens already cached); caches of this rank's
