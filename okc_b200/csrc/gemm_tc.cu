@@ -393,10 +393,15 @@ static TcPlan tc_plan(int M, int N, int K) {
     cap = e ? atoi(e) : 0;
   }
   if (cap > 0 && slots > cap) slots = cap;
-  // Few tiles (small N): split each tile over at most 4 CTAs.  The last arriver of a tile sums
-  // one fp32 slot per contributor, so wider splits make that serial fixup the critical path
-  // (N = 1280, K = 8192 on B200: 148 CTAs 35-41 us, 40 CTAs 23 us).
-  if (slots > 4LL * pl.tiles) slots = 4LL * pl.tiles;
+  // Few tiles (small N): split each tile over at most 8 CTAs; wider splits cost more partial
+  // traffic and reduce work than they gain (N = 1280, K = 8192, M = 128 on B200: 2 CTAs per
+  // tile 24.2 us, 4: 15.2, 8: 11.4, 16: 12.5, no cap: 12.7).
+  static int split = -1;  // OKC_TC_SPLIT: CTAs per tile cap for tuning sweeps (default 8)
+  if (split < 0) {
+    const char* e = getenv("OKC_TC_SPLIT");
+    split = e ? atoi(e) : 8;
+  }
+  if (split > 0 && slots > (long long)split * pl.tiles) slots = (long long)split * pl.tiles;
   pl.ctas = (int)(units < slots ? units : slots);
   return pl;
 }
