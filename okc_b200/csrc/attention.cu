@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
   int* prefix = const_cast<int*>(abort_flag) + 4;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::NS; ++s) {
       mbar_init(&full[s], 1);
@@ -139,6 +140,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
     *abort_flag = 0;
     fence_mbar_init();
   }
+  pdl_wait();
   unit_prefix(a.seq_lens, a.B, C::TS, prefix);
   __syncthreads();
 
@@ -450,6 +452,8 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
 // fixed order, so the result does not depend on which CTA finished first.
 __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int NSUB, int D) {
   extern __shared__ int mprefix[];
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x;
   unit_prefix(a.seq_lens, a.B, TS, mprefix);
   __syncthreads();
@@ -524,6 +528,8 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
     const float* __restrict__ v_scale, __nv_bfloat16* __restrict__ q_out,
     uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache, int64_t* __restrict__ slots_out,
     int Hq, int Hkv, int D, int P, long long num_pages, float q_scale, int qk_norm, float norm_eps, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.x;
   const long long pos = positions[b];
   const long long lp = pos / P;
@@ -617,11 +623,10 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
       return OKC_ERR_LAUNCH;
     configured = smem;
   }
-  attn_decode_kernel<D, HKV><<<a.num_ctas, C::THREADS, smem, stream>>>(a);
-  int st = okc_host::launch_status();
+  int st = okc_host::launch_k(attn_decode_kernel<D, HKV>, dim3(a.num_ctas), dim3(C::THREADS), smem, stream, dim3(1), a);
   if (st) return st;
-  attn_merge_kernel<<<dim3(a.B, (a.Hq + 7) / 8), 256, (size_t)(a.B + 1) * sizeof(int), stream>>>(a, C::TS, C::NSUB, D);
-  return okc_host::launch_status();
+  return okc_host::launch_k(attn_merge_kernel, dim3(a.B, (a.Hq + 7) / 8), dim3(256), (size_t)(a.B + 1) * sizeof(int),
+                            stream, dim3(1), a, (int)C::TS, (int)C::NSUB, D);
 }
 
 int launch_attn_decode(AttnArgs& a, int D, int Hkv, cudaStream_t stream) {
@@ -650,12 +655,11 @@ int launch_rope_append(const void* qkv, int ldqkv, const int64_t* positions,
                        int Hq, int Hkv, int D, int P, long long num_pages, float q_scale, int qk_norm,
                        float norm_eps, int* err, cudaStream_t stream) {
   const int chunks = ((Hq + 2 * Hkv) * D / 8 + 255) / 256;
-  rope_append_kernel<<<dim3(B, chunks), 256, 0, stream>>>(
+  return okc_host::launch_k(rope_append_kernel, dim3(B, chunks), dim3(256), 0, stream, dim3(1),
       reinterpret_cast<const __nv_bfloat16*>(qkv), ldqkv, positions, page_table, table_ld, max_pages,
       inv_freq, k_scale, v_scale, reinterpret_cast<__nv_bfloat16*>(q_out),
       reinterpret_cast<uint8_t*>(k_cache), reinterpret_cast<uint8_t*>(v_cache), slots_out, Hq, Hkv,
       D, P, num_pages, q_scale, qk_norm, norm_eps, err);
-  return okc_host::launch_status();
 }
 
 }  // namespace okc

@@ -14,6 +14,8 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <stdint.h>
+#include <stdlib.h>
+#include <utility>
 
 #include "../../include/okc_b200.h"
 
@@ -174,6 +176,15 @@ __device__ __forceinline__ float warp_max(float v) {
 }  // namespace okc
 
 // Host-side helpers shared by the entry points.
+// Programmatic dependent launch (PDL).  Every kernel lets its successor in the stream launch
+// early (pdl_trigger at entry: the successor's blocks may then be scheduled as soon as all of
+// this grid's blocks have started) and waits for its predecessor grid to complete, with its
+// memory visible, before it touches global memory (pdl_wait).  pdl_wait returns at once when
+// the kernel was launched without the attribute.  This hides the launch latency and the
+// prologue (barrier init, TMEM allocation) of each kernel behind the tail of the previous one.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 namespace okc_host {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -187,5 +198,48 @@ inline int launch_status() {
 }
 
 int num_sms();  // cached per device (defined in capi.cu)
+
+// PDL on by default; OKC_PDL=0 launches every kernel with plain stream order.
+inline bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("OKC_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// Launches `kernel` with the programmatic-stream-serialization attribute (plus an optional
+// cluster shape); returns an OKC status.
+template <typename... KArgs, typename... Args>
+inline int launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                    dim3 cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster.x;
+    attr[n].val.clusterDim.y = cluster.y;
+    attr[n].val.clusterDim.z = cluster.z;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  if (cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) != cudaSuccess) {
+    cudaGetLastError();
+    return OKC_ERR_LAUNCH;
+  }
+  return launch_status();
+}
 
 }  // namespace okc_host

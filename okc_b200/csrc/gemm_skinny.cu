@@ -45,6 +45,8 @@ __global__ void __launch_bounds__(kSkinnyWarps * 32, 2)
   constexpr int MTOK = MT * 8;
   constexpr int RED_LD = MTOK + 1;  // padded row of the partial tile (floats)
   extern __shared__ float red[];    // [kSkinnyRows][RED_LD] when splits > 1
+  pdl_trigger();
+  pdl_wait();
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = lane >> 2, c = lane & 3;
@@ -180,23 +182,10 @@ static int launch_skinny_mt(const void* x, int ldx, const void* w, int ldw, void
   const int cps = (nchunks + splits - 1) / splits;
   const size_t smem = splits > 1 ? (size_t)kSkinnyRows * (MT * 8 + 1) * sizeof(float) : 0;
 
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(row_blocks * splits, 1, 1);
-  cfg.blockDim = dim3(kSkinnyWarps * 32, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = splits;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, skinny_gemm_kernel<MT>, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                     reinterpret_cast<const __nv_bfloat16*>(w), ldw, y, ldy,
-                     reinterpret_cast<const __nv_bfloat16*>(residual), M, N, K, splits, cps,
-                     out_fp32);
-  return okc_host::launch_status();
+  return okc_host::launch_k(skinny_gemm_kernel<MT>, dim3(row_blocks * splits), dim3(kSkinnyWarps * 32), smem,
+                            stream, dim3(splits), reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                            reinterpret_cast<const __nv_bfloat16*>(w), ldw, y, ldy,
+                            reinterpret_cast<const __nv_bfloat16*>(residual), M, N, K, splits, cps, out_fp32);
 }
 
 // M <= 64 per launch; larger M is issued as several 64-token passes by the caller.

@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // the dependent reduce kernel may launch now: it waits for this grid before reading
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_trigger();
   const int nkb = (p.K + TC_BK * KS - 1) / (TC_BK * KS);  // stages (units) per tile
   const int U = p.tiles * nkb;
   int u0, u1;
@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // barriers and TMEM are set up; the inputs are complete from here on
 
   if (warp == 0) {
     if (lane == 0) {
@@ -282,7 +283,8 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
 // consecutive rows of one token (float4 loads, all slots' loads issued before the sum).
 template <int BN>
 __global__ void __launch_bounds__(256) tc_reduce_kernel(TcParams p, int U, int C, int nkb) {
-  asm volatile("griddepcontrol.wait;" ::: "memory");  // the GEMM grid is complete and visible
+  pdl_trigger();
+  pdl_wait();  // the GEMM grid is complete and its partials visible
   const int tile = blockIdx.y;
   const int c_first = sk_owner(U, C, tile * nkb), c_last = sk_owner(U, C, (tile + 1) * nkb - 1);
   if (c_first == c_last) return;  // one CTA covered the tile: written directly
@@ -433,25 +435,15 @@ static int launch_tc_t(const void* x, int ldx, const void* w, int ldw, TcParams&
     return OKC_ERR_WORKSPACE;  // (the tile-count bound keeps the documented N limit)
   p.tiles = pl.tiles;
   p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(ws) + kTcCounterBytes);
-  tc_gemm_kernel<BN, STAGES, KS><<<pl.ctas, 192, C::SMEM, stream>>>(mw, mx, p);
-  int st = okc_host::launch_status();
+  int st = okc_host::launch_k(tc_gemm_kernel<BN, STAGES, KS>, dim3(pl.ctas), dim3(192), C::SMEM, stream, dim3(1),
+                              mw, mx, p);
   if (st) return st;
   // Reduce of the split tiles, as a programmatic dependent launch: its blocks may be scheduled
   // while the GEMM drains and wait in griddepcontrol.wait until the GEMM grid has completed.
   if ((long long)pl.tiles * pl.nkb <= pl.ctas && pl.nkb == 1) return OKC_OK;  // no split tile
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((min(p.M, BN) + 7) / 8), (unsigned)pl.tiles, 1);
-  cfg.blockDim = dim3(256, 1, 1);
-  cfg.dynamicSmemBytes = 0;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
   const int U = pl.tiles * pl.nkb;
-  if (cudaLaunchKernelEx(&cfg, tc_reduce_kernel<BN>, p, U, pl.ctas, pl.nkb) != cudaSuccess) return OKC_ERR_LAUNCH;
-  return okc_host::launch_status();
+  return okc_host::launch_k(tc_reduce_kernel<BN>, dim3((unsigned)((min(p.M, BN) + 7) / 8), (unsigned)pl.tiles),
+                            dim3(256), 0, stream, dim3(1), p, U, pl.ctas, pl.nkb);
 }
 
 int launch_tc_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy, const void* residual, int M,

@@ -13,6 +13,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
                                                       const __nv_bfloat16* __restrict__ w,
                                                       __nv_bfloat16* __restrict__ y, int ldy, int H,
                                                       float eps, int unit_offset) {
+  pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   const __nv_bfloat16* xr = x + (size_t)t * ldx;
   __nv_bfloat16* yr = y + (size_t)t * ldy;
@@ -55,10 +57,10 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
 
 int launch_rmsnorm(const void* x, int ldx, const void* w, void* y, int ldy, int T, int H, float eps,
                    int unit_offset, cudaStream_t stream) {
-  rmsnorm_kernel<<<T, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                                        reinterpret_cast<const __nv_bfloat16*>(w),
-                                        reinterpret_cast<__nv_bfloat16*>(y), ldy, H, eps, unit_offset);
-  return okc_host::launch_status();
+  return okc_host::launch_k(rmsnorm_kernel, dim3(T), dim3(256), 0, stream, dim3(1),
+                            reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                            reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<__nv_bfloat16*>(y), ldy,
+                            H, eps, unit_offset);
 }
 
 }  // namespace okc
