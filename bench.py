@@ -213,12 +213,17 @@ def run_okc(args):
 
     ev_a0 = torch.cuda.Event(enable_timing=True, external=True)
     ev_a1 = torch.cuda.Event(enable_timing=True, external=True)
+    # stage boundaries inside the graph (external events): norm+QKV, RoPE/append, attention,
+    # O projection, all-reduce + residual
+    ev_s = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(4)]
     xn_buf = {}
 
     def step_instrumented():
         cfgl, dd = layer.cfg, layer.cfg.head_dim
+        ev_s[0].record()
         xn = ops.rmsnorm(x, layer.norm_w, cfgl.eps)
         qkv = ops.gemm(xn, layer.wqkv)
+        ev_s[1].record()
         q = ops.rope_kv_append(qkv, positions, table, kc, vc, layer.k_scale, layer.v_scale, layer.lq,
                                layer.lkv, dd, layer.inv_freq)
         ev_a0.record()
@@ -227,10 +232,13 @@ def run_okc(args):
         o2 = o.view(B, layer.lq * dd)
         if world == 1:
             ops.gemm(o2, layer.wo, residual=x, out=out)
+            ev_s[2].record()
         else:
             part = ops.gemm(o2, layer.wo, out_fp32=True)
+            ev_s[2].record()
             dist.all_reduce(part, group=group)
             out.copy_((x.float() + part).to(torch.bfloat16))
+        ev_s[3].record()
         xn_buf["q"] = q
         return out
 
@@ -271,11 +279,18 @@ def run_okc(args):
 
     # attention duration from the in-graph events (same graph, one replay per sample)
     att_us = []
+    stage_us = {"norm_qkv": [], "rope_append": [], "attention": [], "o_proj": [], "allreduce_residual": []}
     for _ in range(args.steps):
         graph.replay()
         torch.cuda.synchronize()
         att_us.append(ev_a0.elapsed_time(ev_a1) * 1000.0)
+        stage_us["norm_qkv"].append(ev_s[0].elapsed_time(ev_s[1]) * 1000.0)
+        stage_us["rope_append"].append(ev_s[1].elapsed_time(ev_a0) * 1000.0)
+        stage_us["attention"].append(ev_a0.elapsed_time(ev_a1) * 1000.0)
+        stage_us["o_proj"].append(ev_a1.elapsed_time(ev_s[2]) * 1000.0)
+        stage_us["allreduce_residual"].append(ev_s[2].elapsed_time(ev_s[3]) * 1000.0)
     att_avg = statistics.mean(att_us)
+    stages = {k: round(statistics.median(v), 2) for k, v in stage_us.items()}
     kv_bytes = sum((n + 1) for n in att["lens"]) * lkv * d * 2
     act_bytes = B * lq * d * 2 * 2 + B * table.shape[1] * 4
     alg_bytes = kv_bytes + act_bytes
@@ -336,6 +351,7 @@ def run_okc(args):
                          "alg_bytes_per_launch": alg_bytes, "launch_us": round(att_avg, 2),
                          "peak_source": peak_kind},
             "gpu_launches": layer.kernels_per_step(B) * args.steps,
+            "stages_us": stages,
             "clocks": clocks, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

@@ -151,25 +151,43 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
 
   if (warp == 8) {
     // ------------------------------- producer -------------------------------------
+    // The page-table entries of unit u+1 are loaded (lane sg: the unit's sg-th page span)
+    // while unit u waits for its ring slot, so the lookup latency is off the critical path.
     const uint64_t pol = l2_evict_first_policy();
+    struct Span { int b, t0, t_end, p_first, nseg, page; };
+    auto lookup = [&](int u, int bb) {
+      Span f;
+      f.b = bb;
+      f.t0 = (u - prefix[bb]) * C::TS;
+      f.t_end = min(a.seq_lens[bb], f.t0 + C::TS);
+      f.p_first = f.t0 / a.P;
+      f.nseg = (f.t_end - 1) / a.P - f.p_first + 1;
+      const int lp = f.p_first + lane;
+      f.page = (lane < f.nseg && lp < a.table_ld) ? a.page_table[(size_t)bb * a.table_ld + lp] : -1;
+      return f;
+    };
+    auto page_of = [&](const Span& f, int sg) {
+      if (sg < 32) return f.page;  // (lane == sg)
+      const int lp = f.p_first + sg;
+      return lp < a.table_ld ? a.page_table[(size_t)f.b * a.table_ld + lp] : -1;
+    };
     int b = find_seq(prefix, a.B, u0);
     int stage = 0;
     uint32_t phase = 0;
     int issued = 0;
+    Span nxt = lookup(u0, b);
     for (int u = u0; u < u1; ++u) {
-      while (prefix[b + 1] <= u) ++b;
       if (*abort_flag) break;
-      const int len = a.seq_lens[b];
-      const int t0 = (u - prefix[b]) * C::TS;
-      const int t_end = min(len, t0 + C::TS);
-      const int p_first = t0 / a.P, p_last = (t_end - 1) / a.P;
-      const int nseg = p_last - p_first + 1;
-      // page lookups first, so the expected byte count is exact
+      const Span cur = nxt;
+      if (u + 1 < u1) {
+        while (prefix[b + 1] <= u + 1) ++b;
+        nxt = lookup(u + 1, b);
+      }
       uint32_t my_bytes = 0;
-      for (int sg = lane; sg < nseg; sg += 32) {
-        const int lp = p_first + sg;
-        const int page = lp < a.table_ld ? a.page_table[(size_t)b * a.table_ld + lp] : -1;
-        const int lo = max(t0, lp * a.P), hi = min(t_end, (lp + 1) * a.P);
+      for (int sg = lane; sg < cur.nseg; sg += 32) {
+        const int lp = cur.p_first + sg;
+        const int page = page_of(cur, sg);
+        const int lo = max(cur.t0, lp * a.P), hi = min(cur.t_end, (lp + 1) * a.P);
         if (page >= 0 && page < a.num_pages) my_bytes += 2u * (uint32_t)(hi - lo) * C::ROW;
         else atomicOr(a.err, OKC_DEVERR_PAGE);
       }
@@ -186,14 +204,14 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
       __syncwarp();
       uint8_t* sk = stages + (size_t)stage * C::STAGE;
       uint8_t* sv = sk + C::KV_BYTES;
-      for (int sg = lane; sg < nseg; sg += 32) {
-        const int lp = p_first + sg;
-        const int page = lp < a.table_ld ? a.page_table[(size_t)b * a.table_ld + lp] : -1;
+      for (int sg = lane; sg < cur.nseg; sg += 32) {
+        const int lp = cur.p_first + sg;
+        const int page = page_of(cur, sg);
         if (page < 0 || page >= a.num_pages) continue;
-        const int lo = max(t0, lp * a.P), hi = min(t_end, (lp + 1) * a.P);
+        const int lo = max(cur.t0, lp * a.P), hi = min(cur.t_end, (lp + 1) * a.P);
         const size_t src = ((size_t)page * a.P + (lo - lp * a.P)) * C::ROW;
         const uint32_t bytes = (uint32_t)(hi - lo) * C::ROW;
-        const int dst = (lo - t0) * C::ROW;
+        const int dst = (lo - cur.t0) * C::ROW;
         bulk_g2s(sk + dst, a.k_cache + src, bytes, &full[stage], pol);
         bulk_g2s(sv + dst, a.v_cache + src, bytes, &full[stage], pol);
       }
@@ -469,29 +487,45 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int
   if (ul >= uf) {
     const int cf = cta_of_unit(U, a.num_ctas, uf), cl = cta_of_unit(U, a.num_ctas, ul);
     const int nparts = (cl - cf + 1) * NSUB;
+    auto row_of = [&](int p) { return ((size_t)(cf + p / NSUB + b) * NSUB + p % NSUB) * a.Hq + hq; };
+    // (m, l) of part p live in lane p % 32 (round p / 32); every load is issued up front
     float M = -INFINITY;
-    for (int p = lane; p < nparts; p += 32) {
-      const size_t rowi = ((size_t)(cf + p / NSUB + b) * NSUB + p % NSUB) * a.Hq + hq;
-      M = fmaxf(M, a.ws_ml[rowi * 2]);
+    for (int p0 = 0; p0 < nparts; p0 += 32) {
+      const int p = p0 + lane;
+      if (p < nparts) M = fmaxf(M, a.ws_ml[row_of(p) * 2]);
     }
     M = warp_max(M);
     if (M != -INFINITY) {
-#pragma unroll 4
-      for (int p = 0; p < nparts; ++p) {
-        const size_t rowi = ((size_t)(cf + p / NSUB + b) * NSUB + p % NSUB) * a.Hq + hq;
-        const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + rowi * 2);
-        if (ml.x == -INFINITY) continue;
-        const float w = exp2f(ml.x - M);
-        L += w * ml.y;
-        const float* src = a.ws_acc + rowi * D + lane * per;
-        if (per == 4) {
-          const float4 v = *reinterpret_cast<const float4*>(src);
-          o[0] += w * v.x; o[1] += w * v.y; o[2] += w * v.z; o[3] += w * v.w;
-        } else {
-          const float2 v = *reinterpret_cast<const float2*>(src);
-          o[0] += w * v.x; o[1] += w * v.y;
+#pragma unroll 1
+      for (int p0 = 0; p0 < nparts; p0 += 32) {
+        const int p = p0 + lane;
+        float w = 0.f;
+        if (p < nparts) {
+          const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + row_of(p) * 2);
+          w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+          L += w * ml.y;
+        }
+        const int n = min(32, nparts - p0);
+#pragma unroll 1
+        for (int i0 = 0; i0 < n; i0 += 8) {
+          float4 v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i0 + i < n) {
+              const float* src = a.ws_acc + row_of(p0 + i0 + i) * D + lane * per;
+              if (per == 4) v[i] = *reinterpret_cast<const float4*>(src);
+              else { const float2 t = *reinterpret_cast<const float2*>(src); v[i].x = t.x; v[i].y = t.y; }
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float wi = __shfl_sync(0xffffffffu, w, (i0 + i) & 31);
+            o[0] += wi * v[i].x; o[1] += wi * v[i].y; o[2] += wi * v[i].z; o[3] += wi * v[i].w;
+          }
         }
       }
+      L = warp_sum(L);
     }
   }
   const float scale = L > 0.f ? a.v_scale[hq / a.G] / L : 0.f;
@@ -500,10 +534,13 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int
   if (a.gate) {
     // Muse output gate (muse_prefill_layer/submission.py:176): rms(o) * sigmoid(gate), per head
     float ss = 0.f;
-    for (int i = 0; i < per; ++i) ss += o[i] * o[i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ss += i < per ? o[i] * o[i] : 0.f;
     const float inv = rsqrtf(warp_sum(ss) / (float)D + a.out_eps);
     const __nv_bfloat16* g = a.gate + (size_t)b * a.ld_gate + (size_t)hq * D + lane * per;
-    for (int i = 0; i < per; ++i) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (i >= per) break;
       const float gv = __bfloat162float(g[i]);
       o[i] = o[i] * inv * (1.f / (1.f + expf(-gv)));
     }

@@ -35,12 +35,13 @@ def _time(fn, warmup, launches):
 
 
 def case_attn(a):
-    c = synth.attention_case(B=a.b, ctx=(a.ctx_lo, a.ctx_hi), pool_pages=a.pool, device="cuda", seed=0)
+    c = synth.attention_case(B=a.b, Hq=a.hq, Hkv=a.hkv, ctx=(a.ctx_lo, a.ctx_hi), pool_pages=a.pool, device="cuda",
+                             seed=0)
     fn = lambda: ops.attn_decode(c["q"], c["k_cache"], c["v_cache"], c["page_table"], c["seq_lens"],  # noqa
                                  c["k_scale"], c["v_scale"], c["sm_scale"])
     us = _time(fn, a.warmup, a.launches)
-    by = sum(c["lens"]) * 8 * 128 * 2
-    return {"case": "attn", "B": a.b, "ctx": [a.ctx_lo, a.ctx_hi], "us": us, "kv_bytes": by,
+    by = sum(c["lens"]) * a.hkv * 128 * 2
+    return {"case": "attn", "B": a.b, "hq": a.hq, "hkv": a.hkv, "ctx": [a.ctx_lo, a.ctx_hi], "us": us, "kv_bytes": by,
             "gbs": by / us / 1e3}
 
 
@@ -78,6 +79,8 @@ def main(argv=None):
     ap.add_argument("--ctx-lo", type=int, default=512)
     ap.add_argument("--ctx-hi", type=int, default=4096)
     ap.add_argument("--pool", type=int, default=1 << 14)
+    ap.add_argument("--hq", type=int, default=64)
+    ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--k", type=int, default=8192)
     ap.add_argument("--n", type=int, default=10240)
