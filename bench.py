@@ -4,8 +4,9 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl okc|reference]
 
-N > 1 runs under torchrun, one rank per GPU, tensor parallel over the heads with one NCCL
-all-reduce after the row-parallel O projection.  Rank 0 prints ONE JSON line.
+N > 1 runs under torchrun, one rank per GPU, tensor parallel over the heads; after the
+row-parallel O projection one kernel over NVLink peer memory (okc_tp_allreduce_residual) sums
+the ranks' partials and adds the residual.  Rank 0 prints ONE JSON line.
 
 value     = device time per step (CUDA events around K graph replays, max over ranks), µs.
 e2e       = the same step through the public API with the step's input copied in from
@@ -234,10 +235,10 @@ def run_okc(args):
             ops.gemm(o2, layer.wo, residual=x, out=out)
             ev_s[2].record()
         else:
-            part = ops.gemm(o2, layer.wo, out_fp32=True)
+            comm = layer.comm_for(B)
+            ops.gemm(o2, layer.wo, out_fp32=True, out=comm.partial)
             ev_s[2].record()
-            dist.all_reduce(part, group=group)
-            out.copy_((x.float() + part).to(torch.bfloat16))
+            out.copy_(comm.allreduce_residual(x))
         ev_s[3].record()
         xn_buf["q"] = q
         return out
@@ -357,6 +358,9 @@ def run_okc(args):
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
+        torch.cuda.synchronize()
+        dist.barrier()
+        layer.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

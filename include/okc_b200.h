@@ -209,6 +209,35 @@ int okc_moe_experts_w4a16(const void* x, const int32_t* ids, const float* weight
                           void* out, int T, int topk, int H, int I, int expert_lo, int E_local,
                           void* workspace, size_t workspace_bytes, okc_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * Tensor-parallel exchange over NVLink peer memory (multi-GPU layer step).  No reference
+ * counterpart: the reference runs the layer on one GPU.  Replaces the NCCL all-reduce of the
+ * row-parallel O-projection partials followed by the residual add (the multi-GPU contract
+ * of the decode layer: column-parallel QKV, row-parallel O, all-reduce after O).
+ *
+ * okc_ipc_alloc / okc_ipc_free: a zero-filled device buffer of its own cudaMalloc
+ * allocation (so that its IPC handle maps exactly that buffer).  okc_ipc_handle writes the
+ * 64-byte cudaIpcMemHandle_t of such a buffer; okc_ipc_open maps a peer's handle (peer
+ * access enabled lazily); okc_ipc_close unmaps it.
+ *
+ * okc_tp_allreduce_residual: out_r = bf16(residual + sum_q parts[q]) on every rank r.
+ * parts[q] (fp32 [n]), outs[q] (bf16 [n]) and flags[q] (int [16], zero-filled) are HOST
+ * arrays of `world` device pointers: this rank's own buffers at index `rank`, the peers'
+ * mapped buffers elsewhere.  state: this rank's int [2] (zero-filled), private to one
+ * exchange group.  Every rank calls it in the same order on its own stream.  Rank r sums
+ * the r-th slice of the elements in rank order and stores it into every rank's output;
+ * the call completes on a rank when all slices have arrived there.  Flag waits are
+ * bounded (2 s): on expiry OKC_DEVERR_TIMEOUT is set in the workspace error word.
+ * n multiple of 4; world 2..8; parts 16-byte aligned, outs and residual 8-byte aligned. */
+int okc_ipc_alloc(size_t bytes, void** ptr);
+int okc_ipc_free(void* ptr);
+int okc_ipc_handle(const void* ptr, void* handle_out);
+int okc_ipc_open(const void* handle, void** ptr);
+int okc_ipc_close(void* ptr);
+int okc_tp_allreduce_residual(const float* const* parts, void* const* outs, int* const* flags,
+                              const void* residual, int* state, int rank, int world,
+                              long long n, void* workspace, okc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -50,6 +50,13 @@ SIGNATURES: dict[str, tuple] = {
                                        _i, _i, _i, _i, _i, _i64, _f, _i, _p, _i, _f, _p, _sz, _p]),
     "okc_attn_decode_fp8": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
                                  _i, _i, _i, _i, _i, _i64, _f, _i, _p, _sz, _p]),
+    "okc_ipc_alloc": (_i, [_sz, C.POINTER(_p)]),
+    "okc_ipc_free": (_i, [_p]),
+    "okc_ipc_handle": (_i, [_p, _p]),
+    "okc_ipc_open": (_i, [_p, C.POINTER(_p)]),
+    "okc_ipc_close": (_i, [_p]),
+    "okc_tp_allreduce_residual": (_i, [C.POINTER(_p), C.POINTER(_p), C.POINTER(_p), _p, _p, _i, _i, C.c_longlong,
+                                       _p, _p]),
     "okc_attn_decode_fp8_noalloc": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
                                          _i, _i, _i, _i, _i, _i64, _f, _i, _p]),
     "okc_moe_route": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),

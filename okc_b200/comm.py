@@ -1,0 +1,125 @@
+"""Tensor-parallel exchange of the multi-GPU decode layer over NVLink peer memory.
+
+`TPComm` owns, on every rank of a process group, three device buffers of its own
+allocation (the fp32 O-projection partial, the bf16 layer output and 16 flag words), exchanges
+their CUDA IPC handles once (torch.distributed is the plumbing: all_gather_object), maps the
+peers' buffers, and then runs `okc_tp_allreduce_residual`: out = bf16(x + sum_r partial_r),
+replicated on every rank, in one kernel that reads and writes the peers' memory directly.
+It replaces the NCCL all-reduce of the partial plus the residual add (one launch instead of
+a collective and three elementwise kernels).  Every rank must construct it and call it in the
+same order; it is CUDA-graph capturable (fixed buffers, the call epoch lives on the device).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+import torch.distributed as dist
+
+from . import _lib, ops
+
+
+class _DeviceBuffer:
+    """A zero-filled cudaMalloc'd buffer (so its IPC handle maps exactly this buffer)."""
+
+    def __init__(self, nbytes: int):
+        self.ptr = C.c_void_p()
+        _lib.check(_lib.load().okc_ipc_alloc(nbytes, C.byref(self.ptr)), "okc_ipc_alloc")
+        self.nbytes = nbytes
+
+    def handle(self) -> bytes:
+        h = C.create_string_buffer(64)
+        _lib.check(_lib.load().okc_ipc_handle(self.ptr, h), "okc_ipc_handle")
+        return h.raw
+
+    def free(self):
+        if self.ptr:
+            _lib.load().okc_ipc_free(self.ptr)
+            self.ptr = C.c_void_p()
+
+
+class _CudaArray:
+    """__cuda_array_interface__ over memory this module owns (no copy, no ownership)."""
+
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 2}
+
+
+def _from_ptr(ptr: int, nbytes: int, dtype, device) -> torch.Tensor:
+    typestr, size = {torch.float32: ("<f4", 4), torch.bfloat16: ("<i2", 2), torch.int32: ("<i4", 4)}[dtype]
+    t = torch.as_tensor(_CudaArray(ptr, nbytes // size, typestr), device=device)
+    return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t
+
+
+class TPComm:
+    """One exchange group: partial fp32 [T, H] -> out bf16 [T, H] on `world` ranks."""
+
+    def __init__(self, T: int, H: int, group=None, device: int | None = None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if not 2 <= self.world <= 8:
+            raise ValueError("TPComm needs 2..8 ranks")
+        if (T * H) % 4:
+            raise ValueError("T*H must be a multiple of 4")
+        self.device = torch.cuda.current_device() if device is None else device
+        self.T, self.H = T, H
+        with torch.cuda.device(self.device):
+            self._part = _DeviceBuffer(T * H * 4)
+            self._out = _DeviceBuffer(T * H * 2)
+            self._flags = _DeviceBuffer(16 * 4)
+            self.state = torch.zeros(4, dtype=torch.int32, device=f"cuda:{self.device}")
+            mine = (self._part.handle(), self._out.handle(), self._flags.handle())
+            allh = [None] * self.world
+            dist.all_gather_object(allh, mine, group=group)
+            lib = _lib.load()
+            self._opened = []
+            parts, outs, flags = [], [], []
+            for q in range(self.world):
+                if q == self.rank:
+                    parts.append(self._part.ptr.value)
+                    outs.append(self._out.ptr.value)
+                    flags.append(self._flags.ptr.value)
+                    continue
+                ptrs = []
+                for h in allh[q]:
+                    p = C.c_void_p()
+                    _lib.check(lib.okc_ipc_open(C.create_string_buffer(h, 64), C.byref(p)), "okc_ipc_open")
+                    self._opened.append(p)
+                    ptrs.append(p.value)
+                parts.append(ptrs[0])
+                outs.append(ptrs[1])
+                flags.append(ptrs[2])
+            arr = C.c_void_p * self.world
+            self._parts_arr = arr(*parts)
+            self._outs_arr = arr(*outs)
+            self._flags_arr = arr(*flags)
+            self.partial = _from_ptr(self._part.ptr.value, T * H * 4, torch.float32,
+                                     f"cuda:{self.device}").view(T, H)
+            self.out = _from_ptr(self._out.ptr.value, T * H * 2, torch.bfloat16,
+                                 f"cuda:{self.device}").view(T, H)
+            self._ws = ops.workspace(self.device, "tp", 256)
+        dist.barrier(group=group)
+
+    def allreduce_residual(self, residual: torch.Tensor) -> torch.Tensor:
+        """out = bf16(residual + sum over ranks of `self.partial`) on every rank; returns
+        `self.out` (valid until the next call)."""
+        if residual.dtype != torch.bfloat16 or residual.shape != (self.T, self.H) or not residual.is_contiguous():
+            raise ValueError("residual must be a contiguous bf16 [T, H] tensor")
+        lib = _lib.load()
+        st = lib.okc_tp_allreduce_residual(self._parts_arr, self._outs_arr, self._flags_arr, residual.data_ptr(),
+                                           self.state.data_ptr(), self.rank, self.world, self.T * self.H,
+                                           self._ws.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(st, "okc_tp_allreduce_residual")
+        return self.out
+
+    def close(self):
+        """Unmaps the peers' buffers and frees this rank's (call on every rank, after a
+        barrier, when no kernel that uses them is in flight)."""
+        lib = _lib.load()
+        for p in self._opened:
+            lib.okc_ipc_close(p)
+        self._opened = []
+        for b in (self._part, self._out, self._flags):
+            b.free()

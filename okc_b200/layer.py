@@ -7,8 +7,8 @@ Every stage is an okc_b200 kernel; the step is captured in one CUDA graph by the
 (bench.py) so launch latency does not count.  Tensor parallel over `world` ranks: rank r
 owns query heads [r*Hq/W, (r+1)*Hq/W) and KV heads [r*Hkv/W, ...) — its slice of the
 QKV weight (column parallel, no communication) and of its own paged cache; the O
-projection is row parallel, produces an fp32 partial, and one NCCL all-reduce sums the
-partials before the residual add.  Mirrors the composition of
+projection is row parallel and produces an fp32 partial, and one kernel over NVLink peer
+memory (okc_b200.comm.TPComm) sums the partials of all ranks and adds the residual.  Mirrors the composition of
 muse_decode_layer/decode/runtime.py:47-75 (attention -> O -> boundary) without Muse's
 gated residual, QK-norm and output gate, which this plain layer (RMSNorm, x + O) does not have.
 """
@@ -65,12 +65,13 @@ class DecodeLayer:
             self.k_scale, self.v_scale = k_scale.contiguous(), v_scale.contiguous()
         self.inv_freq = ops.rope_inv_freq(cfg.rope_theta, cfg.head_dim, norm_w.device)
         self.sm_scale = cfg.head_dim ** -0.5
+        self._comms = {}
 
     def kernels_per_step(self, tokens: int) -> int:
         """Our kernel launches in one step (for the bench's gpu_launches)."""
         passes = 1 if tokens <= 256 else (tokens + 255) // 256  # tcgen05 GEMM: 256 tokens a launch
         per_gemm = 2 * passes if tokens > 32 else 1  # tcgen05 stream-K + split-tile reduce
-        return 1 + per_gemm + 1 + 2 + per_gemm
+        return 1 + per_gemm + 1 + 2 + per_gemm + (1 if self.world > 1 else 0)
 
     def step(self, x, positions, page_table, k_cache, v_cache, lens=None, out=None):
         """x bf16 [B, H]; positions int64 [B] (= tokens already cached); caches of this rank's
@@ -87,10 +88,30 @@ class DecodeLayer:
         o2 = o.view(B, self.lq * d)
         if self.world == 1:
             return ops.gemm(o2, self.wo, residual=x, out=out)
-        part = ops.gemm(o2, self.wo, out_fp32=True)
-        torch.distributed.all_reduce(part, group=self.group)
-        res = (x.float() + part).to(torch.bfloat16)
+        return self.o_proj_allreduce(o2, x, out)
+
+    def comm_for(self, tokens: int):
+        """The NVLink exchange group for `tokens` rows (created on first use: a collective
+        call, so every rank must reach it together and outside CUDA-graph capture)."""
+        from .comm import TPComm
+        c = self._comms.get(tokens)
+        if c is None:
+            c = TPComm(tokens, self.cfg.hidden, group=self.group)
+            self._comms[tokens] = c
+        return c
+
+    def o_proj_allreduce(self, o2, x, out=None):
+        """Row-parallel O projection, then out = bf16(x + sum over ranks) through the
+        peer-memory exchange kernel (okc_tp_allreduce_residual)."""
+        comm = self.comm_for(x.shape[0])
+        ops.gemm(o2, self.wo, out_fp32=True, out=comm.partial)
+        res = comm.allreduce_residual(x)
         if out is not None:
             out.copy_(res)
             return out
         return res
+
+    def close(self):
+        for c in self._comms.values():
+            c.close()
+        self._comms.clear()

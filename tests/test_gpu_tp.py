@@ -1,0 +1,97 @@
+"""Tensor-parallel exchange over NVLink peer memory (okc_tp_allreduce_residual) on 2 GPUs:
+out = bf16(x + sum_r partial_r) on every rank, bit-exact against the same fp32 sums taken in
+rank order on the host side; repeated calls (the device-side epoch) and a CUDA-graph replay.
+Skipped when fewer than 2 GPUs are visible."""
+
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, T, H, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from okc_b200 import ops
+        from okc_b200.comm import TPComm
+        comm = TPComm(T, H)
+        errs = []
+        for it in range(3):
+            parts = [torch.randn((T, H), generator=torch.Generator().manual_seed(100 * it + r)) for r in range(world)]
+            x = torch.randn((T, H), generator=torch.Generator().manual_seed(7 + it)).to(torch.bfloat16)
+            exp = torch.zeros((T, H))
+            for r in range(world):
+                exp = exp + parts[r]
+            exp = (exp + x.float()).to(torch.bfloat16)
+            comm.partial.copy_(parts[rank].cuda())
+            xd = x.cuda()
+            got = comm.allreduce_residual(xd).clone()
+            torch.cuda.synchronize()
+            errs.append(int((got.cpu().view(torch.int16) != exp.view(torch.int16)).sum()))
+        # graph replay of the same exchange (fresh partials copied in before each replay)
+        g = torch.cuda.CUDAGraph()
+        xd = torch.randn((T, H), generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).cuda()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            comm.allreduce_residual(xd)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        with torch.cuda.graph(g):
+            out_g = comm.allreduce_residual(xd)
+        for it in range(2):
+            parts = [torch.randn((T, H), generator=torch.Generator().manual_seed(500 + 10 * it + r)) for r in range(world)]
+            exp = torch.zeros((T, H))
+            for r in range(world):
+                exp = exp + parts[r]
+            exp = (exp + xd.cpu().float()).to(torch.bfloat16)
+            comm.partial.copy_(parts[rank].cuda())
+            torch.cuda.synchronize()
+            dist.barrier()
+            g.replay()
+            torch.cuda.synchronize()
+            errs.append(int((out_g.cpu().view(torch.int16) != exp.view(torch.int16)).sum()))
+        derr = ops.read_device_error("tp", rank)
+        del g
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
+        q.put((rank, errs, derr))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp_allreduce_residual_two_ranks():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    T, H = 128, 1024
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, T, H, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs, derr in res:
+        assert derr == 0, f"rank {rank}: device error {derr}"
+        assert all(e == 0 for e in errs), f"rank {rank}: mismatching elements per call {errs}"
