@@ -85,6 +85,14 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
 
 // Bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) global -> shared,
 // completing `bytes` transactions on `bar`.
+// Same as bulk_g2s with the default L2 policy (for small, re-read data such as activations).
+__device__ __forceinline__ void bulk_g2s_plain(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
                                          uint64_t policy) {
   asm volatile(

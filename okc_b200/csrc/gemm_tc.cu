@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(256) tc_reduce_kernel(TcParams p, int U, int C
 }
 
 // ------------------------------------------------------------------------------ host
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
     void* p = nullptr;
@@ -346,7 +346,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 static bool make_map(CUtensorMap* m, const void* base, int inner, int rows, int ld, int box_rows) {
-  auto fn = encode_fn();
+  auto fn = tensor_map_encoder();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
@@ -359,7 +359,7 @@ static bool make_map(CUtensorMap* m, const void* base, int inner, int rows, int 
 
 bool tc_gemm_supported(int M, int N, int K, int ldx, int ldw) {
   return M >= 1 && M <= 256 && N >= 1 && K >= 16 && K % 8 == 0 && ldx % 8 == 0 && ldw % 8 == 0 &&
-         encode_fn() != nullptr;
+         tensor_map_encoder() != nullptr;
 }
 
 struct TcPlan {

@@ -1,6 +1,8 @@
 // Internal launcher declarations shared by the entry points (capi.cu) and the kernels.
 #pragma once
 
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace okc {
@@ -28,6 +30,9 @@ struct AttnArgs {
   int ld_gate;
   float out_eps;
 };
+
+// cuTensorMapEncodeTiled from the driver (nullptr when unavailable); cached.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 int launch_skinny_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
                        const void* residual, int M, int N, int K, int out_fp32, int splits,

@@ -23,7 +23,7 @@
 #include <cooperative_groups.h>
 #include <stdlib.h>
 
-#include "common.cuh"
+#include "kernels.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -697,6 +697,298 @@ static int launch_moe_pipe(int T, const __half* xin, const int32_t* counts, cons
   return launch_moe_pipe_t<false, 2, 4, 4, 4>(xin, counts, offsets, pairs, w, sf, gs, inter, y, topk, K, NR, I, E, err, stream);
 }
 
+// ---------------------------------------------------------------------------------------
+// Row-owning expert kernel (T <= 64).  A unit = ROWS weight rows of one active expert over the
+// full K; its K is streamed in stages of KC = 512: per stage one 2-D TMA box of codes
+// [ROWS][256 B] and one of scales [ROWS][32 B] per matrix (16 KB + 2 KB), into a 5-deep ring.
+// Warp w owns 16 MMA rows of the unit for the whole K, so its fp32 accumulators finish the
+// rows with no cross-warp reduction and no block barrier:
+//   GATED: MMA rows 0-7 = gate rows 8w..8w+7, rows 8-15 = the same up rows (one MMA yields
+//          both halves of SwiGLU), ROWS = 64;
+//   down:  MMA rows = weight rows 16w..16w+15, ROWS = 128.
+// Tokens: all of the expert's pairs (<= 64) in tiles of 8, x read from L2 per 128-K chunk.
+template <bool GATED, int MTMAX>
+struct MoeRowCfg {
+  static constexpr int KC = 512;
+  static constexpr int ROWS = GATED ? 64 : 128;
+  static constexpr int MATS = GATED ? 2 : 1;
+  static constexpr int CODE_BOX = ROWS * KC / 2;
+  static constexpr int SF_BOX = ROWS * KC / 16;
+  static constexpr int WBYTES = MATS * (CODE_BOX + SF_BOX);  // 36 KB of weights
+  // The first XR token rows' x for this K chunk ride along in the stage (bulk copies of 1 KB,
+  // rows padded to 1040 B so the 8 rows of a fragment load fall in distinct banks); tokens
+  // beyond XR are read from L2.
+  static constexpr int XR = MTMAX >= 2 ? 16 : 8;
+  static constexpr int XROW = KC * 2 + 16;
+  static constexpr int STAGE = WBYTES + XR * XROW;
+  static constexpr int NS = 196608 / STAGE > 5 ? 5 : 196608 / STAGE;
+};
+
+__device__ __forceinline__ void tma_load_2d_u8(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+template <bool GATED, int MTMAX>
+__global__ void __launch_bounds__(288, 1) moe_rows_kernel(
+    const __grid_constant__ CUtensorMap cmap, const __grid_constant__ CUtensorMap smap,
+    const __half* __restrict__ xin, const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets,
+    const int32_t* __restrict__ pairs, const float* __restrict__ gs, __half* __restrict__ inter_out,
+    __nv_bfloat16* __restrict__ y_out, int topk, int K, int NR, int I, int E, int* err) {
+  using C = MoeRowCfg<GATED, MTMAX>;
+  extern __shared__ __align__(128) uint8_t msm_raw[];
+  uint8_t* stages = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(msm_raw) + 127) & ~uintptr_t(127));
+  uint64_t* full = reinterpret_cast<uint64_t*>(stages + (size_t)C::NS * C::STAGE);
+  uint64_t* empty = full + C::NS;
+  int* act = reinterpret_cast<int*>(empty + C::NS);  // [E + 1]
+  volatile int* abort_flag = act + E + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  pdl_wait();
+  if (warp == 0) {  // ordered list of experts with tokens
+    int base = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const bool on = e < E && counts[e] > 0;
+      const unsigned bal = __ballot_sync(0xffffffffu, on);
+      if (on) act[base + __popc(bal & ((1u << lane) - 1u))] = e;
+      base += __popc(bal);
+    }
+    if (lane == 0) act[E] = base;
+  }
+  __syncthreads();
+  const int rows_w = GATED ? 2 * I : NR;           // rows of one expert in the tensor maps
+  const int nrb = (GATED ? I : NR) / C::ROWS;      // row blocks per expert
+  const int nkc = K / C::KC;
+  const int U = act[E] * nrb;
+  const int q = U / (int)gridDim.x, r = U % (int)gridDim.x;
+  const int u0 = blockIdx.x * q + min((int)blockIdx.x, r);
+  const int u1 = u0 + q + ((int)blockIdx.x < r ? 1 : 0);
+  if (u0 >= u1) return;
+
+  if (warp == 8) {
+    // ------------------------------- producer -------------------------------
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      for (int u = u0; u < u1 && !*abort_flag; ++u) {
+        const int e = act[u / nrb];
+        const int y0 = e * rows_w + (u % nrb) * C::ROWS;
+        const int nx = min(counts[e], C::XR), off = offsets[e];
+        for (int kc = 0; kc < nkc; ++kc) {
+          if (*abort_flag || !mbar_wait(&empty[stage], phase ^ 1u, err)) { *abort_flag = 1; break; }
+          mbar_arrive_expect_tx(&full[stage], (uint32_t)(C::WBYTES + nx * C::KC * 2));
+          uint8_t* dst = stages + (size_t)stage * C::STAGE;
+#pragma unroll
+          for (int m = 0; m < C::MATS; ++m) {
+            uint8_t* d = dst + m * (C::CODE_BOX + C::SF_BOX);
+            const int yy = y0 + (m ? I : 0);
+            tma_load_2d_u8(d, &cmap, kc * (C::KC / 2), yy, &full[stage], pol);
+            tma_load_2d_u8(d + C::CODE_BOX, &smap, kc * (C::KC / 16), yy, &full[stage], pol);
+          }
+          for (int i = 0; i < nx; ++i) {  // x rows of the first XR pairs, this K chunk (L2-resident)
+            const int xr = GATED ? pairs[off + i] / topk : off + i;
+            bulk_g2s_plain(dst + C::WBYTES + i * C::XROW, xin + (size_t)xr * K + kc * C::KC, C::KC * 2, &full[stage]);
+          }
+          ++issued;
+          if (++stage == C::NS) { stage = 0; phase ^= 1u; }
+        }
+      }
+      int s = stage;  // make sure the copies issued have landed before leaving
+      uint32_t ph = phase;
+      for (int i = 0; i < min(issued, C::NS); ++i) {
+        if (--s < 0) { s = C::NS - 1; ph ^= 1u; }
+        if (!mbar_wait(&full[s], ph, err)) break;
+      }
+    }
+    return;
+  }
+
+  // -------------------------------- consumers --------------------------------
+  const int g = lane >> 2, c = lane & 3;
+  // shared-memory rows of this lane: "lo" feeds MMA row g, "hi" MMA row g + 8
+  const int row_lo = GATED ? 8 * warp + g : 16 * warp + g;
+  const int row_hi = GATED ? 8 * warp + g : 16 * warp + 8 + g;
+  const int mat_hi = GATED ? 1 : 0;
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int u = u0; u < u1; ++u) {
+    const int e = act[u / nrb];
+    const int rb = u % nrb;
+    const int n_e = min(counts[e], 8 * MTMAX), off = offsets[e];
+    const int ntile = (n_e + 7) >> 3;
+    const float gsc = gs[e];
+    const __half* xrow[MTMAX];
+#pragma unroll
+    for (int t = 0; t < MTMAX; ++t) {
+      const int i = 8 * t + g;
+      int xr = 0;
+      if (i < n_e) xr = GATED ? pairs[off + i] / topk : off + i;
+      xrow[t] = xin + (size_t)xr * K + 32 * c;
+    }
+    float acc[MTMAX][4];
+#pragma unroll
+    for (int t = 0; t < MTMAX; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+    bool ok = true;
+    for (int kc = 0; kc < nkc; ++kc) {
+      ok = ok && !*abort_flag && mbar_wait(&full[stage], phase, err);
+      if (__all_sync(0xffffffffu, ok)) {
+        const uint8_t* sb = stages + (size_t)stage * C::STAGE;
+        const uint8_t* clo_b = sb + (size_t)row_lo * (C::KC / 2);
+        const uint8_t* chi_b = sb + mat_hi * (C::CODE_BOX + C::SF_BOX) + (size_t)row_hi * (C::KC / 2);
+        const uint8_t* slo_b = sb + C::CODE_BOX + (size_t)row_lo * (C::KC / 16);
+        const uint8_t* shi_b = sb + mat_hi * (C::CODE_BOX + C::SF_BOX) + C::CODE_BOX + (size_t)row_hi * (C::KC / 16);
+        const uint8_t* xs_b = sb + C::WBYTES + g * C::XROW + 64 * c;  // token row g (+8 per tile)
+#pragma unroll 1
+        for (int sub = 0; sub < C::KC / 128; ++sub) {
+          const int kl = sub * 128;            // k within the stage
+          const int kb = kc * C::KC + kl;      // absolute k
+          uint4 xq[2][4];                       // x of token tiles t and t+1 (double buffer)
+          auto load_x = [&](uint4 (&dst)[4], int t) {
+            if (8 * t < C::XR) {  // staged with the weights
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                dst[v] = *reinterpret_cast<const uint4*>(xs_b + 8 * t * C::XROW + kl * 2 + 16 * v);
+            } else {
+#pragma unroll
+              for (int v = 0; v < 4; ++v) dst[v] = *reinterpret_cast<const uint4*>(xrow[t] + kb + 8 * v);
+            }
+          };
+          load_x(xq[0], 0);
+          if (MTMAX > 1 && ntile > 1) load_x(xq[1], 1);
+          const uint4 cl = *reinterpret_cast<const uint4*>(clo_b + kl / 2 + 16 * c);
+          const uint4 ch = *reinterpret_cast<const uint4*>(chi_b + kl / 2 + 16 * c);
+          const uint32_t sl16 = *reinterpret_cast<const uint16_t*>(slo_b + kl / 16 + 2 * c);
+          const uint32_t sh16 = *reinterpret_cast<const uint16_t*>(shi_b + kl / 16 + 2 * c);
+          const uint32_t sl[2] = {sf_to_h2(sl16 & 0xff), sf_to_h2(sl16 >> 8)};
+          const uint32_t sh[2] = {sf_to_h2(sh16 & 0xff), sf_to_h2(sh16 >> 8)};
+          uint32_t a[8][4];  // A fragments of the 8 k16 steps of this 128 chunk
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {  // word wi of each row: steps 2wi (bytes 0,1) and 2wi+1 (bytes 2,3)
+            uint32_t l0, l1, l2, l3, h0, h1, h2, h3;
+            e2m1_word_to_f16x2((&cl.x)[wi], l0, l1, l2, l3);
+            e2m1_word_to_f16x2((&ch.x)[wi], h0, h1, h2, h3);
+            const int grp = wi >> 1;
+            a[2 * wi][0] = hmul2u(l0, sl[grp]);
+            a[2 * wi][1] = hmul2u(h0, sh[grp]);
+            a[2 * wi][2] = hmul2u(l1, sl[grp]);
+            a[2 * wi][3] = hmul2u(h1, sh[grp]);
+            a[2 * wi + 1][0] = hmul2u(l2, sl[grp]);
+            a[2 * wi + 1][1] = hmul2u(h2, sh[grp]);
+            a[2 * wi + 1][2] = hmul2u(l3, sl[grp]);
+            a[2 * wi + 1][3] = hmul2u(h3, sh[grp]);
+          }
+#pragma unroll
+          for (int t = 0; t < MTMAX; ++t) {
+            if (t < ntile) {
+              const uint4* xt = xq[t & 1];
+#pragma unroll
+              for (int s8 = 0; s8 < 8; ++s8) {
+                const uint4 v = xt[s8 >> 1];
+                const uint32_t b0 = (s8 & 1) ? v.z : v.x, b1 = (s8 & 1) ? v.w : v.y;
+                mma_f16_16816(acc[t], a[s8][0], a[s8][1], a[s8][2], a[s8][3], b0, b1);
+              }
+              if (t + 2 < ntile) load_x(xq[t & 1], t + 2);
+            }
+          }
+        }
+      } else {
+        ok = false;
+        if (lane == 0) *abort_flag = 1;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == C::NS) { stage = 0; phase ^= 1u; }
+    }
+    if (!ok) continue;
+    // finish the warp's rows: fragment (g, c) holds tokens 2c, 2c+1 of each tile, rows g / g+8
+#pragma unroll
+    for (int t = 0; t < MTMAX; ++t) {
+      if (t >= ntile) break;
+#pragma unroll
+      for (int e2 = 0; e2 < 2; ++e2) {
+        const int i = 8 * t + 2 * c + e2;
+        if (i >= n_e) continue;
+        if (GATED) {
+          const float hg = __bfloat162float(__float2bfloat16_rn(acc[t][e2] * gsc));
+          const float hu = __bfloat162float(__float2bfloat16_rn(acc[t][2 + e2] * gsc));
+          const float act_v = hg / (1.f + expf(-hg)) * hu;
+          inter_out[(size_t)(off + i) * I + rb * C::ROWS + 8 * warp + g] =
+              __float2half_rn(__bfloat162float(__float2bfloat16_rn(act_v)));
+        } else {
+          __nv_bfloat16* yr = y_out + (size_t)pairs[off + i] * NR + rb * C::ROWS + 16 * warp + g;
+          yr[0] = __float2bfloat16_rn(acc[t][e2] * gsc);
+          yr[8] = __float2bfloat16_rn(acc[t][2 + e2] * gsc);
+        }
+      }
+    }
+  }
+}
+
+static bool make_u8_map(CUtensorMap* m, const void* base, long long inner, long long rows, int box_x, int box_y) {
+  auto fn = tensor_map_encoder();
+  if (!fn || !okc_host::aligned16(base) || inner % 16 || rows <= 0 || rows >= (1LL << 31)) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)inner};
+  cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_y};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Shapes the row-owning kernel takes: K a multiple of 512, whole row blocks, <= 64 tokens.
+static bool moe_rows_ok(int T, int H, int I) {
+  return T <= 64 && H % 512 == 0 && I % 512 == 0 && I % MoeRowCfg<true, 1>::ROWS == 0 &&
+         H % MoeRowCfg<false, 1>::ROWS == 0 && tensor_map_encoder() != nullptr;
+}
+
+template <bool GATED, int MTMAX>
+static int launch_moe_rows_t(const void* w, const void* sf, int E, const __half* xin, const int32_t* counts,
+                             const int32_t* offsets, const int32_t* pairs, const float* gs, __half* inter,
+                             __nv_bfloat16* y, int topk, int K, int NR, int I, int* err, cudaStream_t stream) {
+  using C = MoeRowCfg<GATED, MTMAX>;
+  const long long rows = (long long)E * (GATED ? 2 * I : NR);
+  CUtensorMap cm, sm;
+  if (!make_u8_map(&cm, w, K / 2, rows, C::KC / 2, C::ROWS) || !make_u8_map(&sm, sf, K / 16, rows, C::KC / 16, C::ROWS))
+    return OKC_ERR_INVALID;
+  const size_t smem = 128 + (size_t)C::NS * C::STAGE + 2 * C::NS * 8 + (size_t)(E + 2) * 4;
+  if (smem > 232448) return OKC_ERR_INVALID;
+  static size_t configured = 0;
+  if (smem > configured) {
+    if (cudaFuncSetAttribute(moe_rows_kernel<GATED, MTMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+      return OKC_ERR_LAUNCH;
+    configured = smem;
+  }
+  return okc_host::launch_k(moe_rows_kernel<GATED, MTMAX>, dim3(okc_host::num_sms()), dim3(288), smem, stream,
+                            dim3(1), cm, sm, xin, counts, offsets, pairs, gs, inter, y, topk, K, NR, I, E, err);
+}
+
+template <bool GATED>
+static int launch_moe_rows(int T, const void* w, const void* sf, int E, const __half* xin, const int32_t* counts,
+                           const int32_t* offsets, const int32_t* pairs, const float* gs, __half* inter,
+                           __nv_bfloat16* y, int topk, int K, int NR, int I, int* err, cudaStream_t stream) {
+  if (T <= 8) return launch_moe_rows_t<GATED, 1>(w, sf, E, xin, counts, offsets, pairs, gs, inter, y, topk, K, NR, I, err, stream);
+  if (T <= 16) return launch_moe_rows_t<GATED, 2>(w, sf, E, xin, counts, offsets, pairs, gs, inter, y, topk, K, NR, I, err, stream);
+  if (T <= 32) return launch_moe_rows_t<GATED, 4>(w, sf, E, xin, counts, offsets, pairs, gs, inter, y, topk, K, NR, I, err, stream);
+  return launch_moe_rows_t<GATED, 8>(w, sf, E, xin, counts, offsets, pairs, gs, inter, y, topk, K, NR, I, err, stream);
+}
+
 __global__ void __launch_bounds__(256) to_f16_kernel(const __nv_bfloat16* __restrict__ x,
                                                      __half* __restrict__ y, size_t n) {
   for (size_t i = (blockIdx.x * (size_t)blockDim.x + threadIdx.x) * 8; i < n;
@@ -837,7 +1129,18 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
   int st = okc_host::launch_status();
   if (st) return st;
   int* err = reinterpret_cast<int*>(ws);
-  const int pipe_env = getenv("OKC_MOE_PIPE") ? atoi(getenv("OKC_MOE_PIPE")) : 1;
+  const int pipe_env = getenv("OKC_MOE_PIPE") ? atoi(getenv("OKC_MOE_PIPE")) : 2;
+  if (pipe_env == 2 && moe_rows_ok(T, H, I)) {
+    st = launch_moe_rows<true>(T, w13, w13_sf, E, xh, counts, offsets, pairs, w13_gs, inter, nullptr, topk, H, I, I,
+                               err, stream);
+    if (st) return st;
+    st = launch_moe_rows<false>(T, w2, w2_sf, E, inter, counts, offsets, pairs, w2_gs, nullptr, y, topk, I, H, I,
+                                err, stream);
+    if (st) return st;
+    combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, reinterpret_cast<__nv_bfloat16*>(out),
+                                                                 topk, H, expert_lo, E);
+    return okc_host::launch_status();
+  }
   // Measured on B200: the pipelined kernel wins up to 64 tokens, the per-expert kernel above.
   const bool pipe_ok = pipe_env && T <= 64 && H % 1024 == 0 && I % 512 == 0 && I % 16 == 0 && H % 32 == 0 &&
                        (size_t)16 * 2 * (H / 2 + H / 16) * 2 < 200000;
