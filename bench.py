@@ -11,8 +11,9 @@ the ranks' partials and adds the residual.  Rank 0 prints ONE JSON line.
 value     = device time per step (CUDA events around K graph replays, max over ranks), µs.
 e2e       = the same step through the public API with the step's input copied in from
             pinned host memory and its output copied back every step, µs.
-roofline  = the attention kernel (the dominant kernel) measured with CUDA events inside the
-            same graph: algorithmic KV bytes / duration vs MEASURED_PEAKS.json hbm_gbs.
+roofline  = the attention kernel (the dominant kernel) measured with CUDA events inside an
+            instrumented copy of the step graph: algorithmic KV bytes / duration vs
+            MEASURED_PEAKS.json hbm_gbs; stages_us = per-stage times from the same copy.
 cpu_baseline / --impl reference = the oracle (the reference's PyTorch path restated, CPU
             fp32) on the host cores, a bounded sample scaled to one full step.
 """
@@ -243,16 +244,25 @@ def run_okc(args):
         xn_buf["q"] = q
         return out
 
+    # Two graphs of the same step: `graph` is the public API call (DecodeLayer.step) with no
+    # event inside, so programmatic dependent launch chains every kernel to the next; it is
+    # what `value` and `e2e` time.  `graph_i` adds external events between the stages (an event
+    # node breaks the programmatic chain there) for the attention roofline and `stages_us`.
     s = torch.cuda.Stream(device=dev)
     s.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(s):
         step_instrumented()
+        step()
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
+    graph_i = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_i):
+        step_instrumented()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        step_instrumented()
+        step()
     for _ in range(max(args.warmup, 3)):
+        graph_i.replay()
         graph.replay()
     torch.cuda.synchronize()
 
@@ -278,11 +288,11 @@ def run_okc(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     us = float(t.item())
 
-    # attention duration from the in-graph events (same graph, one replay per sample)
+    # attention and stage durations from the instrumented graph (one replay per sample)
     att_us = []
     stage_us = {"norm_qkv": [], "rope_append": [], "attention": [], "o_proj": [], "allreduce_residual": []}
     for _ in range(args.steps):
-        graph.replay()
+        graph_i.replay()
         torch.cuda.synchronize()
         att_us.append(ev_a0.elapsed_time(ev_a1) * 1000.0)
         stage_us["norm_qkv"].append(ev_s[0].elapsed_time(ev_s[1]) * 1000.0)
@@ -356,7 +366,7 @@ def run_okc(args):
             "clocks": clocks, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    del graph
+    del graph, graph_i
     if world > 1:
         torch.cuda.synchronize()
         dist.barrier()

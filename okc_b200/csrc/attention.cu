@@ -143,6 +143,8 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
   pdl_wait();
   unit_prefix(a.seq_lens, a.B, C::TS, prefix);
   __syncthreads();
+  if (blockIdx.x == 0)  // for the merge kernel
+    for (int i = threadIdx.x; i <= a.B; i += blockDim.x) a.ws_prefix[i] = prefix[i];
 
   const int U = prefix[a.B];
   int u0, u1;
@@ -469,64 +471,57 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
 // One warp per (sequence, query head); lane owns D/32 consecutive d.  Parts are read in a
 // fixed order, so the result does not depend on which CTA finished first.
 __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int NSUB, int D) {
-  extern __shared__ int mprefix[];
   pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x;
-  unit_prefix(a.seq_lens, a.B, TS, mprefix);
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hq = blockIdx.y * 8 + warp;
   if (hq >= a.Hq) return;
   const int per = D / 32;  // 4 (D = 128) or 2 (D = 64)
   __nv_bfloat16* dst = a.out + (size_t)b * a.ldo + (size_t)hq * D + lane * per;
-  const int U = mprefix[a.B];
-  const int uf = mprefix[b], ul = mprefix[b + 1] - 1;
+  const int U = a.ws_prefix[a.B];  // unit prefix from the attention kernel
+  const int uf = a.ws_prefix[b], ul = a.ws_prefix[b + 1] - 1;
   float o[4] = {0.f, 0.f, 0.f, 0.f};
   float L = 0.f;
   if (ul >= uf) {
     const int cf = cta_of_unit(U, a.num_ctas, uf), cl = cta_of_unit(U, a.num_ctas, ul);
     const int nparts = (cl - cf + 1) * NSUB;
     auto row_of = [&](int p) { return ((size_t)(cf + p / NSUB + b) * NSUB + p % NSUB) * a.Hq + hq; };
-    // (m, l) of part p live in lane p % 32 (round p / 32); every load is issued up front
+    // Batches of 16 parts: the (m, l) of part p0 + i sit in lane i, and the 16 parts' slices
+    // of acc are loaded in the same round, so one batch costs one memory round trip.  A
+    // running maximum carries the log-sum-exp across batches.
     float M = -INFINITY;
-    for (int p0 = 0; p0 < nparts; p0 += 32) {
-      const int p = p0 + lane;
-      if (p < nparts) M = fmaxf(M, a.ws_ml[row_of(p) * 2]);
-    }
-    M = warp_max(M);
-    if (M != -INFINITY) {
-#pragma unroll 1
-      for (int p0 = 0; p0 < nparts; p0 += 32) {
-        const int p = p0 + lane;
-        float w = 0.f;
-        if (p < nparts) {
-          const float2 ml = *reinterpret_cast<const float2*>(a.ws_ml + row_of(p) * 2);
-          w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
-          L += w * ml.y;
-        }
-        const int n = min(32, nparts - p0);
-#pragma unroll 1
-        for (int i0 = 0; i0 < n; i0 += 8) {
-          float4 v[8];
+    for (int p0 = 0; p0 < nparts; p0 += 16) {
+      const int n = min(16, nparts - p0);
+      float2 ml = make_float2(-INFINITY, 0.f);
+      if (lane < n) ml = *reinterpret_cast<const float2*>(a.ws_ml + row_of(p0 + lane) * 2);
+      float4 v[16];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (i0 + i < n) {
-              const float* src = a.ws_acc + row_of(p0 + i0 + i) * D + lane * per;
-              if (per == 4) v[i] = *reinterpret_cast<const float4*>(src);
-              else { const float2 t = *reinterpret_cast<const float2*>(src); v[i].x = t.x; v[i].y = t.y; }
-            }
-          }
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const float wi = __shfl_sync(0xffffffffu, w, (i0 + i) & 31);
-            o[0] += wi * v[i].x; o[1] += wi * v[i].y; o[2] += wi * v[i].z; o[3] += wi * v[i].w;
-          }
+      for (int i = 0; i < 16; ++i) {
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n) {
+          const float* src = a.ws_acc + row_of(p0 + i) * D + lane * per;
+          if (per == 4) v[i] = *reinterpret_cast<const float4*>(src);
+          else { const float2 t = *reinterpret_cast<const float2*>(src); v[i].x = t.x; v[i].y = t.y; }
         }
       }
-      L = warp_sum(L);
+      const float Mn = fmaxf(M, warp_max(ml.x));
+      if (Mn == -INFINITY) continue;  // nothing attended yet
+      if (M != -INFINITY && M != Mn) {
+        const float r = exp2f(M - Mn);
+        L *= r;
+        o[0] *= r; o[1] *= r; o[2] *= r; o[3] *= r;
+      }
+      M = Mn;
+      const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+      L += w * ml.y;  // per lane; summed over the warp at the end
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float wi = __shfl_sync(0xffffffffu, w, i);
+        o[0] += wi * v[i].x; o[1] += wi * v[i].y; o[2] += wi * v[i].z; o[3] += wi * v[i].w;
+      }
     }
+    L = warp_sum(L);
   }
   const float scale = L > 0.f ? a.v_scale[hq / a.G] / L : 0.f;
 #pragma unroll
@@ -662,8 +657,8 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
   }
   int st = okc_host::launch_k(attn_decode_kernel<D, HKV>, dim3(a.num_ctas), dim3(C::THREADS), smem, stream, dim3(1), a);
   if (st) return st;
-  return okc_host::launch_k(attn_merge_kernel, dim3(a.B, (a.Hq + 7) / 8), dim3(256), (size_t)(a.B + 1) * sizeof(int),
-                            stream, dim3(1), a, (int)C::TS, (int)C::NSUB, D);
+  return okc_host::launch_k(attn_merge_kernel, dim3(a.B, (a.Hq + 7) / 8), dim3(256), 0, stream, dim3(1), a,
+                            (int)C::TS, (int)C::NSUB, D);
 }
 
 int launch_attn_decode(AttnArgs& a, int D, int Hkv, cudaStream_t stream) {

@@ -127,7 +127,8 @@ size_t okc_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int num_ct
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0) return 0;
   const size_t nsub = Hkv >= 8 ? 1 : 8 / Hkv;
   const size_t rows = (size_t)(num_ctas + B) * nsub * Hq;
-  return 256 + ((rows * 2 * 4 + 255) / 256) * 256 + rows * D * 4;
+  return 256 + ((rows * 2 * 4 + 255) / 256) * 256 + ((rows * D * 4 + 255) / 256) * 256 +
+         (((size_t)B + 1) * 4 + 255) / 256 * 256;
 }
 
 int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const void* v_cache,
@@ -167,6 +168,7 @@ int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const
   a.err = reinterpret_cast<int*>(ws);
   a.ws_ml = reinterpret_cast<float*>(ws + 256);
   a.ws_acc = reinterpret_cast<float*>(ws + 256 + ((rows * 2 * 4 + 255) / 256) * 256);
+  a.ws_prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a.ws_acc) + ((rows * D * 4 + 255) / 256) * 256);
   a.B = B;
   a.Hq = Hq;
   a.G = Hq / Hkv;

@@ -21,6 +21,7 @@ struct AttnArgs {
   int ldo;
   float* ws_ml;   // [slots][NSUB][Hq][2]: running max (log2 units), running sum
   float* ws_acc;  // [slots][NSUB][Hq][D]: unnormalised output
+  int* ws_prefix; // [B + 1]: unit prefix of the sequences (written by the attention kernel for the merge)
   int* err;
   int B, Hq, G, P;
   long long num_pages;
