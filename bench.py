@@ -215,8 +215,8 @@ def run_okc(args):
 
     ev_a0 = torch.cuda.Event(enable_timing=True, external=True)
     ev_a1 = torch.cuda.Event(enable_timing=True, external=True)
-    # stage boundaries inside the graph (external events): norm+QKV, RoPE/append, attention,
-    # O projection, all-reduce + residual
+    # stage boundaries inside the graph (external events): norm, QKV + RoPE/append,
+    # attention, O projection, exchange + residual
     ev_s = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(4)]
     xn_buf = {}
 
@@ -224,10 +224,9 @@ def run_okc(args):
         cfgl, dd = layer.cfg, layer.cfg.head_dim
         ev_s[0].record()
         xn = ops.rmsnorm(x, layer.norm_w, cfgl.eps)
-        qkv = ops.gemm(xn, layer.wqkv)
         ev_s[1].record()
-        q = ops.rope_kv_append(qkv, positions, table, kc, vc, layer.k_scale, layer.v_scale, layer.lq,
-                               layer.lkv, dd, layer.inv_freq)
+        q = ops.gemm_rope_kv_append(xn, layer.wqkv, positions, table, kc, vc, layer.k_scale, layer.v_scale,
+                                    layer.lq, layer.lkv, dd, layer.inv_freq)
         ev_a0.record()
         o = ops.attn_decode(q, kc, vc, table, lens, layer.k_scale, layer.v_scale, layer.sm_scale)
         ev_a1.record()
@@ -290,13 +289,13 @@ def run_okc(args):
 
     # attention and stage durations from the instrumented graph (one replay per sample)
     att_us = []
-    stage_us = {"norm_qkv": [], "rope_append": [], "attention": [], "o_proj": [], "allreduce_residual": []}
+    stage_us = {"norm": [], "qkv_rope_append": [], "attention": [], "o_proj": [], "allreduce_residual": []}
     for _ in range(args.steps):
         graph_i.replay()
         torch.cuda.synchronize()
         att_us.append(ev_a0.elapsed_time(ev_a1) * 1000.0)
-        stage_us["norm_qkv"].append(ev_s[0].elapsed_time(ev_s[1]) * 1000.0)
-        stage_us["rope_append"].append(ev_s[1].elapsed_time(ev_a0) * 1000.0)
+        stage_us["norm"].append(ev_s[0].elapsed_time(ev_s[1]) * 1000.0)
+        stage_us["qkv_rope_append"].append(ev_s[1].elapsed_time(ev_a0) * 1000.0)
         stage_us["attention"].append(ev_a0.elapsed_time(ev_a1) * 1000.0)
         stage_us["o_proj"].append(ev_a1.elapsed_time(ev_s[2]) * 1000.0)
         stage_us["allreduce_residual"].append(ev_s[2].elapsed_time(ev_s[3]) * 1000.0)

@@ -84,6 +84,24 @@ int okc_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, int ldy, in
                      float eps, int unit_offset, okc_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
+ * QKV projection with the RoPE + FP8 KV-append fused into its epilogue (the tcgen05 path,
+ * M <= 256): qkv = x · W^T (fp32 accumulate, rounded to bf16 as the unfused path does), then
+ * exactly okc_rope_kv_append_ex's arithmetic with qk_norm = 0: q (rotated, x q_scale) to
+ * bf16 q_out [M][Hq][D], k (rotated) and v quantised e4m3 into k_cache / v_cache at
+ * slot = page_table[m][pos/P]*P + pos%P, slots_out[m] (may be NULL).  N = (Hq + 2 Hkv) * D,
+ * D % 8 == 0.  The bf16 qkv never goes to memory.  Workspace as okc_gemm_bf16_workspace_bytes.
+ * Replaces the QKV projection + `_qkv_norm_store` pair of muse_decode_layer/decode/
+ * projections.py:75-77 and decode/attention.py:13-37 for the plain (no QK-norm) layer.
+ * ---------------------------------------------------------------------------------- */
+int okc_gemm_bf16_rope_kv_append(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
+                                 const int64_t* positions, const int32_t* page_table, int table_ld,
+                                 int max_pages, const float* inv_freq, const float* k_scale,
+                                 const float* v_scale, void* q_out, void* k_cache, void* v_cache,
+                                 int64_t* slots_out, int Hq, int Hkv, int D, int page_size,
+                                 int64_t num_pages, float q_scale, void* workspace, size_t workspace_bytes,
+                                 okc_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
  * RoPE + FP8 KV-append (one decode token per sequence, q_len = 1).
  * Replaces `_qkv_norm_store` muse_decode_layer/decode/attention.py:13-37, the append of
  * muse_attention_decode/submission.py:283-305 and the cache write of

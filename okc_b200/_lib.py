@@ -43,6 +43,8 @@ SIGNATURES: dict[str, tuple] = {
     "okc_rmsnorm_bf16": (_i, [_p, _i, _p, _p, _i, _i, _i, _f, _i, _p]),
     "okc_rope_kv_append": (_i, [_p, _i, _p, _p, _i, _i, _p, _p, _p, _p, _p, _p, _p,
                                 _i, _i, _i, _i, _i, _i64, _p, _sz, _p]),
+    "okc_gemm_bf16_rope_kv_append": (_i, [_p, _i, _p, _i, _i, _i, _i, _p, _p, _i, _i, _p, _p, _p, _p, _p, _p, _p,
+                                          _i, _i, _i, _i, _i64, _f, _p, _sz, _p]),
     "okc_rope_kv_append_ex": (_i, [_p, _i, _p, _p, _i, _i, _p, _p, _p, _p, _p, _p, _p,
                                    _i, _i, _i, _i, _i, _i64, _f, _i, _f, _p, _sz, _p]),
     "okc_attn_decode_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),

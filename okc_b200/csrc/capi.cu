@@ -121,6 +121,48 @@ int okc_rope_kv_append(const void* qkv, int ldqkv, const int64_t* positions, con
                                1.0f, 0, 0.0f, workspace, workspace_bytes, stream);
 }
 
+int okc_gemm_bf16_rope_kv_append(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
+                                 const int64_t* positions, const int32_t* page_table, int table_ld,
+                                 int max_pages, const float* inv_freq, const float* k_scale,
+                                 const float* v_scale, void* q_out, void* k_cache, void* v_cache,
+                                 int64_t* slots_out, int Hq, int Hkv, int D, int page_size,
+                                 int64_t num_pages, float q_scale, void* workspace, size_t workspace_bytes,
+                                 okc_stream_t stream) {
+  if (!x || !w || !positions || !page_table || !k_scale || !v_scale || !q_out || !k_cache || !v_cache)
+    return OKC_ERR_INVALID;
+  if (M <= 0 || M > 256 || K <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || D % 8 || D > 512 || page_size <= 0 ||
+      num_pages <= 0 || table_ld <= 0 || max_pages <= 0 || N != (Hq + 2 * Hkv) * D)
+    return OKC_ERR_INVALID;
+  if (K % 8 || ldx % 8 || ldw % 8 || ldx < K || ldw < K) return OKC_ERR_INVALID;
+  if (!okc::tc_gemm_supported(M, N, K, ldx, ldw)) return OKC_ERR_INVALID;
+  if (!aligned16(x) || !aligned16(w) || (reinterpret_cast<uintptr_t>(q_out) & 7) ||
+      (reinterpret_cast<uintptr_t>(k_cache) & 3) || (reinterpret_cast<uintptr_t>(v_cache) & 3))
+    return OKC_ERR_ALIGNMENT;
+  if (!workspace || workspace_bytes < okc_gemm_bf16_workspace_bytes(M, N, K)) return OKC_ERR_WORKSPACE;
+  okc::TcRopeArgs r;
+  r.positions = positions;
+  r.page_table = page_table;
+  r.table_ld = table_ld;
+  r.max_pages = max_pages;
+  r.inv_freq = inv_freq;
+  r.k_scale = k_scale;
+  r.v_scale = v_scale;
+  r.q_out = q_out;
+  r.k_cache = k_cache;
+  r.v_cache = v_cache;
+  r.slots_out = slots_out;
+  r.Hq = Hq;
+  r.Hkv = Hkv;
+  r.D = D;
+  r.P = page_size;
+  r.num_pages = num_pages;
+  r.q_scale = q_scale;
+  // y is not written (every output goes through the epilogue); pass the q buffer as a
+  // placeholder with a row stride of N.
+  return okc::launch_tc_gemm(x, ldx, w, ldw, q_out, N, nullptr, M, N, K, 0,
+                             reinterpret_cast<uint8_t*>(workspace) + 256, workspace_bytes - 256, stream, &r);
+}
+
 // ------------------------------------------------------------------------ attention
 size_t okc_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int num_ctas) {
   if (num_ctas <= 0) num_ctas = okc_host::num_sms();

@@ -33,12 +33,34 @@ namespace okc {
 constexpr int TC_BM = 128;  // weight rows per tile (MMA M)
 constexpr int TC_BK = 64;   // K elements per stage (128 bytes: one swizzle atom row)
 
+// Optional epilogue of the QKV projection: interleaved RoPE on the q and k columns, q to
+// bf16 [M][Hq][D], k and v quantised to e4m3 into the paged caches at slot(token) (the work of
+// rope_append_kernel, fused so the bf16 qkv never goes to HBM).  Output column n = head*D + d
+// with heads [0, Hq) = q, [Hq, Hq + Hkv) = k, [Hq + Hkv, Hq + 2 Hkv) = v.
+struct TcRopeEpi {
+  const int64_t* positions;
+  const int32_t* page_table;
+  int table_ld, max_pages;
+  const float* inv_freq;
+  const float* k_scale;
+  const float* v_scale;
+  __nv_bfloat16* q_out;
+  uint8_t* k_cache;
+  uint8_t* v_cache;
+  int64_t* slots_out;
+  int Hq, Hkv, D, P;
+  long long num_pages;
+  float q_scale;
+};
+
 struct TcParams {
   int M, N, K, ldy, out_fp32, tiles;
   void* y;
   const __nv_bfloat16* residual;
   int* err;
   float* part;    // stream-K partial slots [ctas + tiles][BN][128] (workspace)
+  int rope_on;    // 1: every tile goes through tc_reduce_kernel, which applies `rope`
+  TcRopeEpi rope;
 };
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -229,7 +251,7 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
     for (int u = u0; u < u1; ++seg) {
       const int tile = u / nkb, kb_first = u - tile * nkb;
       const int seg_end = min(u1, (tile + 1) * nkb);
-      const bool whole = kb_first == 0 && seg_end == (tile + 1) * nkb;
+      const bool whole = kb_first == 0 && seg_end == (tile + 1) * nkb && !p.rope_on;
       const int buf = seg & 1;
       const bool ok = mbar_wait(&accf[buf], (uint32_t)(seg >> 1) & 1u, p.err) && !*abort_flag;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -278,6 +300,71 @@ __global__ void __launch_bounds__(192) tc_gemm_kernel(const __grid_constant__ CU
   }
 }
 
+// RoPE + FP8 KV-append of 4 consecutive projection outputs (token m, columns n4..n4+3, one
+// head: D % 4 == 0), in the arithmetic of rope_append_kernel (sincosf of pos * inv_freq, RN
+// fp32 rotation, q * q_scale -> bf16, k|v / scale -> e4m3 RN, NaN on overflow).  rope_prep
+// runs before the partial sums are loaded (its page-table reads and sincosf overlap them).
+struct RopeCtx {
+  long long slot;
+  float sn[2], cs[2];
+  int head, d0;
+  bool is_v;
+};
+
+__device__ __forceinline__ RopeCtx rope_prep(const TcRopeEpi& e, int m, int n4, int* err) {
+  RopeCtx c;
+  const long long pos = e.positions[m];
+  const long long lp = pos / e.P;
+  c.slot = -1;
+  if (pos >= 0 && lp < e.max_pages) {
+    const int page = e.page_table[(size_t)m * e.table_ld + lp];
+    if (page >= 0 && page < e.num_pages) c.slot = (long long)page * e.P + pos % e.P;
+  }
+  if (n4 == 0) {  // once per token
+    if (c.slot < 0) atomicOr(err, OKC_DEVERR_PAGE);
+    if (e.slots_out) e.slots_out[m] = c.slot;
+  }
+  c.head = n4 / e.D;
+  c.d0 = n4 - c.head * e.D;
+  c.is_v = c.head >= e.Hq + e.Hkv;
+  c.sn[0] = c.sn[1] = 0.f;
+  c.cs[0] = c.cs[1] = 1.f;
+  if (e.inv_freq && !c.is_v) {
+    const float posf = (float)pos;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) sincosf(__fmul_rn(posf, e.inv_freq[c.d0 / 2 + k]), &c.sn[k], &c.cs[k]);
+  }
+  return c;
+}
+
+__device__ __forceinline__ void rope_apply(const TcRopeEpi& e, const RopeCtx& c, int m, float (&x)[4]) {
+  if (e.inv_freq && !c.is_v) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float y0 = __fsub_rn(__fmul_rn(x[2 * k], c.cs[k]), __fmul_rn(x[2 * k + 1], c.sn[k]));
+      const float y1 = __fadd_rn(__fmul_rn(x[2 * k], c.sn[k]), __fmul_rn(x[2 * k + 1], c.cs[k]));
+      x[2 * k] = y0;
+      x[2 * k + 1] = y1;
+    }
+  }
+  if (c.head < e.Hq) {
+    if (e.q_scale != 1.f) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) x[k] *= e.q_scale;
+    }
+    *reinterpret_cast<uint2*>(e.q_out + ((size_t)m * e.Hq + c.head) * e.D + c.d0) =
+        make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+  } else if (c.slot >= 0) {
+    const int h = c.is_v ? c.head - e.Hq - e.Hkv : c.head - e.Hq;
+    const float sc = c.is_v ? e.v_scale[h] : e.k_scale[h];
+    uint32_t v = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v |= (uint32_t)f_to_e4m3_nosat(__fdiv_rn(x[k], sc)) << (8 * k);
+    uint8_t* cache = c.is_v ? e.v_cache : e.k_cache;
+    *reinterpret_cast<uint32_t*>(cache + ((size_t)c.slot * e.Hkv + h) * e.D + c.d0) = v;
+  }
+}
+
 // Split-tile reduction: y[m, tile*128 + r] = sum over the tile's slots (in slot order) of the
 // partials (+ residual).  Block (x, tile) covers tokens [8x, 8x + 8) x 128 rows; thread t owns 4
 // consecutive rows of one token (float4 loads, all slots' loads issued before the sum).
@@ -287,7 +374,7 @@ __global__ void __launch_bounds__(256) tc_reduce_kernel(TcParams p, int U, int C
   pdl_wait();  // the GEMM grid is complete and its partials visible
   const int tile = blockIdx.y;
   const int c_first = sk_owner(U, C, tile * nkb), c_last = sk_owner(U, C, (tile + 1) * nkb - 1);
-  if (c_first == c_last) return;  // one CTA covered the tile: written directly
+  if (c_first == c_last && !p.rope_on) return;  // one CTA covered the tile: written directly
   const int m = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (m >= p.M) return;
   const int r4 = 4 * (threadIdx.x & 31);
@@ -295,6 +382,8 @@ __global__ void __launch_bounds__(256) tc_reduce_kernel(TcParams p, int U, int C
   const int nslot = c_last - c_first + 1;
   const float* base = p.part + (size_t)(c_first + tile) * BN * TC_BM + (size_t)m * TC_BM + r4;
   const size_t slot_stride = (size_t)BN * TC_BM;
+  RopeCtx rc;
+  if (p.rope_on && n4 < p.N) rc = rope_prep(p.rope, m, n4, p.err);
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
   for (int q0 = 0; q0 < nslot; q0 += 8) {
@@ -307,6 +396,13 @@ __global__ void __launch_bounds__(256) tc_reduce_kernel(TcParams p, int U, int C
     for (int i = 0; i < 8; ++i) { acc.x += t4[i].x; acc.y += t4[i].y; acc.z += t4[i].z; acc.w += t4[i].w; }
   }
   float r[4] = {acc.x, acc.y, acc.z, acc.w};
+  if (p.rope_on) {
+    // the unfused path rounds the projection to bf16 before RoPE: do the same
+#pragma unroll
+    for (int j = 0; j < 4; ++j) r[j] = __bfloat162float(__float2bfloat16_rn(r[j]));
+    if (n4 < p.N) rope_apply(p.rope, rc, m, r);
+    return;
+  }
   const size_t o = (size_t)m * p.ldy + n4;
   if (n4 + 3 < p.N && (o & 3) == 0) {
     if (p.residual) {
@@ -440,15 +536,36 @@ static int launch_tc_t(const void* x, int ldx, const void* w, int ldw, TcParams&
   if (st) return st;
   // Reduce of the split tiles, as a programmatic dependent launch: its blocks may be scheduled
   // while the GEMM drains and wait in griddepcontrol.wait until the GEMM grid has completed.
-  if ((long long)pl.tiles * pl.nkb <= pl.ctas && pl.nkb == 1) return OKC_OK;  // no split tile
+  if ((long long)pl.tiles * pl.nkb <= pl.ctas && pl.nkb == 1 && !p.rope_on) return OKC_OK;  // no split tile
   const int U = pl.tiles * pl.nkb;
   return okc_host::launch_k(tc_reduce_kernel<BN>, dim3((unsigned)((min(p.M, BN) + 7) / 8), (unsigned)pl.tiles),
                             dim3(256), 0, stream, dim3(1), p, U, pl.ctas, pl.nkb);
 }
 
 int launch_tc_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy, const void* residual, int M,
-                   int N, int K, int out_fp32, void* ws, size_t ws_bytes, cudaStream_t stream) {
-  TcParams p;
+                   int N, int K, int out_fp32, void* ws, size_t ws_bytes, cudaStream_t stream,
+                   const TcRopeArgs* rope) {
+  TcParams p = {};
+  p.rope_on = rope != nullptr;
+  if (rope) {
+    p.rope.positions = rope->positions;
+    p.rope.page_table = rope->page_table;
+    p.rope.table_ld = rope->table_ld;
+    p.rope.max_pages = rope->max_pages;
+    p.rope.inv_freq = rope->inv_freq;
+    p.rope.k_scale = rope->k_scale;
+    p.rope.v_scale = rope->v_scale;
+    p.rope.q_out = reinterpret_cast<__nv_bfloat16*>(rope->q_out);
+    p.rope.k_cache = reinterpret_cast<uint8_t*>(rope->k_cache);
+    p.rope.v_cache = reinterpret_cast<uint8_t*>(rope->v_cache);
+    p.rope.slots_out = rope->slots_out;
+    p.rope.Hq = rope->Hq;
+    p.rope.Hkv = rope->Hkv;
+    p.rope.D = rope->D;
+    p.rope.P = rope->P;
+    p.rope.num_pages = rope->num_pages;
+    p.rope.q_scale = rope->q_scale;
+  }
   p.M = M;
   p.N = N;
   p.K = K;

@@ -38,9 +38,25 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 int launch_skinny_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
                        const void* residual, int M, int N, int K, int out_fp32, int splits,
                        cudaStream_t stream);
+// RoPE + FP8 KV-append fused into the QKV projection's epilogue (tcgen05 path).
+struct TcRopeArgs {
+  const int64_t* positions;
+  const int32_t* page_table;
+  int table_ld, max_pages;
+  const float* inv_freq;
+  const float* k_scale;
+  const float* v_scale;
+  void* q_out;
+  void* k_cache;
+  void* v_cache;
+  int64_t* slots_out;
+  int Hq, Hkv, D, P;
+  long long num_pages;
+  float q_scale;
+};
 int launch_tc_gemm(const void* x, int ldx, const void* w, int ldw, void* y, int ldy,
                    const void* residual, int M, int N, int K, int out_fp32, void* ws, size_t ws_bytes,
-                   cudaStream_t stream);
+                   cudaStream_t stream, const TcRopeArgs* rope = nullptr);
 size_t tc_gemm_ws_bytes(int M, int N, int K);
 bool tc_gemm_supported(int M, int N, int K, int ldx, int ldw);
 int launch_rmsnorm(const void* x, int ldx, const void* w, void* y, int ldy, int T, int H, float eps,

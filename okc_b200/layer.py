@@ -2,6 +2,7 @@
 
     x -> RMSNorm -> QKV projection -> RoPE + FP8 KV-append -> paged attention
       -> O projection (+ residual) -> out
+(above 32 tokens the RoPE + KV-append run in the QKV projection's epilogue)
 
 Every stage is an okc_b200 kernel; the step is captured in one CUDA graph by the caller
 (bench.py) so launch latency does not count.  Tensor parallel over `world` ranks: rank r
@@ -71,7 +72,8 @@ class DecodeLayer:
         """Our kernel launches in one step (for the bench's gpu_launches)."""
         passes = 1 if tokens <= 256 else (tokens + 255) // 256  # tcgen05 GEMM: 256 tokens a launch
         per_gemm = 2 * passes if tokens > 32 else 1  # tcgen05 stream-K + split-tile reduce
-        return 1 + per_gemm + 1 + 2 + per_gemm + (1 if self.world > 1 else 0)
+        rope = 0 if tokens > 32 else 1  # fused into the QKV reduce on the tcgen05 path
+        return 1 + per_gemm + rope + 2 + per_gemm + (1 if self.world > 1 else 0)
 
     def step(self, x, positions, page_table, k_cache, v_cache, lens=None, out=None):
         """x bf16 [B, H]; positions int64 [B] (= tokens already cached); caches of this rank's
@@ -79,9 +81,13 @@ class DecodeLayer:
         cfg, d = self.cfg, self.cfg.head_dim
         B = x.shape[0]
         xn = ops.rmsnorm(x, self.norm_w, cfg.eps)
-        qkv = ops.gemm(xn, self.wqkv)
-        q = ops.rope_kv_append(qkv, positions, page_table, k_cache, v_cache, self.k_scale, self.v_scale,
-                               self.lq, self.lkv, d, self.inv_freq)
+        if B > 32:  # tcgen05 projection with RoPE + KV-append in its epilogue
+            q = ops.gemm_rope_kv_append(xn, self.wqkv, positions, page_table, k_cache, v_cache, self.k_scale,
+                                        self.v_scale, self.lq, self.lkv, d, self.inv_freq)
+        else:
+            qkv = ops.gemm(xn, self.wqkv)
+            q = ops.rope_kv_append(qkv, positions, page_table, k_cache, v_cache, self.k_scale, self.v_scale,
+                                   self.lq, self.lkv, d, self.inv_freq)
         if lens is None:
             lens = (positions + 1).to(torch.int32)
         o = ops.attn_decode(q, k_cache, v_cache, page_table, lens, self.k_scale, self.v_scale, self.sm_scale)

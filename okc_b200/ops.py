@@ -141,6 +141,34 @@ def rope_kv_append(qkv: torch.Tensor, positions: torch.Tensor, page_table: torch
     return q_out
 
 
+def gemm_rope_kv_append(x: torch.Tensor, wqkv: torch.Tensor, positions: torch.Tensor, page_table: torch.Tensor,
+                        k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: torch.Tensor,
+                        v_scale: torch.Tensor, Hq: int, Hkv: int, D: int, inv_freq: torch.Tensor | None,
+                        q_out: torch.Tensor | None = None, slots_out: torch.Tensor | None = None,
+                        q_scale: float = 1.0) -> torch.Tensor:
+    """qkv = x @ wqkv^T with RoPE + FP8 KV-append fused into the tcgen05 GEMM's epilogue
+    (okc_gemm_bf16_rope_kv_append): same results as gemm() followed by rope_kv_append()
+    without QK-norm.  Returns q_out bf16 [M, Hq, D]."""
+    dev = _dev_index(x)
+    _need(x, torch.bfloat16, "x")
+    _need(wqkv, torch.bfloat16, "wqkv")
+    M, K = x.shape
+    N = wqkv.shape[0]
+    if q_out is None:
+        q_out = torch.empty((M, Hq, D), dtype=torch.bfloat16, device=x.device)
+    lib = _lib.load()
+    ws = workspace(dev, "gemm", lib.okc_gemm_bf16_workspace_bytes(M, N, K))
+    P = k_cache.shape[1]
+    st = lib.okc_gemm_bf16_rope_kv_append(x.data_ptr(), x.stride(0), wqkv.data_ptr(), wqkv.stride(0), M, N, K,
+                                          positions.data_ptr(), page_table.data_ptr(), page_table.stride(0),
+                                          page_table.shape[1], _ptr(inv_freq), k_scale.data_ptr(),
+                                          v_scale.data_ptr(), q_out.data_ptr(), k_cache.data_ptr(),
+                                          v_cache.data_ptr(), _ptr(slots_out), Hq, Hkv, D, P, k_cache.shape[0],
+                                          float(q_scale), ws.data_ptr(), ws.numel(), _stream(dev))
+    check(st, "okc_gemm_bf16_rope_kv_append")
+    return q_out
+
+
 def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                 page_table: torch.Tensor, seq_lens: torch.Tensor, k_scale: torch.Tensor,
                 v_scale: torch.Tensor, sm_scale: float, out: torch.Tensor | None = None,
