@@ -421,19 +421,21 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
           acc[i][0] *= alpha; acc[i][1] *= alpha; acc[i][2] *= alpha; acc[i][3] *= alpha;
         }
       }
-      // ---- P as two e4m3 terms: p*256 ~= p1 + p2/16 ----
-      uint32_t pa[4] = {0, 0, 0, 0};  // a0 (p1, tokens 4c..), a1 (p2), a2 (p1, 16+4c..), a3 (p2)
+      // ---- P as two e4m3 terms: p*256 ~= p1 + p2/16, formed in f16x2 arithmetic (p*256 is in
+      // [0, 256]: its f16 rounding, 2^-11, is far below the ~2^-8 of the two-term form; the
+      // residual x - p1 is exact in f16) ----
+      uint16_t t1[4], t2[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float x0 = p[j][0] * 256.f, x1 = p[j][1] * 256.f;
-        const uint16_t h1 = f2_to_e4m3x2_sat(x0, x1);
-        const __half2 bk = __half2(__nv_cvt_fp8x2_to_halfraw2(h1, __NV_E4M3));
-        const uint16_t h2 = f2_to_e4m3x2_sat((x0 - __low2float(bk)) * 16.f, (x1 - __high2float(bk)) * 16.f);
-        const int reg = (j >> 1) * 2;       // j=0,1 -> a0/a1 ; j=2,3 -> a2/a3
-        const int sh = 16 * (j & 1);
-        pa[reg] |= (uint32_t)h1 << sh;
-        pa[reg + 1] |= (uint32_t)h2 << sh;
+        const __half2 xh = __floats2half2_rn(p[j][0] * 256.f, p[j][1] * 256.f);
+        t1[j] = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(xh), __NV_SATFINITE, __NV_E4M3);
+        const __half2 bk = __half2(__nv_cvt_fp8x2_to_halfraw2(t1[j], __NV_E4M3));
+        const __half2 r = __hmul2(__hsub2(xh, bk), __float2half2_rn(16.f));
+        t2[j] = __nv_cvt_halfraw2_to_fp8x2(__half2_raw(r), __NV_SATFINITE, __NV_E4M3);
       }
+      // a0 (p1, tokens 4c..), a1 (p2), a2 (p1, 16+4c..), a3 (p2): j = 0,1 -> a0/a1, j = 2,3 -> a2/a3
+      const uint32_t pa[4] = {(uint32_t)t1[0] | ((uint32_t)t1[1] << 16), (uint32_t)t2[0] | ((uint32_t)t2[1] << 16),
+                              (uint32_t)t1[2] | ((uint32_t)t1[3] << 16), (uint32_t)t2[2] | ((uint32_t)t2[3] << 16)};
       // ---- O += P V: V rows (4c+u) and (16+4c+u), columns [RL*g, RL*g + RL) ----
       const bool tail = valid < 32;
       uint32_t mlo = 0xffffffffu, mhi = 0xffffffffu;
