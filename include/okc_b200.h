@@ -226,6 +226,14 @@ int okc_moe_experts_w4a16(const void* x, const int32_t* ids, const float* weight
                           const void* w2, const void* w2_sf, const float* w2_gs,
                           void* out, int T, int topk, int H, int I, int expert_lo, int E_local,
                           void* workspace, size_t workspace_bytes, okc_stream_t stream);
+/* Same, with out_fp32 != 0: out is fp32 [T,H] and holds this rank's unrounded share of the
+ * sum (expert parallelism: the ranks' shares are summed by okc_tp_allreduce_residual). */
+int okc_moe_experts_w4a16_ex(const void* x, const int32_t* ids, const float* weights,
+                             const int32_t* counts, const int32_t* offsets, const int32_t* pairs,
+                             const void* w13, const void* w13_sf, const float* w13_gs,
+                             const void* w2, const void* w2_sf, const float* w2_gs,
+                             void* out, int T, int topk, int H, int I, int expert_lo, int E_local,
+                             int out_fp32, void* workspace, size_t workspace_bytes, okc_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
  * Tensor-parallel exchange over NVLink peer memory (multi-GPU layer step).  No reference
@@ -238,7 +246,8 @@ int okc_moe_experts_w4a16(const void* x, const int32_t* ids, const float* weight
  * 64-byte cudaIpcMemHandle_t of such a buffer; okc_ipc_open maps a peer's handle (peer
  * access enabled lazily); okc_ipc_close unmaps it.
  *
- * okc_tp_allreduce_residual: out_r = bf16(residual + sum_q parts[q]) on every rank r.
+ * okc_tp_allreduce_residual: out_r = bf16(residual + sum_q parts[q]) on every rank r
+ * (residual may be NULL: out_r = bf16(sum_q parts[q])).
  * parts[q] (fp32 [n]), outs[q] (bf16 [n]) and flags[q] (int [16], zero-filled) are HOST
  * arrays of `world` device pointers: this rank's own buffers at index `rank`, the peers'
  * mapped buffers elsewhere.  state: this rank's int [2] (zero-filled), private to one

@@ -102,13 +102,15 @@ class TPComm:
             self._ws = ops.workspace(self.device, "tp", 256)
         dist.barrier(group=group)
 
-    def allreduce_residual(self, residual: torch.Tensor) -> torch.Tensor:
-        """out = bf16(residual + sum over ranks of `self.partial`) on every rank; returns
-        `self.out` (valid until the next call)."""
-        if residual.dtype != torch.bfloat16 or residual.shape != (self.T, self.H) or not residual.is_contiguous():
+    def allreduce_residual(self, residual: torch.Tensor | None) -> torch.Tensor:
+        """out = bf16(residual + sum over ranks of `self.partial`) on every rank (residual may
+        be None); returns `self.out` (valid until the next call)."""
+        if residual is not None and (residual.dtype != torch.bfloat16 or residual.shape != (self.T, self.H)
+                                     or not residual.is_contiguous()):
             raise ValueError("residual must be a contiguous bf16 [T, H] tensor")
         lib = _lib.load()
-        st = lib.okc_tp_allreduce_residual(self._parts_arr, self._outs_arr, self._flags_arr, residual.data_ptr(),
+        st = lib.okc_tp_allreduce_residual(self._parts_arr, self._outs_arr, self._flags_arr,
+                                           None if residual is None else residual.data_ptr(),
                                            self.state.data_ptr(), self.rank, self.world, self.T * self.H,
                                            self._ws.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
         _lib.check(st, "okc_tp_allreduce_residual")
@@ -123,3 +125,47 @@ class TPComm:
         self._opened = []
         for b in (self._part, self._out, self._flags):
             b.free()
+
+
+class ExpertParallelMoE:
+    """Expert-parallel W4A16 MoE over the ranks of `group`.
+
+    Rank r holds experts [expert_lo, expert_lo + E_local) of the bank (its slices of w13/w2 and
+    their scales).  Routing is computed on every rank (bit-exact, so the ranks agree on every
+    id); each rank runs its local experts for the pairs routed to them and leaves its fp32
+    share of the weighted sum in the exchange buffer, and `okc_tp_allreduce_residual` sums the
+    shares over NVLink (plus an optional residual) into the replicated bf16 output.  With the
+    tokens replicated on every rank (tensor-parallel attention before the MoE) this is the
+    all-to-all dispatch + combine with the dispatch already in place."""
+
+    def __init__(self, router: torch.Tensor, w13, w13_sf, w13_gs, w2, w2_sf, w2_gs, expert_lo: int,
+                 topk: int, group=None, renormalize: bool = True):
+        self.router = router
+        self.w13, self.w13_sf, self.w13_gs = w13, w13_sf, w13_gs
+        self.w2, self.w2_sf, self.w2_gs = w2, w2_sf, w2_gs
+        self.expert_lo, self.E_local = expert_lo, w13.shape[0]
+        self.topk, self.group, self.renormalize = topk, group, renormalize
+        self._comms: dict[int, TPComm] = {}
+
+    def comm_for(self, tokens: int) -> TPComm:
+        """The exchange group for `tokens` rows (created on first use: every rank together,
+        outside graph capture)."""
+        c = self._comms.get(tokens)
+        if c is None:
+            c = TPComm(tokens, self.w2.shape[1], group=self.group)
+            self._comms[tokens] = c
+        return c
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        """bf16 [T, H] = (residual +) sum over the top-k experts of weight * expert(x)."""
+        ids, wts = ops.moe_route(x, self.router, self.topk, self.renormalize)
+        perm = ops.moe_permute(ids, self.expert_lo, self.E_local)
+        comm = self.comm_for(x.shape[0])
+        ops.moe_experts(x, ids, wts, perm, self.w13, self.w13_sf, self.w13_gs, self.w2, self.w2_sf, self.w2_gs,
+                        self.expert_lo, out=comm.partial, out_fp32=True)
+        return comm.allreduce_residual(residual)
+
+    def close(self):
+        for c in self._comms.values():
+            c.close()
+        self._comms.clear()

@@ -265,6 +265,16 @@ int okc_moe_experts_w4a16(const void* x, const int32_t* ids, const float* weight
                           const void* w13_sf, const float* w13_gs, const void* w2, const void* w2_sf,
                           const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
                           int E_local, void* workspace, size_t workspace_bytes, okc_stream_t stream) {
+  return okc_moe_experts_w4a16_ex(x, ids, weights, counts, offsets, pairs, w13, w13_sf, w13_gs, w2, w2_sf, w2_gs,
+                                  out, T, topk, H, I, expert_lo, E_local, 0, workspace, workspace_bytes, stream);
+}
+
+int okc_moe_experts_w4a16_ex(const void* x, const int32_t* ids, const float* weights, const int32_t* counts,
+                             const int32_t* offsets, const int32_t* pairs, const void* w13,
+                             const void* w13_sf, const float* w13_gs, const void* w2, const void* w2_sf,
+                             const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
+                             int E_local, int out_fp32, void* workspace, size_t workspace_bytes,
+                             okc_stream_t stream) {
   if (!x || !ids || !weights || !counts || !offsets || !pairs || !w13 || !w13_sf || !w13_gs || !w2 ||
       !w2_sf || !w2_gs || !out)
     return OKC_ERR_INVALID;
@@ -272,7 +282,7 @@ int okc_moe_experts_w4a16(const void* x, const int32_t* ids, const float* weight
   if (!aligned16(x) || !aligned16(w13) || !aligned16(w2) || !aligned16(out)) return OKC_ERR_ALIGNMENT;
   if (!workspace || workspace_bytes < okc::moe_experts_ws_bytes(T, topk, H, I)) return OKC_ERR_WORKSPACE;
   return okc::launch_moe_experts(x, ids, weights, counts, offsets, pairs, w13, w13_sf, w13_gs, w2, w2_sf,
-                                 w2_gs, out, T, topk, H, I, expert_lo, E_local, workspace, stream);
+                                 w2_gs, out, T, topk, H, I, expert_lo, E_local, workspace, stream, out_fp32);
 }
 
 }  // extern "C"

@@ -78,6 +78,6 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
                        const int32_t* offsets, const int32_t* pairs, const void* w13,
                        const void* w13_sf, const float* w13_gs, const void* w2, const void* w2_sf,
                        const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
-                       int E, void* ws, cudaStream_t stream);
+                       int E, void* ws, cudaStream_t stream, int out_fp32 = 0);
 
 }  // namespace okc

@@ -1008,8 +1008,8 @@ __global__ void __launch_bounds__(256) to_f16_kernel(const __nv_bfloat16* __rest
 __global__ void __launch_bounds__(64) combine_kernel(const __nv_bfloat16* __restrict__ y,
                                                      const int32_t* __restrict__ ids,
                                                      const float* __restrict__ wts,
-                                                     __nv_bfloat16* __restrict__ out, int topk, int H,
-                                                     int expert_lo, int E) {
+                                                     void* __restrict__ out, int topk, int H,
+                                                     int expert_lo, int E, int out_fp32) {
   // grid (T, H / 512): 64 threads x 8 elements (one 16-byte load per slot)
   const int t = blockIdx.x;
   const int d = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
@@ -1027,10 +1027,16 @@ __global__ void __launch_bounds__(64) combine_kernel(const __nv_bfloat16* __rest
       a[2 * k + 1] = fmaf(wv, bf16_hi(u[k]), a[2 * k + 1]);
     }
   }
+  if (out_fp32) {  // this rank's share of an expert-parallel sum, reduced across ranks later
+    float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)t * H + d);
+    o4[0] = make_float4(a[0], a[1], a[2], a[3]);
+    o4[1] = make_float4(a[4], a[5], a[6], a[7]);
+    return;
+  }
   uint4 o;
   o.x = pack_bf16x2(a[0], a[1]); o.y = pack_bf16x2(a[2], a[3]);
   o.z = pack_bf16x2(a[4], a[5]); o.w = pack_bf16x2(a[6], a[7]);
-  *reinterpret_cast<uint4*>(out + (size_t)t * H + d) = o;
+  *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)t * H + d) = o;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1115,7 +1121,7 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
                        const int32_t* offsets, const int32_t* pairs, const void* w13,
                        const void* w13_sf, const float* w13_gs, const void* w2, const void* w2_sf,
                        const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
-                       int E, void* ws, cudaStream_t stream) {
+                       int E, void* ws, cudaStream_t stream, int out_fp32) {
   uint8_t* base = reinterpret_cast<uint8_t*>(ws) + 256;
   __half* xh = reinterpret_cast<__half*>(base);
   base += ((size_t)T * H * 2 + 255) / 256 * 256;
@@ -1137,8 +1143,8 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
     st = launch_moe_rows<false>(T, w2, w2_sf, E, inter, counts, offsets, pairs, w2_gs, nullptr, y, topk, I, H, I,
                                 err, stream);
     if (st) return st;
-    combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, reinterpret_cast<__nv_bfloat16*>(out),
-                                                                 topk, H, expert_lo, E);
+    combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, out, topk, H, expert_lo, E,
+                                                                 out_fp32);
     return okc_host::launch_status();
   }
   // Measured on B200: the pipelined kernel wins up to 64 tokens, the per-expert kernel above.
@@ -1162,8 +1168,7 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
                               I, E, sp2, expert_lo, stream);
     if (st) return st;
   }
-  combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, reinterpret_cast<__nv_bfloat16*>(out),
-                                                               topk, H, expert_lo, E);
+  combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, out, topk, H, expert_lo, E, out_fp32);
   return okc_host::launch_status();
 }
 

@@ -104,8 +104,10 @@ __global__ void __launch_bounds__(256) tp_allreduce_kernel(TpArgs a) {
 #pragma unroll
       for (int q = 0; q < kTpMaxRanks; ++q)
         if (q < a.world) { s0 += v[q].x; s1 += v[q].y; s2 += v[q].z; s3 += v[q].w; }
-      const uint2 rv = reinterpret_cast<const uint2*>(a.residual)[i];
-      s0 += bf16_lo(rv.x); s1 += bf16_hi(rv.x); s2 += bf16_lo(rv.y); s3 += bf16_hi(rv.y);
+      if (a.residual) {
+        const uint2 rv = reinterpret_cast<const uint2*>(a.residual)[i];
+        s0 += bf16_lo(rv.x); s1 += bf16_hi(rv.x); s2 += bf16_lo(rv.y); s3 += bf16_hi(rv.y);
+      }
       const uint2 o = make_uint2(pack_bf16x2(s0, s1), pack_bf16x2(s2, s3));
 #pragma unroll
       for (int q = 0; q < kTpMaxRanks; ++q)
@@ -178,7 +180,7 @@ extern "C" int okc_tp_allreduce_residual(const float* const* parts, void* const*
                                          const void* residual, int* state, int rank, int world,
                                          long long n, void* workspace, okc_stream_t stream) {
   if (world < 2 || world > okc::kTpMaxRanks || rank < 0 || rank >= world || n <= 0 || (n & 3) ||
-      !parts || !outs || !flags || !residual || !state || !workspace)
+      !parts || !outs || !flags || !state || !workspace)
     return OKC_ERR_INVALID;
   okc::TpArgs a = {};
   for (int q = 0; q < world; ++q) {

@@ -242,7 +242,9 @@ def moe_permute(ids: torch.Tensor, expert_lo: int, E_local: int, bm: int = 8) ->
 def moe_experts(x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, perm: dict,
                 w13: torch.Tensor, w13_sf: torch.Tensor, w13_gs: torch.Tensor,
                 w2: torch.Tensor, w2_sf: torch.Tensor, w2_gs: torch.Tensor, expert_lo: int,
-                out: torch.Tensor | None = None) -> torch.Tensor:
+                out: torch.Tensor | None = None, out_fp32: bool = False) -> torch.Tensor:
+    """Routing-weighted sum of the local experts' SwiGLU MLPs ([T, H]; bf16, or with out_fp32
+    the unrounded fp32 share of an expert-parallel sum)."""
     dev = _dev_index(x)
     _need(x, torch.bfloat16, "x")
     T, H = x.shape
@@ -250,14 +252,14 @@ def moe_experts(x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, perm: dic
     E_local, two_i, _ = w13.shape
     I = two_i // 2
     if out is None:
-        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+        out = torch.empty((T, H), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=x.device)
     lib = _lib.load()
     ws = workspace(dev, "moe", lib.okc_moe_experts_workspace_bytes(T, topk, H, I))
-    st = lib.okc_moe_experts_w4a16(x.data_ptr(), ids.data_ptr(), wts.data_ptr(), perm["counts"].data_ptr(),
-                                   perm["offsets"].data_ptr(), perm["pairs"].data_ptr(), w13.data_ptr(),
-                                   w13_sf.data_ptr(), w13_gs.data_ptr(), w2.data_ptr(), w2_sf.data_ptr(),
-                                   w2_gs.data_ptr(), out.data_ptr(), T, topk, H, I, expert_lo, E_local,
-                                   ws.data_ptr(), ws.numel(), _stream(dev))
+    st = lib.okc_moe_experts_w4a16_ex(x.data_ptr(), ids.data_ptr(), wts.data_ptr(), perm["counts"].data_ptr(),
+                                      perm["offsets"].data_ptr(), perm["pairs"].data_ptr(), w13.data_ptr(),
+                                      w13_sf.data_ptr(), w13_gs.data_ptr(), w2.data_ptr(), w2_sf.data_ptr(),
+                                      w2_gs.data_ptr(), out.data_ptr(), T, topk, H, I, expert_lo, E_local,
+                                      int(out_fp32), ws.data_ptr(), ws.numel(), _stream(dev))
     check(st, "okc_moe_experts_w4a16")
     return out
 

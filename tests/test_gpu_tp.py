@@ -1,7 +1,8 @@
 """Tensor-parallel exchange over NVLink peer memory (okc_tp_allreduce_residual) on 2 GPUs:
 out = bf16(x + sum_r partial_r) on every rank, bit-exact against the same fp32 sums taken in
 rank order on the host side; repeated calls (the device-side epoch) and a CUDA-graph replay.
-Skipped when fewer than 2 GPUs are visible."""
+Expert-parallel MoE (okc_b200.comm.ExpertParallelMoE, half of the experts per rank) against the
+single-GPU MoE over the whole bank.  Skipped when fewer than 2 GPUs are visible."""
 
 import os
 import socket
@@ -95,3 +96,59 @@ def test_tp_allreduce_residual_two_ranks():
     for rank, errs, derr in res:
         assert derr == 0, f"rank {rank}: device error {derr}"
         assert all(e == 0 for e in errs), f"rank {rank}: mismatching elements per call {errs}"
+
+
+def _ep_worker(rank, world, port, T, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from okc_b200 import ops, synth
+        from okc_b200.comm import ExpertParallelMoE
+        m = synth.moe_case(T=T, device="cuda", seed=3)  # identical on every rank
+        E = m["w13"].shape[0]
+        el = E // world
+        sl = slice(rank * el, (rank + 1) * el)
+        ep = ExpertParallelMoE(m["router"], m["w13"][sl].contiguous(), m["w13_sf"][sl].contiguous(),
+                               m["w13_gs"][sl].contiguous(), m["w2"][sl].contiguous(), m["w2_sf"][sl].contiguous(),
+                               m["w2_gs"][sl].contiguous(), rank * el, 8)
+        got = ep.forward(m["x"]).clone()
+        ids, wts = ops.moe_route(m["x"], m["router"], 8)
+        perm = ops.moe_permute(ids, 0, E)
+        full = ops.moe_experts(m["x"], ids, wts, perm, m["w13"], m["w13_sf"], m["w13_gs"], m["w2"], m["w2_sf"],
+                               m["w2_gs"], 0)
+        torch.cuda.synchronize()
+        d = (got.float() - full.float())
+        rel = float(d.norm() / full.float().norm())
+        mx = float(d.abs().max())
+        derr = ops.read_device_error("tp", rank)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ep.close()
+        q.put((rank, rel, mx, derr))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("T", [8, 64])
+def test_expert_parallel_moe_two_ranks(T):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, 2, port, T, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, rel, mx, derr in res:
+        assert derr == 0, f"rank {rank}: device error {derr}"
+        # the shares are summed over ranks instead of in one slot loop: bf16 outputs may move
+        # by one rounding step
+        assert rel < 2e-3 and mx < 5e-2, f"rank {rank}: rel-L2 {rel:.2e}, max abs {mx:.2e}"
