@@ -848,9 +848,14 @@ __global__ void __launch_bounds__(288, 1) moe_rows_kernel(
       if (i < n_e) xr = GATED ? pairs[off + i] / topk : off + i;
       xrow[t] = xin + (size_t)xr * K + 32 * c;
     }
-    float acc[MTMAX][4];
+    // NACC independent accumulators per token tile (k16 step s feeds acc[t][s % NACC]) so that
+    // consecutive MMAs do not wait on each other; they are summed in a fixed order at the end.
+    constexpr int NACC = MTMAX <= 2 ? 4 : 2;
+    float acc[MTMAX][NACC][4];
 #pragma unroll
-    for (int t = 0; t < MTMAX; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+    for (int t = 0; t < MTMAX; ++t)
+#pragma unroll
+      for (int q = 0; q < NACC; ++q) acc[t][q][0] = acc[t][q][1] = acc[t][q][2] = acc[t][q][3] = 0.f;
     bool ok = true;
     for (int kc = 0; kc < nkc; ++kc) {
       ok = ok && !*abort_flag && mbar_wait(&full[stage], phase, err);
@@ -908,7 +913,7 @@ __global__ void __launch_bounds__(288, 1) moe_rows_kernel(
               for (int s8 = 0; s8 < 8; ++s8) {
                 const uint4 v = xt[s8 >> 1];
                 const uint32_t b0 = (s8 & 1) ? v.z : v.x, b1 = (s8 & 1) ? v.w : v.y;
-                mma_f16_16816(acc[t], a[s8][0], a[s8][1], a[s8][2], a[s8][3], b0, b1);
+                mma_f16_16816(acc[t][s8 % NACC], a[s8][0], a[s8][1], a[s8][2], a[s8][3], b0, b1);
               }
               if (t + 2 < ntile) load_x(xq[t & 1], t + 2);
             }
@@ -928,19 +933,23 @@ __global__ void __launch_bounds__(288, 1) moe_rows_kernel(
     for (int t = 0; t < MTMAX; ++t) {
       if (t >= ntile) break;
 #pragma unroll
+      for (int q = 1; q < NACC; ++q)
+#pragma unroll
+        for (int z = 0; z < 4; ++z) acc[t][0][z] += acc[t][q][z];
+#pragma unroll
       for (int e2 = 0; e2 < 2; ++e2) {
         const int i = 8 * t + 2 * c + e2;
         if (i >= n_e) continue;
         if (GATED) {
-          const float hg = __bfloat162float(__float2bfloat16_rn(acc[t][e2] * gsc));
-          const float hu = __bfloat162float(__float2bfloat16_rn(acc[t][2 + e2] * gsc));
+          const float hg = __bfloat162float(__float2bfloat16_rn(acc[t][0][e2] * gsc));
+          const float hu = __bfloat162float(__float2bfloat16_rn(acc[t][0][2 + e2] * gsc));
           const float act_v = hg / (1.f + expf(-hg)) * hu;
           inter_out[(size_t)(off + i) * I + rb * C::ROWS + 8 * warp + g] =
               __float2half_rn(__bfloat162float(__float2bfloat16_rn(act_v)));
         } else {
           __nv_bfloat16* yr = y_out + (size_t)pairs[off + i] * NR + rb * C::ROWS + 16 * warp + g;
-          yr[0] = __float2bfloat16_rn(acc[t][e2] * gsc);
-          yr[8] = __float2bfloat16_rn(acc[t][2 + e2] * gsc);
+          yr[0] = __float2bfloat16_rn(acc[t][0][e2] * gsc);
+          yr[8] = __float2bfloat16_rn(acc[t][0][2 + e2] * gsc);
         }
       }
     }
