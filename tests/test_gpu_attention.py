@@ -57,6 +57,24 @@ def test_decode_shapes(ops, D, Hkv, G, page):
     assert ops.read_device_error("attn") == 0
 
 
+def test_bad_page_id_is_flagged_not_faulted(ops):
+    """A page-table entry outside [0, num_pages) is skipped by the copy engine and reported in
+    the workspace error word; the sequences whose pages are valid stay correct."""
+    lens = [40, 300, 17]
+    page, Hkv, G, D = 16, 8, 8, 128
+    pool = sum(math.ceil(n / page) for n in lens) + 5
+    q, kc, vc, table, sl, ks, vs = _case(len(lens), Hkv * G, Hkv, D, lens, page, pool, seed=11)
+    ops.read_device_error("attn")  # clear
+    bad = table.clone()
+    bad[1, 3] = pool + 7  # sequence 1, tokens 48..63
+    out = ops.attn_decode(q, kc, vc, bad, sl, ks, vs, 1 / math.sqrt(D))
+    err = ops.read_device_error("attn")
+    assert err & 2, f"expected OKC_DEVERR_PAGE, got {err}"
+    exp = ref.decode(q.cpu(), kc.cpu(), vc.cpu(), table.cpu(), sl.cpu(), ks.cpu(), vs.cpu(), 1 / math.sqrt(D))
+    for b in (0, 2):
+        _check(out[b:b + 1], exp[b:b + 1], f"valid sequence {b}")
+
+
 @pytest.mark.parametrize("num_ctas", [1, 3, 148, 400])
 def test_stream_k_partitions(ops, num_ctas):
     lens = [5000, 17, 64, 0, 2049, 31, 32, 96]

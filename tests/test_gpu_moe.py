@@ -65,8 +65,9 @@ def test_permute_bit_exact(ops, T, lo, E):
     assert torch.equal(perm["tiles"].cpu()[: n + 1], tiles)
 
 
-@pytest.mark.parametrize("T", [1, 8, 64])
+@pytest.mark.parametrize("T", [1, 8, 16, 32, 64, 100])
 def test_experts(ops, bank, T):
+    """T <= 64: the row-owning kernel (token tiles of 8/16/32/64); T = 100: the per-expert kernel."""
     x = bank["x"][:T]
     ids, wts = ops.moe_route(x, bank["router"], 8)
     perm = ops.moe_permute(ids, 0, 64)
