@@ -265,6 +265,32 @@ int okc_tp_allreduce_residual(const float* const* parts, void* const* outs, int*
                               const void* residual, int* state, int rank, int world,
                               long long n, void* workspace, okc_stream_t stream);
 
+/* ------------------------------------------------------------------------------------
+ * The short names of the decode-path contract (the C-ABI list the drop-in boundary
+ * names), as thin forms of the entry points above:
+ *   okc_gemv_bf16       = okc_gemm_bf16 with contiguous x [M,K], W [N,K], y [M,N] (bf16,
+ *                         no residual); `scratch` must hold okc_gemm_bf16_workspace_bytes(M,N,K)
+ *                         bytes, zero-filled once;
+ *   okc_kv_append_rope  = okc_rope_kv_append;
+ *   okc_moe_w4a16       = okc_moe_experts_w4a16;
+ *   okc_rmsnorm         = okc_rmsnorm_bf16 with plain weight (no unit offset).
+ * ---------------------------------------------------------------------------------- */
+int okc_gemv_bf16(const void* x, const void* w, void* y, int M, int N, int K, int ldw, void* scratch,
+                  okc_stream_t stream);
+int okc_kv_append_rope(const void* qkv, int ldqkv, const int64_t* positions,
+                       const int32_t* page_table, int table_ld, int max_pages,
+                       const float* inv_freq, const float* k_scale, const float* v_scale,
+                       void* q_out, void* k_cache, void* v_cache, int64_t* slots_out,
+                       int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
+                       void* workspace, size_t workspace_bytes, okc_stream_t stream);
+int okc_moe_w4a16(const void* x, const int32_t* ids, const float* weights,
+                  const int32_t* counts, const int32_t* offsets, const int32_t* pairs,
+                  const void* w13, const void* w13_sf, const float* w13_gs,
+                  const void* w2, const void* w2_sf, const float* w2_gs,
+                  void* out, int T, int topk, int H, int I, int expert_lo, int E_local,
+                  void* workspace, size_t workspace_bytes, okc_stream_t stream);
+int okc_rmsnorm(const void* x, const void* w, void* y, int T, int H, float eps, okc_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

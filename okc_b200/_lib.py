@@ -52,6 +52,12 @@ SIGNATURES: dict[str, tuple] = {
                                        _i, _i, _i, _i, _i, _i64, _f, _i, _p, _i, _f, _p, _sz, _p]),
     "okc_attn_decode_fp8": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
                                  _i, _i, _i, _i, _i, _i64, _f, _i, _p, _sz, _p]),
+    "okc_gemv_bf16": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),
+    "okc_kv_append_rope": (_i, [_p, _i, _p, _p, _i, _i, _p, _p, _p, _p, _p, _p, _p,
+                                _i, _i, _i, _i, _i, _i64, _p, _sz, _p]),
+    "okc_moe_w4a16": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
+                           _p, _sz, _p]),
+    "okc_rmsnorm": (_i, [_p, _p, _p, _i, _i, _f, _p]),
     "okc_ipc_alloc": (_i, [_sz, C.POINTER(_p)]),
     "okc_ipc_free": (_i, [_p]),
     "okc_ipc_handle": (_i, [_p, _p]),

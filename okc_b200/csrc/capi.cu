@@ -285,4 +285,36 @@ int okc_moe_experts_w4a16_ex(const void* x, const int32_t* ids, const float* wei
                                  w2_gs, out, T, topk, H, I, expert_lo, E_local, workspace, stream, out_fp32);
 }
 
+
+// ------------------------------------------------------------------ contract short names
+int okc_gemv_bf16(const void* x, const void* w, void* y, int M, int N, int K, int ldw, void* scratch,
+                  okc_stream_t stream) {
+  if (!scratch) return OKC_ERR_WORKSPACE;
+  return okc_gemm_bf16_ex(x, K, w, ldw, y, N, nullptr, M, N, K, 0, 0, 0, scratch,
+                          okc_gemm_bf16_workspace_bytes(M, N, K), stream);
+}
+
+int okc_kv_append_rope(const void* qkv, int ldqkv, const int64_t* positions, const int32_t* page_table,
+                       int table_ld, int max_pages, const float* inv_freq, const float* k_scale,
+                       const float* v_scale, void* q_out, void* k_cache, void* v_cache, int64_t* slots_out,
+                       int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages, void* workspace,
+                       size_t workspace_bytes, okc_stream_t stream) {
+  return okc_rope_kv_append(qkv, ldqkv, positions, page_table, table_ld, max_pages, inv_freq, k_scale, v_scale,
+                            q_out, k_cache, v_cache, slots_out, B, Hq, Hkv, D, page_size, num_pages, workspace,
+                            workspace_bytes, stream);
+}
+
+int okc_moe_w4a16(const void* x, const int32_t* ids, const float* weights, const int32_t* counts,
+                  const int32_t* offsets, const int32_t* pairs, const void* w13, const void* w13_sf,
+                  const float* w13_gs, const void* w2, const void* w2_sf, const float* w2_gs, void* out, int T,
+                  int topk, int H, int I, int expert_lo, int E_local, void* workspace, size_t workspace_bytes,
+                  okc_stream_t stream) {
+  return okc_moe_experts_w4a16(x, ids, weights, counts, offsets, pairs, w13, w13_sf, w13_gs, w2, w2_sf, w2_gs,
+                               out, T, topk, H, I, expert_lo, E_local, workspace, workspace_bytes, stream);
+}
+
+int okc_rmsnorm(const void* x, const void* w, void* y, int T, int H, float eps, okc_stream_t stream) {
+  return okc_rmsnorm_bf16(x, H, w, y, H, T, H, eps, 0, stream);
+}
+
 }  // extern "C"

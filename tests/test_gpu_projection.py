@@ -91,3 +91,29 @@ def test_tcgen05_family(ops, M, K, N):
     _close(y2, ref.gemm(x.cpu(), w.cpu(), residual=r.cpu()), f"tc+res M{M}")
     y3 = ops.gemm(x, w, out_fp32=True, family=2)
     torch.testing.assert_close(y3.cpu(), ref.gemm(x.cpu(), w.cpu(), out_fp32=True), rtol=1e-3, atol=1e-3)
+
+
+def test_contract_short_names(ops):
+    """okc_gemv_bf16 / okc_rmsnorm (the contract's short names) give the same bytes as the
+    full entry points."""
+    import ctypes as C
+    from okc_b200 import _lib, synth
+    lib = _lib.load()
+    x, w = synth.projection_case(4, 4096, 6144, device="cuda")
+    y_ref = ops.gemm(x, w)
+    y = torch.empty_like(y_ref)
+    scratch = torch.zeros(lib.okc_gemm_bf16_workspace_bytes(4, 6144, 4096) + 256, dtype=torch.uint8, device="cuda")
+    st = lib.okc_gemv_bf16(x.data_ptr(), w.data_ptr(), y.data_ptr(), 4, 6144, 4096, 4096, scratch.data_ptr(),
+                           torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.int16), y_ref.view(torch.int16))
+    g = torch.Generator(device="cuda").manual_seed(5)
+    xn = torch.randn((3, 1024), generator=g, device="cuda").to(torch.bfloat16)
+    nw = torch.randn((1024,), generator=g, device="cuda").to(torch.bfloat16)
+    r_ref = ops.rmsnorm(xn, nw, 1e-6)
+    r = torch.empty_like(r_ref)
+    assert lib.okc_rmsnorm(xn.data_ptr(), nw.data_ptr(), r.data_ptr(), 3, 1024, C.c_float(1e-6),
+                           torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(r.view(torch.int16), r_ref.view(torch.int16))
