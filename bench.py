@@ -151,7 +151,7 @@ def run_reference(args):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(val / 1000, 3), "higher_is_better": False, "scaling": "strong",
             "vs_baseline": None, "dtype": "fp32 (CPU oracle)", "data": "synthetic",
-            "config": dict(WORKLOAD, parallelism="cpu"),
+            "config": dict(WORKLOAD, parallelism=f"tp{args.gpus}", reference_runs_on="host cores (rank 0)"),
             "cpu_baseline": {"value": round(val, 1), "unit": "us/step", "cores": cores, "kind": "port",
                              "sample": sample},
             "e2e": {"value": round(val, 1), "unit": "us/step", "h2d_bytes_per_step": 0,
