@@ -248,14 +248,19 @@ int okc_moe_experts_w4a16_ex(const void* x, const int32_t* ids, const float* wei
  *
  * okc_tp_allreduce_residual: out_r = bf16(residual + sum_q parts[q]) on every rank r
  * (residual may be NULL: out_r = bf16(sum_q parts[q])).
- * parts[q] (fp32 [n]), outs[q] (bf16 [n]) and flags[q] (int [16], zero-filled) are HOST
- * arrays of `world` device pointers: this rank's own buffers at index `rank`, the peers'
- * mapped buffers elsewhere.  state: this rank's int [2] (zero-filled), private to one
- * exchange group.  Every rank calls it in the same order on its own stream.  Rank r sums
+ * parts[q] (fp32 [n]), outs[q] (bf16 [n]) and flags[q] (int [OKC_TP_EXCHANGE_FLAG_WORDS],
+ * zero-filled) are HOST arrays of `world` device pointers: this rank's own buffers at index
+ * `rank`, the peers' mapped buffers elsewhere.  state: this rank's int [OKC_TP_STATE_WORDS]
+ * (zero-filled), private to one exchange group and shared by its calls of both exchange
+ * entry points.  Every rank calls it in the same order on its own stream.  Rank r sums
  * the r-th slice of the elements in rank order and stores it into every rank's output;
- * the call completes on a rank when all slices have arrived there.  Flag waits are
- * bounded (2 s): on expiry OKC_DEVERR_TIMEOUT is set in the workspace error word.
+ * the call completes on a rank when all slices have arrived there.  Synchronisation is per
+ * CTA (CTA c waits only for CTA c of the other ranks).  Flag waits are bounded (2 s): on
+ * expiry OKC_DEVERR_TIMEOUT is set in the workspace error word.  The workspace holds at
+ * least 4096 bytes (error word; optional phase trace at byte 256, OKC_TP_TRACE=1).
  * n multiple of 4; world 2..8; parts 16-byte aligned, outs and residual 8-byte aligned. */
+#define OKC_TP_STATE_WORDS 1024
+#define OKC_TP_EXCHANGE_FLAG_WORDS 8192
 int okc_ipc_alloc(size_t bytes, void** ptr);
 int okc_ipc_free(void* ptr);
 int okc_ipc_handle(const void* ptr, void* handle_out);
@@ -264,6 +269,28 @@ int okc_ipc_close(void* ptr);
 int okc_tp_allreduce_residual(const float* const* parts, void* const* outs, int* const* flags,
                               const void* residual, int* state, int rank, int world,
                               long long n, void* workspace, okc_stream_t stream);
+
+/* okc_tp_oproj_allreduce_residual: the row-parallel O projection fused with the exchange
+ * above, in one tcgen05 kernel: out_r = bf16(residual + sum_q x_q · W_q^T) on every rank r,
+ * x_q bf16 [M, K] (row stride ldx) and W_q bf16 [N, K] (row stride ldw) being rank q's
+ * attention output and O-weight columns; out and residual bf16 [M, N] with row stride ldo.
+ * Each CTA pair splits one 128-row weight tile's K range (partial sums meet in distributed
+ * shared memory), pushes each token slice of the tile as fp32 into the owning rank's receive
+ * buffer over NVLink, and the owner sums the ranks' slices in rank order, adds the residual
+ * and stores bf16 into every rank's output.  recv[q], outs[q], flags[q] are HOST arrays of
+ * `world` device pointers (own buffers at `rank`, mapped peer buffers elsewhere): recv of
+ * okc_tp_oproj_plan's recv_bytes, flags of its flag_words ints (zero-filled, not shared with
+ * okc_tp_allreduce_residual's flag words).  state: the exchange group's int
+ * [OKC_TP_STATE_WORDS].  Same ordering, per-CTA synchronisation and timeout rules as
+ * okc_tp_allreduce_residual.  M 1..128, N multiple of 8, K multiple of 8, world 2..8 with
+ * 64 (M <= 64: 32) divisible by world; 16-byte aligned pointers.  OKC_ERR_INVALID when the
+ * shape is outside that range or the grid cannot be co-resident on this GPU.
+ * okc_tp_oproj_plan: OKC_OK and the buffer sizes when the shape is supported. */
+int okc_tp_oproj_plan(int M, int N, int K, int world, size_t* recv_bytes, int* flag_words);
+int okc_tp_oproj_allreduce_residual(const void* x, int ldx, const void* w, int ldw, int M, int N, int K,
+                                    float* const* recv, void* const* outs, int* const* flags,
+                                    const void* residual, int ldo, int* state, int rank, int world,
+                                    void* workspace, okc_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
  * The short names of the decode-path contract (the C-ABI list the drop-in boundary

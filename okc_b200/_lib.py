@@ -65,6 +65,9 @@ SIGNATURES: dict[str, tuple] = {
     "okc_ipc_close": (_i, [_p]),
     "okc_tp_allreduce_residual": (_i, [C.POINTER(_p), C.POINTER(_p), C.POINTER(_p), _p, _p, _i, _i, C.c_longlong,
                                        _p, _p]),
+    "okc_tp_oproj_plan": (_i, [_i, _i, _i, _i, C.POINTER(_sz), C.POINTER(_i)]),
+    "okc_tp_oproj_allreduce_residual": (_i, [_p, _i, _p, _i, _i, _i, _i, C.POINTER(_p), C.POINTER(_p),
+                                             C.POINTER(_p), _p, _i, _p, _i, _i, _p, _p]),
     "okc_attn_decode_fp8_noalloc": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
                                          _i, _i, _i, _i, _i, _i64, _f, _i, _p]),
     "okc_moe_route": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),

@@ -6,18 +6,26 @@ their CUDA IPC handles once (torch.distributed is the plumbing: all_gather_objec
 peers' buffers, and then runs `okc_tp_allreduce_residual`: out = bf16(x + sum_r partial_r),
 replicated on every rank, in one kernel that reads and writes the peers' memory directly.
 It replaces the NCCL all-reduce of the partial plus the residual add (one launch instead of
-a collective and three elementwise kernels).  Every rank must construct it and call it in the
+a collective and three elementwise kernels).  Given the O projection's K (`oproj_k`), it also
+sets up `okc_tp_oproj_allreduce_residual`, the O projection fused with that exchange in one
+tcgen05 kernel (fp32 tile slices pushed into the owner rank's receive buffer as each tile's
+accumulator completes).  Every rank must construct it and call it in the
 same order; it is CUDA-graph capturable (fixed buffers, the call epoch lives on the device).
 """
 
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import torch
 import torch.distributed as dist
 
 from . import _lib, ops
+
+
+_STATE_WORDS = 1024            # OKC_TP_STATE_WORDS
+_EXCHANGE_FLAG_WORDS = 8192    # OKC_TP_EXCHANGE_FLAG_WORDS
 
 
 class _DeviceBuffer:
@@ -55,7 +63,7 @@ def _from_ptr(ptr: int, nbytes: int, dtype, device) -> torch.Tensor:
 class TPComm:
     """One exchange group: partial fp32 [T, H] -> out bf16 [T, H] on `world` ranks."""
 
-    def __init__(self, T: int, H: int, group=None, device: int | None = None):
+    def __init__(self, T: int, H: int, group=None, device: int | None = None, oproj_k: int | None = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -65,22 +73,35 @@ class TPComm:
             raise ValueError("T*H must be a multiple of 4")
         self.device = torch.cuda.current_device() if device is None else device
         self.T, self.H = T, H
+        lib = _lib.load()
+        self.oproj_k = None
+        flag_words, recv_bytes = _EXCHANGE_FLAG_WORDS, 16  # exchange flags, then the fused kernel's
+        if oproj_k is not None and os.environ.get("OKC_TP_FUSED", "1") != "0":
+            rb, fw = C.c_size_t(), C.c_int()
+            with torch.cuda.device(self.device):
+                ok = lib.okc_tp_oproj_plan(T, H, oproj_k, self.world, C.byref(rb), C.byref(fw)) == 0
+            agree = [None] * self.world  # every rank must take the same path
+            dist.all_gather_object(agree, ok, group=group)
+            if all(agree):
+                self.oproj_k, recv_bytes = oproj_k, rb.value
+                flag_words += fw.value
         with torch.cuda.device(self.device):
             self._part = _DeviceBuffer(T * H * 4)
             self._out = _DeviceBuffer(T * H * 2)
-            self._flags = _DeviceBuffer(16 * 4)
-            self.state = torch.zeros(4, dtype=torch.int32, device=f"cuda:{self.device}")
-            mine = (self._part.handle(), self._out.handle(), self._flags.handle())
+            self._flags = _DeviceBuffer(flag_words * 4)
+            self._recv = _DeviceBuffer(recv_bytes)
+            self.state = torch.zeros(_STATE_WORDS, dtype=torch.int32, device=f"cuda:{self.device}")
+            mine = (self._part.handle(), self._out.handle(), self._flags.handle(), self._recv.handle())
             allh = [None] * self.world
             dist.all_gather_object(allh, mine, group=group)
-            lib = _lib.load()
             self._opened = []
-            parts, outs, flags = [], [], []
+            parts, outs, flags, recvs = [], [], [], []
             for q in range(self.world):
                 if q == self.rank:
                     parts.append(self._part.ptr.value)
                     outs.append(self._out.ptr.value)
                     flags.append(self._flags.ptr.value)
+                    recvs.append(self._recv.ptr.value)
                     continue
                 ptrs = []
                 for h in allh[q]:
@@ -91,15 +112,18 @@ class TPComm:
                 parts.append(ptrs[0])
                 outs.append(ptrs[1])
                 flags.append(ptrs[2])
+                recvs.append(ptrs[3])
             arr = C.c_void_p * self.world
             self._parts_arr = arr(*parts)
             self._outs_arr = arr(*outs)
             self._flags_arr = arr(*flags)
+            self._flags_f_arr = arr(*[f + _EXCHANGE_FLAG_WORDS * 4 for f in flags])  # the fused kernel's words
+            self._recv_arr = arr(*recvs)
             self.partial = _from_ptr(self._part.ptr.value, T * H * 4, torch.float32,
                                      f"cuda:{self.device}").view(T, H)
             self.out = _from_ptr(self._out.ptr.value, T * H * 2, torch.bfloat16,
                                  f"cuda:{self.device}").view(T, H)
-            self._ws = ops.workspace(self.device, "tp", 256)
+            self._ws = ops.workspace(self.device, "tp", 4096)
         dist.barrier(group=group)
 
     def allreduce_residual(self, residual: torch.Tensor | None) -> torch.Tensor:
@@ -116,6 +140,39 @@ class TPComm:
         _lib.check(st, "okc_tp_allreduce_residual")
         return self.out
 
+    def trace_stamps(self) -> torch.Tensor:
+        """The phase trace of the last 4 calls of each kernel (int64 ns [2, 4, 16]: kernel 0 the
+        exchange, 1 the fused O projection; slot = call epoch % 4), filled only when the
+        library runs with OKC_TP_TRACE=1.  Synchronises."""
+        torch.cuda.synchronize(self.device)
+        return self._ws[256:256 + 2 * 64 * 8].view(torch.int64).view(2, 4, 16).cpu()
+
+    @property
+    def fused(self) -> bool:
+        """True when `oproj_allreduce_residual` (the fused kernel) is set up on every rank."""
+        return self.oproj_k is not None
+
+    def oproj_allreduce_residual(self, x: torch.Tensor, w: torch.Tensor,
+                                 residual: torch.Tensor | None) -> torch.Tensor:
+        """out = bf16(residual + sum over ranks of x_r · w_r^T) on every rank, in one kernel:
+        x bf16 [T, K] (this rank's attention output), w bf16 [H, K] (this rank's columns of the
+        O weight), residual bf16 [T, H] or None.  Returns `self.out` (valid until the next call)."""
+        if not self.fused:
+            raise RuntimeError("the fused O projection was not set up (pass oproj_k; shape unsupported?)")
+        K = self.oproj_k
+        if (x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or x.shape != (self.T, K)
+                or w.shape != (self.H, K) or not x.is_contiguous() or not w.is_contiguous()):
+            raise ValueError(f"x must be bf16 [{self.T}, {K}] and w bf16 [{self.H}, {K}], both contiguous")
+        if residual is not None and (residual.dtype != torch.bfloat16 or residual.shape != (self.T, self.H)
+                                     or not residual.is_contiguous()):
+            raise ValueError("residual must be a contiguous bf16 [T, H] tensor")
+        st = _lib.load().okc_tp_oproj_allreduce_residual(
+            x.data_ptr(), K, w.data_ptr(), K, self.T, self.H, K, self._recv_arr, self._outs_arr, self._flags_f_arr,
+            None if residual is None else residual.data_ptr(), self.H, self.state.data_ptr(), self.rank, self.world,
+            self._ws.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+        _lib.check(st, "okc_tp_oproj_allreduce_residual")
+        return self.out
+
     def close(self):
         """Unmaps the peers' buffers and frees this rank's (call on every rank, after a
         barrier, when no kernel that uses them is in flight)."""
@@ -123,7 +180,7 @@ class TPComm:
         for p in self._opened:
             lib.okc_ipc_close(p)
         self._opened = []
-        for b in (self._part, self._out, self._flags):
+        for b in (self._part, self._out, self._flags, self._recv):
             b.free()
 
 

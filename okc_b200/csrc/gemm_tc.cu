@@ -27,11 +27,9 @@
 #include <stdlib.h>
 
 #include "kernels.cuh"
+#include "tcgen05.cuh"
 
 namespace okc {
-
-constexpr int TC_BM = 128;  // weight rows per tile (MMA M)
-constexpr int TC_BK = 64;   // K elements per stage (128 bytes: one swizzle atom row)
 
 // Optional epilogue of the QKV projection: interleaved RoPE on the q and k columns, q to
 // bf16 [M][Hq][D], k and v quantised to e4m3 into the paged caches at slot(token) (the work of
@@ -62,51 +60,6 @@ struct TcParams {
   int rope_on;    // 1: every tile goes through tc_reduce_kernel, which applies `rope`
   TcRopeEpi rope;
 };
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// UMMA shared-memory descriptor, K-major SWIZZLE_128B: 8-row groups 1024 B apart (SBO),
-// LBO unused (1), descriptor version 1, layout type 2.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-// kind::f16 instruction descriptor: D f32, A/B bf16, both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
 
 template <int BN, int STAGES, int KS = 1>
 struct TcCfg {
@@ -441,7 +394,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-static bool make_map(CUtensorMap* m, const void* base, int inner, int rows, int ld, int box_rows) {
+bool tc_make_map(CUtensorMap* m, const void* base, int inner, int rows, int ld, int box_rows) {
   auto fn = tensor_map_encoder();
   if (!fn) return false;
   cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
@@ -518,7 +471,7 @@ static int launch_tc_t(const void* x, int ldx, const void* w, int ldw, TcParams&
                        void* ws, size_t ws_bytes, cudaStream_t stream) {
   using C = TcCfg<BN, STAGES, KS>;
   CUtensorMap mw, mx;
-  if (!make_map(&mw, w, p.K, p.N, ldw, TC_BM) || !make_map(&mx, x, p.K, p.M, ldx, BN)) return OKC_ERR_INVALID;
+  if (!tc_make_map(&mw, w, p.K, p.N, ldw, TC_BM) || !tc_make_map(&mx, x, p.K, p.M, ldx, BN)) return OKC_ERR_INVALID;
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(tc_gemm_kernel<BN, STAGES, KS>, cudaFuncAttributeMaxDynamicSharedMemorySize,

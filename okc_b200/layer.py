@@ -8,8 +8,9 @@ Every stage is an okc_b200 kernel; the step is captured in one CUDA graph by the
 (bench.py) so launch latency does not count.  Tensor parallel over `world` ranks: rank r
 owns query heads [r*Hq/W, (r+1)*Hq/W) and KV heads [r*Hkv/W, ...) — its slice of the
 QKV weight (column parallel, no communication) and of its own paged cache; the O
-projection is row parallel and produces an fp32 partial, and one kernel over NVLink peer
-memory (okc_b200.comm.TPComm) sums the partials of all ranks and adds the residual.  Mirrors the composition of
+projection is row parallel, and one tcgen05 kernel computes it and sums the ranks' partials
+over NVLink peer memory with the residual (okc_b200.comm.TPComm; fallback: an fp32 partial
+GEMM followed by the peer-memory exchange kernel).  Mirrors the composition of
 muse_decode_layer/decode/runtime.py:47-75 (attention -> O -> boundary) without Muse's
 gated residual, QK-norm and output gate, which this plain layer (RMSNorm, x + O) does not have.
 """
@@ -73,7 +74,11 @@ class DecodeLayer:
         passes = 1 if tokens <= 256 else (tokens + 255) // 256  # tcgen05 GEMM: 256 tokens a launch
         per_gemm = 2 * passes if tokens > 32 else 1  # tcgen05 stream-K + split-tile reduce
         rope = 0 if tokens > 32 else 1  # fused into the QKV reduce on the tcgen05 path
-        return 1 + per_gemm + rope + 2 + per_gemm + (1 if self.world > 1 else 0)
+        oproj = per_gemm
+        if self.world > 1:
+            c = self._comms.get(tokens)
+            oproj = 1 if (c is not None and c.fused) else per_gemm + 1
+        return 1 + per_gemm + rope + 2 + oproj
 
     def step(self, x, positions, page_table, k_cache, v_cache, lens=None, out=None):
         """x bf16 [B, H]; positions int64 [B] (= tokens already cached); caches of this rank's
@@ -102,16 +107,20 @@ class DecodeLayer:
         from .comm import TPComm
         c = self._comms.get(tokens)
         if c is None:
-            c = TPComm(tokens, self.cfg.hidden, group=self.group)
+            c = TPComm(tokens, self.cfg.hidden, group=self.group, oproj_k=self.lq * self.cfg.head_dim)
             self._comms[tokens] = c
         return c
 
     def o_proj_allreduce(self, o2, x, out=None):
-        """Row-parallel O projection, then out = bf16(x + sum over ranks) through the
-        peer-memory exchange kernel (okc_tp_allreduce_residual)."""
+        """Row-parallel O projection and out = bf16(x + sum over ranks): one fused tcgen05 +
+        NVLink kernel (okc_tp_oproj_allreduce_residual) where the shape allows, else the fp32
+        partial GEMM followed by the peer-memory exchange kernel (okc_tp_allreduce_residual)."""
         comm = self.comm_for(x.shape[0])
-        ops.gemm(o2, self.wo, out_fp32=True, out=comm.partial)
-        res = comm.allreduce_residual(x)
+        if comm.fused:
+            res = comm.oproj_allreduce_residual(o2, self.wo, x)
+        else:
+            ops.gemm(o2, self.wo, out_fp32=True, out=comm.partial)
+            res = comm.allreduce_residual(x)
         if out is not None:
             out.copy_(res)
             return out

@@ -152,3 +152,180 @@ def test_expert_parallel_moe_two_ranks(T):
         # the shares are summed over ranks instead of in one slot loop: bf16 outputs may move
         # by one rounding step
         assert rel < 2e-3 and mx < 5e-2, f"rank {rank}: rel-L2 {rel:.2e}, max abs {mx:.2e}"
+
+
+def _fused_worker(rank, world, port, T, H, K, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from okc_b200 import ops
+        from okc_b200.comm import TPComm
+        comm = TPComm(T, H, oproj_k=K)
+        out = {"fused": comm.fused, "bad": [], "bad_unfused": [], "replica_diff": []}
+
+        def case(seed):
+            xs = [torch.randn((T, K), generator=torch.Generator().manual_seed(seed + r)).to(torch.bfloat16)
+                  for r in range(world)]
+            ws = [(torch.randn((H, K), generator=torch.Generator().manual_seed(seed + 50 + r)) * 0.05).to(torch.bfloat16)
+                  for r in range(world)]
+            res = torch.randn((T, H), generator=torch.Generator().manual_seed(seed + 99)).to(torch.bfloat16)
+            exp = res.float().clone()
+            for r in range(world):
+                exp += xs[r].float() @ ws[r].float().T
+            return xs[rank].cuda(), ws[rank].cuda(), res.cuda(), exp
+
+        def n_bad(got, exp):
+            # within one bf16 rounding step of the exact fp32 sum (fp32 accumulation error ~1e-6)
+            err = (got.float().cpu() - exp).abs()
+            return int((err > exp.abs() * 2.0 ** -7 + 1e-3).sum())
+
+        for it in range(3):
+            xd, wd, rd, exp = case(1000 * it)
+            got = comm.oproj_allreduce_residual(xd, wd, rd).clone()
+            # the unfused path on the same exchange group (shared call epoch, other flag words)
+            ops.gemm(xd, wd, out_fp32=True, out=comm.partial)
+            ref2 = comm.allreduce_residual(rd).clone()
+            torch.cuda.synchronize()
+            allg = [torch.empty_like(got) for _ in range(world)]
+            dist.all_gather(allg, got)
+            out["replica_diff"].append(sum(int((a.view(torch.int16) != got.view(torch.int16)).sum()) for a in allg))
+            out["bad"].append(n_bad(got, exp))
+            out["bad_unfused"].append(n_bad(ref2, exp))
+        # CUDA-graph replay with fresh inputs copied in
+        xd, wd, rd, _ = case(7)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            comm.oproj_allreduce_residual(xd, wd, rd)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            out_g = comm.oproj_allreduce_residual(xd, wd, rd)
+        for it in range(2):
+            x2, w2, r2, exp = case(5000 + 100 * it)
+            xd.copy_(x2)
+            wd.copy_(w2)
+            rd.copy_(r2)
+            torch.cuda.synchronize()
+            dist.barrier()
+            g.replay()
+            torch.cuda.synchronize()
+            out["bad"].append(n_bad(out_g, exp))
+        out["derr"] = ops.read_device_error("tp", rank)
+        del g
+        torch.cuda.synchronize()
+        dist.barrier()
+        comm.close()
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("T,H,K", [(128, 1024, 512), (100, 2048, 256), (8, 1024, 512), (64, 8192, 4096),
+                                   (128, 8192, 4096)])
+def test_tp_oproj_fused_two_ranks(T, H, K):
+    """okc_tp_oproj_allreduce_residual (O projection + exchange in one tcgen05 kernel): every output
+    within one bf16 rounding of the exact fp32 result, identical bits on both ranks, interleaved
+    with the unfused path on the same group, and under CUDA-graph replay."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, 2, port, T, H, K, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, out in res:
+        assert out["fused"], f"rank {rank}: fused path not available for {T}x{H}x{K}"
+        assert out["derr"] == 0, f"rank {rank}: device error {out['derr']}"
+        assert all(b == 0 for b in out["bad"]), f"rank {rank}: elements off by more than one bf16 step {out['bad']}"
+        assert all(b == 0 for b in out["bad_unfused"]), f"rank {rank}: unfused path {out['bad_unfused']}"
+        assert all(d == 0 for d in out["replica_diff"]), f"rank {rank}: replicas differ {out['replica_diff']}"
+
+
+def _layer_worker(rank, world, port, B, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from okc_b200 import ops, synth
+        from okc_b200.layer import DecodeLayer, LayerConfig
+        from oracle import layer as olayer
+        H, Hq, Hkv, D, page = 4096, 32, 4, 128, 16
+        g = torch.Generator(device="cuda").manual_seed(11)  # identical on every rank
+        lens = [int(v) for v in torch.randint(16, 1500, (B,), generator=torch.Generator().manual_seed(2))]
+        pool = sum((n + 1 + page - 1) // page for n in lens) + 8
+        table = synth.paged_layout(lens, page, pool, g, "cuda", extra_tokens=1)
+        kc = torch.empty((pool, page, Hkv, D), dtype=torch.float8_e4m3fn, device="cuda")
+        vc = torch.empty_like(kc)
+        ks = (torch.rand(Hkv, generator=g, device="cuda") * 1.5 + 0.5).float()
+        vs = (torch.rand(Hkv, generator=g, device="cuda") * 1.5 + 0.5).float()
+        synth.fill_e4m3_normal(kc, g, ks)
+        synth.fill_e4m3_normal(vc, g, vs)
+        x = torch.randn((B, H), generator=g, device="cuda").to(torch.bfloat16)
+        nw = (1 + 0.02 * torch.randn(H, generator=g, device="cuda")).to(torch.bfloat16)
+        wqkv = (torch.randn(((Hq + 2 * Hkv) * D, H), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        wo = (torch.randn((H, Hq * D), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        pos = torch.tensor(lens, dtype=torch.int64, device="cuda")
+        cfg = LayerConfig(hidden=H, num_q_heads=Hq, num_kv_heads=Hkv, head_dim=D, rope_theta=5e5, eps=1e-6,
+                          page_size=page)
+        lkv = Hkv // world
+        kc_r = kc[:, :, rank * lkv:(rank + 1) * lkv].contiguous()
+        vc_r = vc[:, :, rank * lkv:(rank + 1) * lkv].contiguous()
+        layer = DecodeLayer(cfg, nw, wqkv, wo, ks, vs, rank, world)
+        got = layer.step(x, pos, table, kc_r, vc_r).clone()
+        fused = layer.comm_for(B).fused
+        torch.cuda.synchronize()
+        allg = [torch.empty_like(got) for _ in range(world)]
+        dist.all_gather(allg, got)
+        replica_diff = sum(int((a.view(torch.int16) != got.view(torch.int16)).sum()) for a in allg)
+        derr = ops.read_device_error("tp", rank)
+        torch.cuda.synchronize()
+        dist.barrier()
+        layer.close()
+        exp = None
+        if rank == 0:
+            exp, _ = olayer.decode_layer(x.cpu(), nw.cpu(), wqkv.cpu(), wo.cpu(), pos.cpu(), table.cpu(), kc.cpu(),
+                                         vc.cpu(), ks.cpu(), vs.cpu(), Hq, Hkv, D, 5e5, 1e-6, D ** -0.5)
+        q.put((rank, got.cpu(), exp, fused, replica_diff, derr))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("B", [8, 48])
+def test_tp_layer_two_ranks_vs_oracle(B):
+    """The decode layer at TP 2 (heads and KV cache split by rank, fused O projection + exchange)
+    against the CPU oracle of the whole layer; both ranks hold the same output bits."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_layer_worker, args=(r, 2, port, B, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=600) for _ in procs], key=lambda t: t[0])
+    for p in procs:
+        p.join(timeout=60)
+    exp = res[0][2]
+    for rank, got, _, fused, replica_diff, derr in res:
+        assert fused, f"rank {rank}: the fused O projection was not used"
+        assert derr == 0, f"rank {rank}: device error {derr}"
+        assert replica_diff == 0, f"rank {rank}: replicas differ in {replica_diff} elements"
+        o, e = got.float(), exp.float()
+        torch.testing.assert_close(o, e, rtol=2e-2, atol=2e-2, msg=f"rank {rank}")
+        assert (o - e).norm() / e.norm() < 1e-2
