@@ -12,10 +12,9 @@
 // Synchronisation is per CTA: CTA c of a rank only ever waits for CTA c of the other ranks
 // (the grids are identical on every rank), with one flag word per (CTA, source rank) and one
 // call epoch per CTA in `state`.  A signal is a release: the CTA's threads finish their stores,
-// meet at a barrier, and thread q < W issues fence.acq_rel.sys and a relaxed system-scope store
-// of the epoch into rank q's flag word (the W fences run in parallel; a fence.sc.sys, or a
-// chain of release stores to the peers, costs more).  A wait is an acquire load loop on the
-// local flag word.  There is no grid-wide barrier, no atomic counter and no "last CTA".
+// meet at a barrier, and one thread issues fence.acq_rel.sys followed by relaxed system-scope
+// stores of the epoch into the peers' flag words (a fence.sc.sys, a fence per peer, or a chain
+// of release stores costs more).  A wait is an acquire load loop on the local flag word.  There is no grid-wide barrier, no atomic counter and no "last CTA".
 // Every wait is bounded (2 s of %globaltimer): on expiry the kernel sets OKC_DEVERR_TIMEOUT in
 // the error word and goes on, so a missing rank cannot hang the GPU.
 // No TMA multicast; the only TMA sources are this GPU's own buffers.
@@ -56,12 +55,15 @@ __device__ bool wait_flag(const int* f, int epoch, int* err) {
   return true;
 }
 
-// After a barrier over the CTA's storing threads: thread q < W (q != rank) publishes `epoch`
-// into word `slot` of rank q's flag array.
+// After a barrier over the CTA's storing threads: thread 0 issues ONE system-scope release
+// fence and then publishes `epoch` into word `slot` of every other rank's flag array (relaxed
+// stores after the fence: they do not wait for one another).  Concurrent system fences are
+// expensive (each waits for the SM's outstanding NVLink stores), so a CTA issues one per signal.
 __device__ __forceinline__ void tp_signal(int* const* flags, int t, int world, int rank, int slot, int epoch) {
-  if (t < world && t != rank) {
+  if (t == 0) {
     fence_acq_rel_sys();
-    st_relaxed_sys(&flags[t][slot], epoch);
+    for (int q = 0; q < world; ++q)
+      if (q != rank) st_relaxed_sys(&flags[q][slot], epoch);
   }
 }
 // Thread q < W (q != rank) waits for word `base + q` of this rank's flag array; false on timeout.

@@ -1,8 +1,13 @@
-"""Tensor-parallel exchange over NVLink peer memory (okc_tp_allreduce_residual) on 2 GPUs:
-out = bf16(x + sum_r partial_r) on every rank, bit-exact against the same fp32 sums taken in
-rank order on the host side; repeated calls (the device-side epoch) and a CUDA-graph replay.
-Expert-parallel MoE (okc_b200.comm.ExpertParallelMoE, half of the experts per rank) against the
-single-GPU MoE over the whole bank.  Skipped when fewer than 2 GPUs are visible."""
+"""Tensor-parallel exchange over NVLink peer memory on 2 (4, 8) GPUs:
+  * okc_tp_allreduce_residual: out = bf16(x + sum_r partial_r) on every rank, bit-exact against
+    the same fp32 sums taken in rank order on the host side; repeated calls (the device-side
+    epochs) and a CUDA-graph replay;
+  * okc_tp_oproj_allreduce_residual (O projection fused with the exchange): within one bf16
+    rounding of the exact result, identical replicas, interleaved with the unfused path;
+  * the decode layer at TP 2 against the CPU oracle of the whole layer;
+  * expert-parallel MoE (okc_b200.comm.ExpertParallelMoE, half of the experts per rank)
+    against the single-GPU MoE over the whole bank.
+Each test is skipped when fewer GPUs than its ranks are visible."""
 
 import os
 import socket
@@ -228,18 +233,21 @@ def _fused_worker(rank, world, port, T, H, K, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("T,H,K", [(128, 1024, 512), (100, 2048, 256), (8, 1024, 512), (64, 8192, 4096),
-                                   (128, 8192, 4096)])
-def test_tp_oproj_fused_two_ranks(T, H, K):
+@pytest.mark.parametrize("world,T,H,K", [(2, 128, 1024, 512), (2, 100, 2048, 256), (2, 8, 1024, 512),
+                                         (2, 64, 8192, 4096), (2, 128, 8192, 4096), (4, 128, 8192, 2048),
+                                         (4, 40, 1024, 256), (8, 128, 8192, 1024), (8, 16, 2048, 512)])
+def test_tp_oproj_fused_ranks(world, T, H, K):
     """okc_tp_oproj_allreduce_residual (O projection + exchange in one tcgen05 kernel): every output
-    within one bf16 rounding of the exact fp32 result, identical bits on both ranks, interleaved
-    with the unfused path on the same group, and under CUDA-graph replay."""
+    within one bf16 rounding of the exact fp32 result, identical bits on every rank, interleaved
+    with the unfused path on the same group, and under CUDA-graph replay.  Runs when `world`
+    GPUs are visible."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_fused_worker, args=(r, 2, port, T, H, K, q)) for r in range(2)]
+    procs = [ctx.Process(target=_fused_worker, args=(r, world, port, T, H, K, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in procs]
