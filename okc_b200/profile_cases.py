@@ -8,12 +8,21 @@ prints one JSON line with the CUDA-event time per launch and the algorithmic byt
     python -m okc_b200.profile_cases gemv   --m 1 --k 8192 --n 10240
     python -m okc_b200.profile_cases moe    --t 8
     python -m okc_b200.profile_cases layer
+
+The `tp` case runs on W ranks (one process per GPU, under torchrun) and times the O projection
++ tensor-parallel exchange variants at T = 128 tokens, H = 8192 per call (graphs of 20
+back-to-back calls, the max over ranks); with OKC_TP_TRACE=1 it adds the %globaltimer phase
+trace of CTA 0 of each kernel (ns from its griddepcontrol.wait) for its last three calls:
+
+    OKC_TP_TRACE=1 python -m torch.distributed.run --nnodes=1 --nproc-per-node 2 \
+        --master-addr 127.0.0.1 --master-port 29513 -m okc_b200.profile_cases tp --kk 4096,1024
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import os
 import sys
 
 import torch
@@ -70,9 +79,75 @@ def case_moe(a):
     return {"case": "moe", "t": a.t, "experts_hit": hit, "us": us, "bytes": by, "gbs": by / us / 1e3}
 
 
+def case_tp(a):
+    import datetime
+
+    import torch.distributed as dist
+
+    from .comm import TPComm
+    world, rank = int(os.environ["WORLD_SIZE"]), int(os.environ["RANK"])
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    T, H, R = 128, 8192, 20
+    res = {"case": "tp", "world": world, "T": T, "H": H}
+    for K in [int(k) for k in a.kk.split(",")]:
+        comm = TPComm(T, H, oproj_k=K)
+        g = torch.Generator(device="cuda").manual_seed(rank)
+        x = torch.randn((T, K), generator=g, device="cuda").to(torch.bfloat16)
+        w = (torch.randn((H, K), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+        r = torch.randn((T, H), generator=g, device="cuda").to(torch.bfloat16)
+        variants = {
+            "fused": lambda: comm.oproj_allreduce_residual(x, w, r),
+            "gemm+exchange": lambda: (ops.gemm(x, w, out_fp32=True, out=comm.partial), comm.allreduce_residual(r)),
+            "gemm_fp32": lambda: ops.gemm(x, w, out_fp32=True, out=comm.partial),
+            "exchange": lambda: comm.allreduce_residual(r),
+        }
+        for name, fn in variants.items():
+            if name == "fused" and not comm.fused:
+                continue
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for _ in range(3):
+                    fn()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            dist.barrier()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                for _ in range(R):
+                    fn()
+            for _ in range(3):
+                gr.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                gr.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = torch.tensor([e0.elapsed_time(e1) * 1000 / (5 * R)], device="cuda")
+            dist.all_reduce(us, op=dist.ReduceOp.MAX)
+            res[f"K{K}/{name}_us"] = round(float(us), 2)
+            if name in ("fused", "exchange") and rank == 0:
+                st = comm.trace_stamps()[1 if name == "fused" else 0]
+                ep = int(comm.state[512 if name == "fused" else 0].item())
+                if int(st[ep & 3][1]):
+                    res[f"K{K}/{name}_trace_ns"] = [[int(v) - int(st[e & 3][1]) if int(v) else None
+                                                     for v in st[e & 3].tolist()[:11]] for e in (ep - 2, ep - 1, ep)]
+            del gr
+            torch.cuda.synchronize()
+            dist.barrier()
+        res[f"K{K}/device_error"] = ops.read_device_error("tp", rank)
+        comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return res if rank == 0 else None
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["attn", "gemv", "moe"])
+    ap.add_argument("case", choices=["attn", "gemv", "moe", "tp"])
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--b", type=int, default=64)
@@ -86,10 +161,12 @@ def main(argv=None):
     ap.add_argument("--n", type=int, default=10240)
     ap.add_argument("--family", type=int, default=0)
     ap.add_argument("--t", type=int, default=8)
+    ap.add_argument("--kk", default="1024", help="tp: comma-separated O-projection K per rank")
     a = ap.parse_args(argv)
-    torch.cuda.set_device(0)
-    res = {"attn": case_attn, "gemv": case_gemv, "moe": case_moe}[a.case](a)
-    print(json.dumps(res), flush=True)
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    res = {"attn": case_attn, "gemv": case_gemv, "moe": case_moe, "tp": case_tp}[a.case](a)
+    if res is not None:
+        print(json.dumps(res), flush=True)
     return 0
 
 
