@@ -61,3 +61,61 @@ def test_workspace_queries(lib):
                  + ((64 + 1) * 4 + 255) // 256 * 256)  # + the unit prefix for the merge
     assert lib.okc_attn_decode_workspace_bytes(8, 8, 1, 128, 10) > lib.okc_attn_decode_workspace_bytes(8, 8, 8, 128, 10)
     assert lib.okc_moe_experts_workspace_bytes(256, 8, 4096, 1536) > 256
+
+
+def _header_prototypes():
+    src = (ROOT / "include" / "okc_b200.h").read_text()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = re.sub(r"//[^\n]*", "", src)
+    src = re.sub(r"#[^\n]*", "", src)
+    protos = {}
+    for ret, name, params in re.findall(r"([A-Za-z_][\w \t\*]*?)\s*\b(okc_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", src):
+        ps = [p.strip() for p in params.split(",") if p.strip() and p.strip() != "void"]
+        protos[name] = (ret.strip(), ps)
+    return protos
+
+
+def _kind_of_c(decl: str) -> str:
+    decl = " ".join(decl.split())
+    if "*" in decl or decl.startswith("okc_stream_t"):
+        return "ptr"
+    base = decl.replace("const ", "").rsplit(" ", 1)[0] if " " in decl.replace("const ", "") else decl
+    base = base.strip()
+    return {"int": "i32", "long long": "i64", "int64_t": "i64", "size_t": "size", "float": "f32",
+            "double": "f64"}.get(base, "?" + base)
+
+
+def _kind_of_ctypes(t) -> str:
+    import ctypes as C
+    if t in (C.c_void_p, C.c_char_p) or (isinstance(t, type) and issubclass(t, C._Pointer)):
+        return "ptr"
+    if t is C.c_size_t:
+        return "size"
+    if t in (C.c_int, C.c_int32):
+        return "i32"
+    if t in (C.c_longlong, C.c_int64):
+        return "i64"
+    if t is C.c_float:
+        return "f32"
+    if t is C.c_double:
+        return "f64"
+    return "?" + repr(t)
+
+
+def test_ctypes_signatures_match_header_prototypes():
+    """Every ctypes argtype / restype has the kind (pointer, int, 64-bit int, size_t, float)
+    of the header's parameter in the same position: a mismatch would pass arguments wrongly."""
+    from okc_b200 import _lib
+    protos = _header_prototypes()
+    assert sorted(protos) == declared_functions()
+    bad = []
+    for name, (ret, params) in protos.items():
+        restype, argtypes = _lib.SIGNATURES[name]
+        want = [_kind_of_c(p) for p in params]
+        got = [_kind_of_ctypes(t) for t in argtypes]
+        if want != got:
+            bad.append(f"{name}: header {want} vs ctypes {got}")
+        rk = "ptr" if "*" in ret else _kind_of_c(ret + " r")
+        if rk != _kind_of_ctypes(restype):
+            bad.append(f"{name}: returns {ret} vs ctypes {restype}")
+    assert not bad, "\n".join(bad)
