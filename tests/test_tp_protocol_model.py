@@ -1,5 +1,6 @@
-"""Explicit-state model check of the tensor-parallel exchange protocols of
-okc_b200/csrc/tp_comm.cu (CPU only).
+"""Explicit-state model checks (CPU only) of the synchronisation protocols of the kernels:
+the tensor-parallel exchange protocols of okc_b200/csrc/tp_comm.cu, and (at the end of the
+file) the mbarrier shared-memory ring of the attention and tcgen05 GEMM kernels.
 
 Both kernels synchronise per CTA index: CTA c of a rank only exchanges flags with CTA c of the
 other ranks, so one CTA index is modelled, on W ranks, over E consecutive calls.  Every
@@ -179,3 +180,114 @@ def test_planted_mistake_in_alternating_use_is_found():
         return _renamed(exchange_program(W, r, wait_exit=False), "x")
     err = _explore(2, 3, prog)
     assert err is not None and "read (" in err, err
+
+
+# ------------------------------------------------------------------------------------------
+# The shared-memory ring of the attention and tcgen05 GEMM kernels (mbarrier full/empty pairs).
+# Producer: for unit i, slot s = i % NS with phase bit ph (flips when s wraps): wait
+# empty[s] with parity ph ^ 1, arm full[s] (expect_tx), issue the copy; the copy lands
+# asynchronously and completes full[s]'s phase.  Consumers (C warps; empty[s] expects C
+# arrivals): wait full[s] with parity ph, read the slot, arrive on empty[s].  Before exiting the
+# producer waits on the full barriers of its last min(issued, NS) units, walking the slots
+# backwards (attention.cu / gemm_tc.cu drain loops).  try_wait.parity(P) succeeds once the
+# barrier's completed-phase count has parity != P (the phase with parity P is complete).
+
+def _ring_explore(NS, N, C, drain=True, parity_ok=True, aborts=True, empty_count=None):
+    """All interleavings of one producer, C consumers and the asynchronous copy completions
+    over N units, including aborts: a consumer may give up at any point (a wait that timed out)
+    and set the abort flag, after which the producer stops issuing (its own bounded empty-wait
+    gives up too) and drains.  Checked: a consumer reads only the unit it waited for; a copy
+    never lands in a slot a consumer has not released; no copy is in flight when the CTA exits
+    (producer drained, every consumer finished or gave up); and nothing is stuck (with aborts
+    off this is the liveness of the protocol itself: a wait that never ends is a hang)."""
+    # state: producer (issued, stage, ph, stopped, drained), abort flag, consumers (unit, stage,
+    # ph, gone), full (completed phases, armed), empty (completed phases, arrivals), copies in
+    # flight ((unit, slot), ...), slot contents
+    init = (0, 0, 0, False, 0, False, tuple((0, 0, 0, False) for _ in range(C)),
+            tuple((0, 0) for _ in range(NS)), tuple((0, 0) for _ in range(NS)), (), tuple(-1 for _ in range(NS)))
+    ec = C if empty_count is None else empty_count  # arrivals that complete an empty phase
+    seen = {init}
+    dq = deque([init])
+    while dq:
+        st = dq.popleft()
+        pi, ps, pph, stopped, dk, ab, cons, full, empty, fly, slot = st
+        looping = pi < N and not stopped
+        n_drain = min(pi, NS) if drain else 0
+        nxt = []
+        if looping:
+            want = (pph ^ 1) if parity_ok else pph
+            if empty[ps][0] % 2 != want:  # issue unit pi into slot ps
+                f = list(full)
+                f[ps] = (f[ps][0], 1)
+                ns, nph = ps + 1, pph
+                if ns == NS:
+                    ns, nph = 0, pph ^ 1
+                nxt.append((pi + 1, ns, nph, stopped, dk, ab, cons, tuple(f), empty, fly + ((pi, ps),), slot))
+            if ab:  # the abort flag is seen (or the bounded empty-wait gives up)
+                nxt.append((pi, ps, pph, True, dk, ab, cons, full, empty, fly, slot))
+        elif dk < n_drain:  # drain: the k-th slot back from the next one to issue
+            sd, ph = ps, pph
+            for _ in range(dk + 1):
+                sd -= 1
+                if sd < 0:
+                    sd, ph = NS - 1, ph ^ 1
+            if full[sd][0] % 2 != ph:
+                nxt.append((pi, ps, pph, stopped, dk + 1, ab, cons, full, empty, fly, slot))
+        for k, (u, sl_) in enumerate(fly):  # a copy lands
+            for ci, (ciu, _, _, gone) in enumerate(cons):
+                if not gone and ciu < u - NS + 1:
+                    return f"unit {u} landed in slot {sl_} before consumer {ci} released unit {u - NS}"
+            f = list(full)
+            f[sl_] = (f[sl_][0] + 1, 0)  # armed arrival + bytes complete: the phase completes
+            sl = list(slot)
+            sl[sl_] = u
+            nxt.append((pi, ps, pph, stopped, dk, ab, cons, tuple(f), empty, fly[:k] + fly[k + 1:], tuple(sl)))
+        for ci, (u, sc, ph, gone) in enumerate(cons):
+            if gone or u >= N:
+                continue
+            if aborts:
+                c2 = list(cons)
+                c2[ci] = (u, sc, ph, True)  # gives up: sets the abort flag and leaves
+                nxt.append((pi, ps, pph, stopped, dk, True, tuple(c2), full, empty, fly, slot))
+            if full[sc][0] % 2 == ph:
+                continue
+            if slot[sc] != u:
+                return f"consumer {ci} read slot {sc} holding unit {slot[sc]} for unit {u}"
+            e = list(empty)
+            ph_e, arr = e[sc]
+            arr += 1
+            e[sc] = (ph_e + 1, 0) if arr == ec else (ph_e, arr)
+            ns, nph = sc + 1, ph
+            if ns == NS:
+                ns, nph = 0, ph ^ 1
+            c2 = list(cons)
+            c2[ci] = (u + 1, ns, nph, False)
+            nxt.append((pi, ps, pph, stopped, dk, ab, tuple(c2), full, tuple(e), fly, slot))
+        producer_done = not looping and dk == n_drain
+        consumers_done = all(g or u >= N for u, _, _, g in cons)
+        if producer_done and consumers_done and fly:
+            return f"CTA exits with copies in flight {fly}"
+        if not nxt and not (producer_done and consumers_done):
+            return f"stuck: producer {pi} stopped={stopped} drained={dk}, consumers {cons}"
+        for t in nxt:
+            if t not in seen:
+                seen.add(t)
+                dq.append(t)
+    return None
+
+
+@pytest.mark.parametrize("NS,N,C", [(2, 5, 1), (3, 6, 1), (3, 5, 2), (2, 4, 3)])
+def test_mbarrier_ring_is_safe_and_drains(NS, N, C):
+    assert _ring_explore(NS, N, C, aborts=False) is None  # safety and liveness
+    assert _ring_explore(NS, N, C) is None                # safety and a clean exit under aborts
+
+
+def test_planted_ring_mistakes_are_found():
+    # the wrong parity on the empty barrier: the producer waits for a phase that never comes
+    assert "stuck" in (_ring_explore(2, 4, 1, parity_ok=False, aborts=False) or "")
+    # empty barriers that expect fewer arrivals than there are consumer warps: a slot is
+    # refilled while a consumer has not read it yet
+    err = _ring_explore(2, 4, 2, aborts=False, empty_count=1) or ""
+    assert "landed in slot" in err or "read slot" in err, err
+    # no drain: after an abort the CTA can exit with copies still landing in its shared memory
+    assert "in flight" in (_ring_explore(2, 4, 1, drain=False) or "")
