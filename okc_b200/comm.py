@@ -1,16 +1,18 @@
 """Tensor-parallel exchange of the multi-GPU decode layer over NVLink peer memory.
 
-`TPComm` owns, on every rank of a process group, three device buffers of its own
-allocation (the fp32 O-projection partial, the bf16 layer output and 16 flag words), exchanges
-their CUDA IPC handles once (torch.distributed is the plumbing: all_gather_object), maps the
-peers' buffers, and then runs `okc_tp_allreduce_residual`: out = bf16(x + sum_r partial_r),
-replicated on every rank, in one kernel that reads and writes the peers' memory directly.
-It replaces the NCCL all-reduce of the partial plus the residual add (one launch instead of
-a collective and three elementwise kernels).  Given the O projection's K (`oproj_k`), it also
-sets up `okc_tp_oproj_allreduce_residual`, the O projection fused with that exchange in one
-tcgen05 kernel (fp32 tile slices pushed into the owner rank's receive buffer as each tile's
-accumulator completes).  Every rank must construct it and call it in the
-same order; it is CUDA-graph capturable (fixed buffers, the call epoch lives on the device).
+`TPComm` owns, on every rank of a process group, four device buffers of its own allocation
+(the fp32 O-projection partial, the bf16 layer output, the fused kernel's fp32 receive slots and
+the flag words), exchanges their CUDA IPC handles once (torch.distributed is the plumbing:
+all_gather_object) and maps the peers' buffers.  Two kernels use them:
+  * `okc_tp_oproj_allreduce_residual` (set up when the O projection's K is given as
+    `oproj_k`): the O projection fused with the exchange in one tcgen05 kernel, fp32 tile
+    slices pushed into the owner rank's receive slots as each tile's accumulator completes,
+    out = bf16(x + sum_r o_r @ wo_r^T) replicated on every rank;
+  * `okc_tp_allreduce_residual`: out = bf16(x + sum_r partial_r) for a partial already in HBM
+    (the expert-parallel MoE's shares), reading and writing the peers' memory directly.
+They replace the NCCL all-reduce of the partial plus the residual add.  Every rank must
+construct a TPComm and call it in the same order; it is CUDA-graph capturable (fixed buffers;
+the per-CTA call epochs live on the device in `state`).
 """
 
 from __future__ import annotations
