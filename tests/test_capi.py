@@ -119,3 +119,46 @@ def test_ctypes_signatures_match_header_prototypes():
         if rk != _kind_of_ctypes(restype):
             bad.append(f"{name}: returns {ret} vs ctypes {restype}")
     assert not bad, "\n".join(bad)
+
+
+def _kernel_bodies():
+    bodies = {}
+    for f in sorted((ROOT / "okc_b200" / "csrc").glob("*.cu")):
+        src = f.read_text()
+        for m in re.finditer(r"__global__\s+void\s+(?:__launch_bounds__\([^)]*\)\s*)?(\w+)\s*\(", src):
+            i = src.index("{", m.end())
+            depth, j = 0, i
+            while True:
+                if src[j] == "{":
+                    depth += 1
+                elif src[j] == "}":
+                    depth -= 1
+                    if depth == 0:
+                        break
+                j += 1
+            bodies[m.group(1)] = src[i:j]
+    return bodies
+
+
+def test_every_pdl_launched_kernel_waits_before_returning():
+    """Kernels launched with programmatic dependent launch (okc_host::launch_k) may start before
+    their predecessor finished, so each must execute griddepcontrol.wait (pdl_wait) before it
+    returns or reads the predecessor's output; then a kernel's completion implies every earlier
+    kernel's, which the cross-GPU protocols rely on.  Kernels launched with <<<>>> are stream
+    ordered and exempt."""
+    src = "".join(f.read_text() for f in (ROOT / "okc_b200" / "csrc").glob("*.cu"))
+    launched = set(re.findall(r"launch_k\(\s*(?:okc::)?(\w+)", src))
+    bodies = _kernel_bodies()
+    assert launched, "no launch_k call found"
+    bad = []
+    for name in sorted(launched):
+        assert name in bodies, f"launch_k of unknown kernel {name}"
+        body = bodies[name]
+        w = body.find("pdl_wait()")
+        if w < 0:
+            bad.append(f"{name}: no pdl_wait")
+            continue
+        early = [r.start() for r in re.finditer(r"\breturn\b", body) if r.start() < w]
+        if early:
+            bad.append(f"{name}: returns before pdl_wait")
+    assert not bad, bad
