@@ -162,3 +162,30 @@ def test_every_pdl_launched_kernel_waits_before_returning():
         if early:
             bad.append(f"{name}: returns before pdl_wait")
     assert not bad, bad
+
+
+def test_every_device_spin_wait_is_bounded():
+    """Device code polls in exactly two places, both bounded by kWaitNs of %globaltimer:
+    mbar_wait (common.cuh: mbarrier phases) and wait_flag (tp_comm.cu: cross-GPU flags).  No
+    other code issues mbarrier.try_wait / test_wait or loops on an acquire load."""
+    csrc = ROOT / "okc_b200" / "csrc"
+    files = {f.name: f.read_text() for f in list(csrc.glob("*.cu")) + list(csrc.glob("*.cuh"))}
+    for name, src in files.items():
+        code = re.sub(r"//[^\n]*", "", src)
+        if name != "common.cuh":
+            assert "mbarrier.try_wait" not in code and "mbarrier.test_wait" not in code, name
+            assert "mbar_try_wait(" not in code, f"{name}: polls an mbarrier outside mbar_wait"
+        for m in re.finditer(r"while\s*\(([^)]*(?:\([^)]*\)[^)]*)*)\)", code):
+            cond = m.group(1)
+            if "ld_acquire" in cond or "volatile" in cond or "ld.acquire" in cond:
+                head = code[:m.start()]
+                fn = re.findall(r"__device__[^{;]*?\b(\w+)\s*\([^;{]*\)\s*\{", head)
+                assert fn and fn[-1] == "wait_flag", f"{name}: flag polling outside wait_flag"
+    common = re.sub(r"//[^\n]*", "", files["common.cuh"])
+    body = common[common.index("bool mbar_wait("):]
+    body = body[:body.index("\n}\n")]
+    assert "kWaitNs" in body and "globaltimer" in body
+    tp = re.sub(r"//[^\n]*", "", files["tp_comm.cu"])
+    body = tp[tp.index("bool wait_flag("):]
+    body = body[:body.index("\n}\n")]
+    assert "kWaitNs" in body and "globaltimer" in body
