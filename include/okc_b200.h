@@ -175,12 +175,20 @@ int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const
  * every call on a device and keeps the last call's contents: calls that may overlap on the GPU
  * (streams without ordering between them) race and must not be issued.  The first call on each
  * device looks up the array's device address (with that device current); make it before any
- * stream capture.  Device-side error bits are cleared by each call and not reported here. */
+ * stream capture.  Device-side problems (a page id outside [0, num_pages) is skipped, not
+ * read) OR their OKC_DEVERR_* bits into an error word kept beside the array, which collects
+ * every call's bits until okc_attn_decode_fp8_noalloc_error() reads and clears it. */
 int okc_attn_decode_fp8_noalloc(const void* q, int ldq, const void* k_cache, const void* v_cache,
                                 const int32_t* page_table, int table_ld, const int32_t* seq_lens,
                                 const float* k_scale, const float* v_scale, void* out, int ldo,
                                 int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
                                 float sm_scale, int num_ctas, okc_stream_t stream);
+
+/* Reads and clears the device error word of okc_attn_decode_fp8_noalloc on the current device
+ * once the work enqueued on `stream` is done (synchronises the stream; allocates nothing).
+ * Returns 0 (no error) or OKC_DEVERR_* bits, or a negative OKC_ERR_* code.  Like the entry
+ * point it belongs to, it has no counterpart in the reference. */
+int okc_attn_decode_fp8_noalloc_error(okc_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
  * MoE routing: logits = bf16(x · Wr^T) (fp32 sums in a fixed order: lane l of a warp sums

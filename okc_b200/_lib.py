@@ -70,6 +70,7 @@ SIGNATURES: dict[str, tuple] = {
                                              C.POINTER(_p), _p, _i, _p, _i, _i, _p, _p]),
     "okc_attn_decode_fp8_noalloc": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
                                          _i, _i, _i, _i, _i, _i64, _f, _i, _p]),
+    "okc_attn_decode_fp8_noalloc_error": (_i, [_p]),
     "okc_moe_route": (_i, [_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p]),
     "okc_moe_permute": (_i, [_p, _i, _i, _i, _i, _i, _p, _p, _p, _p, _i, _p]),
     "okc_moe_experts_workspace_bytes": (_sz, [_i, _i, _i, _i]),

@@ -12,9 +12,11 @@
 // GPU that loads this part of the library keeps it until the process exits.  It is shared
 // by every call on that device and keeps the last call's contents; calls that can overlap
 // on the GPU (different streams without ordering between them) race on it and must not be
-// issued.  The partials need no clearing (each call writes every entry it later reads); the
-// error word at its start is cleared by each call.  Requests whose partials do not fit are
-// rejected with OKC_ERR_TOO_LARGE.
+// issued.  The partials need no clearing (each call writes every entry it later reads).  The
+// error word at its start starts at zero (static device storage is zero-filled when the
+// library's module loads), collects the OKC_DEVERR_* bits of every call on the device, and is
+// read and cleared by okc_attn_decode_fp8_noalloc_error().  Requests whose partials do not fit
+// are rejected with OKC_ERR_TOO_LARGE.
 #include <mutex>
 
 #include "kernels.cuh"
@@ -58,8 +60,23 @@ extern "C" int okc_attn_decode_fp8_noalloc(const void* q, int ldq, const void* k
   if (need > kNoAllocScratchBytes) return OKC_ERR_TOO_LARGE;
   void* scratch = scratch_on_current_device();
   if (!scratch) return OKC_ERR_DEVICE;
-  if (cudaMemsetAsync(scratch, 0, sizeof(int), stream) != cudaSuccess) return OKC_ERR_LAUNCH;
   return okc_attn_decode_fp8(q, ldq, k_cache, v_cache, page_table, table_ld, seq_lens, k_scale, v_scale, out,
                              ldo, B, Hq, Hkv, D, page_size, num_pages, sm_scale, num_ctas, scratch,
                              kNoAllocScratchBytes, stream);
+}
+
+// Reads and clears the error word of the no-alloc scratch on the current device, after the
+// work already enqueued on `stream` (synchronises the stream).  The copy lands in a local
+// variable, so this allocates nothing either.
+extern "C" int okc_attn_decode_fp8_noalloc_error(okc_stream_t stream) {
+  void* scratch = scratch_on_current_device();
+  if (!scratch) return OKC_ERR_DEVICE;
+  int word = 0;
+  if (cudaMemcpyAsync(&word, scratch, sizeof(int), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaMemsetAsync(scratch, 0, sizeof(int), stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess) {
+    cudaGetLastError();
+    return OKC_ERR_LAUNCH;
+  }
+  return word;
 }

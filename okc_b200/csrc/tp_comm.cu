@@ -25,6 +25,9 @@
 
 namespace okc {
 
+// Payload pushed in place of a partial whose accumulation did not complete (quiet NaN).
+constexpr float kTpPoison = __builtin_nanf("");
+
 constexpr int kTpMaxRanks = 8;
 constexpr int kTpMaxCtas = 512;                     // per kernel: sizes the state and flag words
 constexpr int kTpStateExchange = 0;                 // state[0, 512): tp_allreduce_kernel CTA epochs
@@ -348,6 +351,7 @@ __global__ void __launch_bounds__(192, 1) tp_oproj_kernel(const __grid_constant_
     const int row = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const bool ok = mbar_wait(&accf[0], 0, a.err) && !*abort_flag;
+    if (!ok) *abort_flag = 1;  // read again by every epilogue thread in part 2
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (threadIdx.x == 64) s_tacc = globaltimer();
     if (S > 1) {
@@ -358,7 +362,7 @@ __global__ void __launch_bounds__(192, 1) tp_oproj_kernel(const __grid_constant_
         float v[16];
         tmem_ld16(tmem + lane_base + c_other + c0, v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) st_cluster_f32(dst + (uint32_t)(((c0 + j) * TC_BM + row) * 4), ok ? v[j] : 0.f);
+        for (int j = 0; j < 16; ++j) st_cluster_f32(dst + (uint32_t)(((c0 + j) * TC_BM + row) * 4), ok ? v[j] : kTpPoison);
       }
     }
   }
@@ -377,11 +381,20 @@ __global__ void __launch_bounds__(192, 1) tp_oproj_kernel(const __grid_constant_
     tp_stamp(st0, epoch, 2, s_tacc);
     tp_stamp(st0, epoch, 3, globaltimer());
     // ---------- epilogue part 2: finish the own half in shared memory, push the slices ----------
+    // An expired wait anywhere in this CTA (loads, MMAs, accumulator) leaves the accumulator
+    // incomplete: the slices are then pushed as NaN, so the peers (whose own error words stay
+    // clear) produce visibly invalid rows for this tile instead of a silently wrong sum, and
+    // nobody waits for flags that are never raised.
     const int c_own = part * C::HALF;
+    const bool acc_ok = !*abort_flag;
 #pragma unroll 1
     for (int c0 = 0; c0 < C::HALF; c0 += 16) {
       float v[16];
       tmem_ld16(tmem + lane_base + c_own + c0, v);
+      if (!acc_ok) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = kTpPoison;
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         float* sp = stage + (c0 + j) * TC_BM + row;

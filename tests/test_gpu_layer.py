@@ -78,3 +78,86 @@ def test_mid_size_layer_and_graph_replay():
     g.replay()  # same inputs: the append rewrites the same slots, so the step is idempotent
     torch.cuda.synchronize()
     _check(res, exp, "graph replay")
+
+
+def _compact_subset(table, kc, vc, seqs, need_pages):
+    """The pages of sequences `seqs` gathered into a small cache with a renumbered table, so
+    the CPU oracle runs on a few sequences of a full-size pool."""
+    rows, new_table = [], torch.full((len(seqs), table.shape[1]), -1, dtype=torch.int32)
+    off = 0
+    for i, b in enumerate(seqs):
+        n = need_pages[b]
+        rows.append(table[b, :n].long())
+        new_table[i, :n] = torch.arange(off, off + n, dtype=torch.int32)
+        off += n
+    idx = torch.cat(rows)
+    return new_table, kc[idx].cpu(), vc[idx].cpu()
+
+
+def test_decode_layer_full_shape_fused_branch_vs_oracle():
+    """The configuration the bench times: batch 128, hidden 8192, 64q/8kv, D128, ctx U[1024, 8192],
+    theta 5e5, P16, pool 2^17 pages.  B > 32 takes the tcgen05 QKV projection with RoPE + FP8
+    KV-append in its reduce, then attention, then the tcgen05 O projection with the residual.
+    Every stage is row-independent per token and attention is per sequence, so the CPU oracle
+    runs on 8 of the 128 sequences (their pages gathered into a compact cache).  Checks:
+      * out rows of those sequences within rtol 2e-2 / atol 2e-2 (and relative L2 < 1e-2);
+      * the set of cache rows the step changed is exactly the 128 oracle slots
+        table[b][pos // P] * P + pos % P (integer, bit-exact), in K and in V;
+      * the appended K/V codes of all 128 tokens against the oracle's append: equal codes for
+        >= 99 % of the elements and never more than one e4m3 step apart (the bf16 rounding of
+        the projection may fall on the other side of a code boundary)."""
+    from okc_b200 import synth
+    from okc_b200.layer import DecodeLayer, LayerConfig
+    from oracle import attention as oatt
+    c = synth.layer_case(B=128, seed=3, fill=False)
+    B, H, Hq, Hkv, D, P = 128, 8192, 64, 8, 128, 16
+    kc, vc, table, pos = c["k_cache"], c["v_cache"], c["page_table"], c["positions"]
+    ks, vs = c["k_scale"], c["v_scale"]
+    synth.fill_e4m3_normal(kc, torch.Generator(device="cuda").manual_seed(4), ks)
+    synth.fill_e4m3_normal(vc, torch.Generator(device="cuda").manual_seed(5), vs)
+    kc0, vc0 = kc.clone(), vc.clone()
+    cfg = LayerConfig(hidden=H, num_q_heads=Hq, num_kv_heads=Hkv, head_dim=D, rope_theta=c["theta"], eps=c["eps"],
+                      page_size=P)
+    layer = DecodeLayer(cfg, c["norm_w"], c["wqkv"], c["wo"], ks, vs)
+    assert B > 32, "this test covers the fused-QKV branch"
+    out = layer.step(c["x"], pos, table, kc, vc)
+    torch.cuda.synchronize()
+
+    # --- append slots: exactly the oracle's rows changed, nothing else ---
+    slots = oatt.cache_slots(table.cpu(), pos.cpu(), P)
+    for new, old in ((kc, kc0), (vc, vc0)):
+        changed = (new.view(torch.uint8).view(-1, Hkv * D) != old.view(torch.uint8).view(-1, Hkv * D)).any(-1)
+        got_rows = torch.nonzero(changed).reshape(-1).cpu()
+        assert torch.equal(torch.sort(got_rows).values, torch.sort(slots).values)
+    del kc0, vc0
+
+    # --- appended codes of all 128 tokens against the oracle's append into a scratch cache ---
+    xc, nw = c["x"].cpu(), c["norm_w"].cpu()
+    from oracle.projection import gemm, rmsnorm
+    qkv = gemm(rmsnorm(xc, nw, c["eps"]), c["wqkv"].cpu())
+    # the oracle's rows (kv_append's arithmetic: RoPE at the true position, e4m3(k / k_scale[h]))
+    _, k_r, v_r = oatt.split_qkv(qkv, Hq, Hkv, D)
+    k_r = oatt.rope(k_r, pos.cpu(), c["theta"])
+    kf = (k_r / ks.cpu()[None, :, None]).to(torch.float8_e4m3fn)
+    vf = (v_r / vs.cpu()[None, :, None]).to(torch.float8_e4m3fn)
+    for name, cache, exp_codes in (("K", kc, kf), ("V", vc, vf)):
+        got_codes = cache.view(-1, Hkv, D)[slots.cuda()].cpu()
+        same = (got_codes.view(torch.uint8) == exp_codes.view(torch.uint8)).float().mean().item()
+        assert same >= 0.99, f"{name}: only {same:.4f} of the appended codes equal"
+        # never more than one e4m3 step apart (3 mantissa bits; subnormal step 2^-9)
+        gf, ef = got_codes.float(), exp_codes.float()
+        mag = torch.maximum(gf.abs(), ef.abs())
+        step = torch.where(mag >= 2.0 ** -6, torch.exp2(torch.floor(torch.log2(mag.clamp_min(2.0 ** -6))) - 3),
+                           torch.full_like(mag, 2.0 ** -9))
+        assert bool(((gf - ef).abs() <= step).all()), f"{name}: appended codes more than one step apart"
+
+    # --- output rows of 8 sequences against the oracle on a compact cache ---
+    seqs = [0, 5, 17, 42, 63, 64, 100, 127]
+    need = [math.ceil((n + 1) / P) for n in c["lens"]]
+    # the compact cache holds the GPU's appended row at each slot; the oracle overwrites it with
+    # its own append before attending
+    t_sub, kc_sub, vc_sub = _compact_subset(table.cpu(), kc, vc, seqs, need)
+    idx = torch.tensor(seqs)
+    exp, _ = olayer.decode_layer(xc[idx], nw, c["wqkv"].cpu(), c["wo"].cpu(), pos.cpu()[idx], t_sub, kc_sub,
+                                 vc_sub, ks.cpu(), vs.cpu(), Hq, Hkv, D, c["theta"], c["eps"], D ** -0.5)
+    _check(out[idx.cuda()], exp, "full decode-layer shape, fused QKV branch")

@@ -261,7 +261,7 @@ def test_tp_oproj_fused_ranks(world, T, H, K):
         assert all(d == 0 for d in out["replica_diff"]), f"rank {rank}: replicas differ {out['replica_diff']}"
 
 
-def _layer_worker(rank, world, port, B, q):
+def _layer_worker(rank, world, port, B, q, Hq=32, Hkv=4):
     import datetime
 
     import torch.distributed as dist
@@ -273,7 +273,7 @@ def _layer_worker(rank, world, port, B, q):
         from okc_b200 import ops, synth
         from okc_b200.layer import DecodeLayer, LayerConfig
         from oracle import layer as olayer
-        H, Hq, Hkv, D, page = 4096, 32, 4, 128, 16
+        H, D, page = 4096, 128, 16
         g = torch.Generator(device="cuda").manual_seed(11)  # identical on every rank
         lens = [int(v) for v in torch.randint(16, 1500, (B,), generator=torch.Generator().manual_seed(2))]
         pool = sum((n + 1 + page - 1) // page for n in lens) + 8
@@ -314,16 +314,19 @@ def _layer_worker(rank, world, port, B, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("B", [8, 48])
-def test_tp_layer_two_ranks_vs_oracle(B):
-    """The decode layer at TP 2 (heads and KV cache split by rank, fused O projection + exchange)
-    against the CPU oracle of the whole layer; both ranks hold the same output bits."""
+@pytest.mark.parametrize("world,B,Hq,Hkv", [(2, 8, 32, 4), (2, 48, 32, 4), (4, 48, 32, 4), (4, 128, 64, 8),
+                                           (8, 48, 64, 8), (8, 128, 64, 8)])
+def test_tp_layer_vs_oracle(world, B, Hq, Hkv):
+    """The decode layer at TP 2, 4 and 8 (heads and KV cache split by rank, fused O projection +
+    exchange; B > 32 takes the fused QKV + RoPE/append branch) against the CPU oracle of the whole
+    layer; every rank holds the same output bits.  Runs when `world` GPUs are visible."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_layer_worker, args=(r, 2, port, B, q)) for r in range(2)]
+    procs = [ctx.Process(target=_layer_worker, args=(r, world, port, B, q, Hq, Hkv)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=600) for _ in procs], key=lambda t: t[0])
