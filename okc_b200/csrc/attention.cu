@@ -24,7 +24,7 @@
 //
 // Mirrors muse_attention_decode/submission.py:100-351 (tile loop, online softmax,
 // split partials and merge) and muse_prefill_layer/submission.py:137-176 (semantics).
-#include "kernels.cuh"
+#include "attention_common.cuh"
 
 namespace okc {
 
@@ -42,57 +42,6 @@ struct AttnCfg {
   static constexpr int THREADS = 9 * 32;
 };
 
-
-// ---------------------------------------------------------------------------------------
-// Balanced partition of U units over C CTAs: CTA c gets q or q+1 consecutive units.
-__host__ __device__ __forceinline__ void unit_range(int U, int C, int c, int& u0, int& u1) {
-  const int q = U / C, r = U % C;
-  u0 = c * q + (c < r ? c : r);
-  u1 = u0 + q + (c < r ? 1 : 0);
-}
-__host__ __device__ __forceinline__ int cta_of_unit(int U, int C, int u) {
-  const int q = U / C, r = U % C;
-  const int big = r * (q + 1);
-  return u < big ? u / (q + 1) : r + (u - big) / q;
-}
-
-// Exclusive prefix of per-sequence unit counts into prefix[0..B], by warp 0.
-__device__ __forceinline__ void unit_prefix(const int32_t* seq_lens, int B, int TS, int* prefix) {
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    int carry = 0;
-    for (int base = 0; base < B; base += 32) {
-      const int b = base + lane;
-      int len = b < B ? seq_lens[b] : 0;
-      if (len < 0) len = 0;
-      const int n = (len + TS - 1) / TS;
-      int v = n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += t;
-      }
-      if (b < B) prefix[b] = carry + v - n;
-      carry += __shfl_sync(0xffffffffu, v, 31);
-    }
-    if (lane == 0) prefix[B] = carry;
-  }
-}
-
-__device__ __forceinline__ int find_seq(const int* prefix, int B, int u) {
-  int lo = 0, hi = B - 1;  // largest b with prefix[b] <= u
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (prefix[mid] <= u) lo = mid; else hi = mid - 1;
-  }
-  return lo;
-}
-
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 // 4x4 byte transpose: out_i = (w0.byte_i, w1.byte_i, w2.byte_i, w3.byte_i).
 __device__ __forceinline__ void transpose4x4(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3,
@@ -141,7 +90,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
     fence_mbar_init();
   }
   pdl_wait();
-  unit_prefix(a.seq_lens, a.B, C::TS, prefix);
+  unit_prefix(a.seq_lens, a.B, C::TS, a.window, 1, prefix);
   __syncthreads();
   if (blockIdx.x == 0)  // for the merge kernel
     for (int i = threadIdx.x; i <= a.B; i += blockDim.x) a.ws_prefix[i] = prefix[i];
@@ -156,22 +105,23 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
     // The page-table entries of unit u+1 are loaded (lane sg: the unit's sg-th page span)
     // while unit u waits for its ring slot, so the lookup latency is off the critical path.
     const uint64_t pol = l2_evict_first_policy();
-    struct Span { int b, t0, t_end, p_first, nseg, page; };
+    struct Span { int row, t0, t_end, p_first, nseg, page; };
     auto lookup = [&](int u, int bb) {
       Span f;
-      f.b = bb;
-      f.t0 = (u - prefix[bb]) * C::TS;
-      f.t_end = min(a.seq_lens[bb], f.t0 + C::TS);
+      const int len = a.seq_lens[bb];
+      f.row = bb / a.q_per_seq;
+      f.t0 = seq_origin(len, a.window, 1) + (u - prefix[bb]) * C::TS;
+      f.t_end = min(len, f.t0 + C::TS);
       f.p_first = f.t0 / a.P;
       f.nseg = (f.t_end - 1) / a.P - f.p_first + 1;
       const int lp = f.p_first + lane;
-      f.page = (lane < f.nseg && lp < a.table_ld) ? a.page_table[(size_t)bb * a.table_ld + lp] : -1;
+      f.page = (lane < f.nseg && lp < a.table_ld) ? a.page_table[(size_t)f.row * a.table_ld + lp] : -1;
       return f;
     };
     auto page_of = [&](const Span& f, int sg) {
       if (sg < 32) return f.page;  // (lane == sg)
       const int lp = f.p_first + sg;
-      return lp < a.table_ld ? a.page_table[(size_t)f.b * a.table_ld + lp] : -1;
+      return lp < a.table_ld ? a.page_table[(size_t)f.row * a.table_ld + lp] : -1;
     };
     int b = find_seq(prefix, a.B, u0);
     int stage = 0;
@@ -343,7 +293,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
       cur_b = b;
     }
     const int len = a.seq_lens[b];
-    const int tb = (u - prefix[b]) * C::TS + sub * 32;
+    const int tb = seq_origin(len, a.window, 1) + (u - prefix[b]) * C::TS + sub * 32;
     const int valid = min(32, max(0, len - tb));
 
     bool ok = mbar_wait(&full[stage], phase, a.err);
@@ -659,11 +609,16 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
   }
   int st = okc_host::launch_k(attn_decode_kernel<D, HKV>, dim3(a.num_ctas), dim3(C::THREADS), smem, stream, dim3(1), a);
   if (st) return st;
-  return okc_host::launch_k(attn_merge_kernel, dim3(a.B, (a.Hq + 7) / 8), dim3(256), 0, stream, dim3(1), a,
-                            (int)C::TS, (int)C::NSUB, D);
+  return launch_attn_merge(a, C::TS, C::NSUB, D, stream);
+}
+
+int launch_attn_merge(AttnArgs& a, int TS, int NSUB, int D, cudaStream_t stream) {
+  return okc_host::launch_k(attn_merge_kernel, dim3(a.B, (a.Hq + 7) / 8), dim3(256), 0, stream, dim3(1), a, TS,
+                            NSUB, D);
 }
 
 int launch_attn_decode(AttnArgs& a, int D, int Hkv, cudaStream_t stream) {
+  if (attn_tc_eligible(a, D, Hkv)) return launch_attn_tc(a, Hkv, stream);
   if (D == 128) {
     switch (Hkv) {
       case 1: return launch_attn_t<128, 1>(a, stream);

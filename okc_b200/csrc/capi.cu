@@ -221,6 +221,8 @@ int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const
   a.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
   a.ld_gate = ld_gate;
   a.out_eps = out_eps;
+  a.window = 0;
+  a.q_per_seq = 1;
   return okc::launch_attn_decode(a, D, Hkv, stream);
 }
 

@@ -64,15 +64,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Returns false (and sets
-// OKC_DEVERR_TIMEOUT in *err) if it did not complete within kWaitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// OKC_DEVERR_TIMEOUT in *err) if it did not complete within kWaitNs.  With `abort` given, it
+// also returns false (at once, or within 256 polls) once *abort is non-zero: a CTA whose other
+// role gave up stops waiting for work that will never arrive.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          const volatile int* abort = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
+  if (abort && *abort) return false;
   const unsigned long long t0 = globaltimer();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && globaltimer() - t0 > kWaitNs) {
-      atomicOr(err, OKC_DEVERR_TIMEOUT);
-      return false;
+    if ((it & 255u) == 255u) {
+      if (abort && *abort) return false;
+      if (globaltimer() - t0 > kWaitNs) {
+        atomicOr(err, OKC_DEVERR_TIMEOUT);
+        return false;
+      }
     }
   }
 }

@@ -30,6 +30,8 @@ struct AttnArgs {
   const __nv_bfloat16* gate;  // optional output gate (Muse): out = rms(o) * sigmoid(gate)
   int ld_gate;
   float out_eps;
+  int window;     // sliding window in tokens (0: the whole context)
+  int q_per_seq;  // query tokens per request (verify blocks): sequence b reads table row b / q_per_seq
 };
 
 // cuTensorMapEncodeTiled from the driver (nullptr when unavailable); cached.

@@ -43,10 +43,18 @@ def _check(out, exp, what, lens=None):
     assert rel < 1e-2, f"{what}: rel L2 {rel:.2e}"
 
 
+@pytest.fixture(params=["tc", "mma"])
+def kernel(request, monkeypatch):
+    """Both decode kernels: the tcgen05 one (OKC_ATTN_TC=1; head_dim 128, pages 16..128, 2..8 KV
+    heads, the mma.sync kernel otherwise) and the mma.sync one (every shape, the default)."""
+    monkeypatch.setenv("OKC_ATTN_TC", "1" if request.param == "tc" else "0")
+    return request.param
+
+
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("Hkv,G", [(8, 8), (4, 8), (2, 8), (1, 8), (8, 4), (2, 3)])
 @pytest.mark.parametrize("page", [16, 1, 64])
-def test_decode_shapes(ops, D, Hkv, G, page):
+def test_decode_shapes(ops, kernel, D, Hkv, G, page):
     lens = [37, 200, 1, 512, 33, 1000]
     Hq = Hkv * G
     pool = sum(math.ceil(n / page) for n in lens) + 7
@@ -57,7 +65,7 @@ def test_decode_shapes(ops, D, Hkv, G, page):
     assert ops.read_device_error("attn") == 0
 
 
-def test_bad_page_id_is_flagged_not_faulted(ops):
+def test_bad_page_id_is_flagged_not_faulted(ops, kernel):
     """A page-table entry outside [0, num_pages) is skipped by the copy engine and reported in
     the workspace error word; the sequences whose pages are valid stay correct."""
     lens = [40, 300, 17]
@@ -76,7 +84,7 @@ def test_bad_page_id_is_flagged_not_faulted(ops):
 
 
 @pytest.mark.parametrize("num_ctas", [1, 3, 148, 400])
-def test_stream_k_partitions(ops, num_ctas):
+def test_stream_k_partitions(ops, kernel, num_ctas):
     lens = [5000, 17, 64, 0, 2049, 31, 32, 96]
     page, D, Hkv, Hq = 16, 128, 8, 64
     pool = sum(math.ceil(max(n, 1) / page) for n in lens) + 3
@@ -87,7 +95,7 @@ def test_stream_k_partitions(ops, num_ctas):
     assert torch.all(out[3].float() == 0), "an empty sequence yields zeros"
 
 
-def test_peaked_scores_and_graph_replay(ops):
+def test_peaked_scores_and_graph_replay(ops, kernel):
     # large-magnitude queries make the softmax nearly one-hot: stresses the max tracking
     lens = [700, 1500, 3]
     page, D, Hkv, Hq = 16, 128, 8, 64
@@ -114,7 +122,7 @@ def test_peaked_scores_and_graph_replay(ops):
     _check(out, exp2, "graph replay with fresh q")
 
 
-def test_baseline_c3_subset(ops):
+def test_baseline_c3_subset(ops, kernel):
     """The attention-decode workload at full size (B64, 64q/8kv, D128, ctx U[512, 32768], P16, pool 2^17);
     the oracle checks a subset of the sequences (CPU time), the rest through a property:
     every output row is a convex combination of V rows, so |out| <= max|V| * v_scale."""
