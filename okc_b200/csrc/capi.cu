@@ -170,7 +170,7 @@ size_t okc_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int num_ct
   const size_t nsub = Hkv >= 8 ? 1 : 8 / Hkv;
   const size_t rows = (size_t)(num_ctas + B) * nsub * Hq;
   return 256 + ((rows * 2 * 4 + 255) / 256) * 256 + ((rows * D * 4 + 255) / 256) * 256 +
-         (((size_t)B + 1) * 4 + 255) / 256 * 256;
+         (((size_t)B + 1) * 4 + 255) / 256 * 256 + (okc::attn_q8_ws_bytes(B, Hkv) + 255) / 256 * 256;
 }
 
 int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const void* v_cache,
@@ -211,6 +211,8 @@ int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const
   a.ws_ml = reinterpret_cast<float*>(ws + 256);
   a.ws_acc = reinterpret_cast<float*>(ws + 256 + ((rows * 2 * 4 + 255) / 256) * 256);
   a.ws_prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a.ws_acc) + ((rows * D * 4 + 255) / 256) * 256);
+  a.ws_q8 = reinterpret_cast<uint8_t*>(a.ws_prefix) + (((size_t)B + 1) * 4 + 255) / 256 * 256;
+  a.ws_qf = reinterpret_cast<float*>(a.ws_q8 + (size_t)B * Hkv * 2048);
   a.B = B;
   a.Hq = Hq;
   a.G = Hq / Hkv;

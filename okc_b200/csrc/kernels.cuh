@@ -32,7 +32,10 @@ struct AttnArgs {
   float out_eps;
   int window;     // sliding window in tokens (0: the whole context)
   int q_per_seq;  // query tokens per request (verify blocks): sequence b reads table row b / q_per_seq
+  uint8_t* ws_q8; // [B][Hkv][16][128] two-term e4m3 queries (tcgen05 kernel)
+  float* ws_qf;   // [B][Hkv][8] their per-row scales
 };
+size_t attn_q8_ws_bytes(int B, int Hkv);
 
 // cuTensorMapEncodeTiled from the driver (nullptr when unavailable); cached.
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
