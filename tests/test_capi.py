@@ -58,7 +58,8 @@ def test_workspace_queries(lib):
     n = lib.okc_attn_decode_workspace_bytes(64, 64, 8, 128, 148)
     rows = (148 + 64) * 1 * 64
     assert n == (256 + ((rows * 8 + 255) // 256) * 256 + ((rows * 128 * 4 + 255) // 256) * 256
-                 + ((64 + 1) * 4 + 255) // 256 * 256)  # + the unit prefix for the merge
+                 + ((64 + 1) * 4 + 255) // 256 * 256   # + the unit prefix for the merge
+                 + (64 * 8 * (2048 + 32) + 255) // 256 * 256)  # + two-term e4m3 queries and scales
     assert lib.okc_attn_decode_workspace_bytes(8, 8, 1, 128, 10) > lib.okc_attn_decode_workspace_bytes(8, 8, 8, 128, 10)
     assert lib.okc_moe_experts_workspace_bytes(256, 8, 4096, 1536) > 256
 
