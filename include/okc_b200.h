@@ -167,6 +167,22 @@ int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const
                               float out_eps, void* workspace, size_t workspace_bytes,
                               okc_stream_t stream);
 
+/* okc_attn_decode_fp8_gated with Muse's sliding-window layers and speculative-verify blocks
+ * (muse_attention_decode/submission.py:191-351, 409-439; the mask of
+ * muse_prefill_layer/submission.py:169-171): a query at position p attends the cached
+ * positions (p - window, p] (window = 0: [0, p]).  A verify block of q_per_seq query tokens per
+ * request is passed as q_per_seq consecutive rows of q / out / seq_lens per request, row i
+ * of request r having seq_lens = (its position + 1) and reading page-table row r (so B is
+ * requests * q_per_seq and page_table has B / q_per_seq rows).  window = 0 and q_per_seq = 1
+ * give okc_attn_decode_fp8_gated. */
+int okc_attn_decode_fp8_ex(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                           const int32_t* page_table, int table_ld, const int32_t* seq_lens,
+                           const float* k_scale, const float* v_scale, void* out, int ldo,
+                           int B, int Hq, int Hkv, int D, int page_size, int64_t num_pages,
+                           float sm_scale, int num_ctas, int window, int q_per_seq,
+                           const void* gate, int ld_gate, float out_eps,
+                           void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
 /* Same computation as okc_attn_decode_fp8, for callers that cannot allocate device memory
  * (no counterpart in the reference, whose operators allocate their scratch per call).  The
  * split-KV partials live in a fixed 16 MiB array inside the library, so the caller passes only

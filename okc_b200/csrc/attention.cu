@@ -419,42 +419,36 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
 }
 
 // ---------------------------------------------------------------------------------------
-// Merge: out[b, hq, :] = v_scale[h] * sum_parts 2^(m_i - M) acc_i / sum_parts 2^(m_i - M) l_i.
-// One warp per (sequence, query head); lane owns D/32 consecutive d.  Parts are read in a
-// fixed order, so the result does not depend on which CTA finished first.
-__global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int NSUB, int D) {
-  pdl_trigger();
-  pdl_wait();
-  const int b = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hq = blockIdx.y * 8 + warp;
-  if (hq >= a.Hq) return;
+// Merge of one (sequence b, query head hq): out = v_scale[h] * sum_parts 2^(m_i - M) acc_i /
+// sum_parts 2^(m_i - M) l_i over the split-KV partials of the CTAs that covered b (units
+// [uf, ul] of U over C CTAs; NSUB sub-tiles per unit), by one warp, lane owning D/32
+// consecutive d.  Parts are read in a fixed order (and through L2: they may come from other
+// SMs of the running grid), so the result does not depend on which CTA finished first.
+__device__ void merge_row(const AttnArgs& a, int b, int hq, int U, int uf, int ul, int NSUB, int D, int lane) {
   const int per = D / 32;  // 4 (D = 128) or 2 (D = 64)
   __nv_bfloat16* dst = a.out + (size_t)b * a.ldo + (size_t)hq * D + lane * per;
-  const int U = a.ws_prefix[a.B];  // unit prefix from the attention kernel
-  const int uf = a.ws_prefix[b], ul = a.ws_prefix[b + 1] - 1;
   float o[4] = {0.f, 0.f, 0.f, 0.f};
   float L = 0.f;
   if (ul >= uf) {
     const int cf = cta_of_unit(U, a.num_ctas, uf), cl = cta_of_unit(U, a.num_ctas, ul);
     const int nparts = (cl - cf + 1) * NSUB;
     auto row_of = [&](int p) { return ((size_t)(cf + p / NSUB + b) * NSUB + p % NSUB) * a.Hq + hq; };
-    // Batches of 16 parts: the (m, l) of part p0 + i sit in lane i, and the 16 parts' slices
+    // Batches of 8 parts: the (m, l) of part p0 + i sit in lane i, and the 8 parts' slices
     // of acc are loaded in the same round, so one batch costs one memory round trip.  A
     // running maximum carries the log-sum-exp across batches.
     float M = -INFINITY;
-    for (int p0 = 0; p0 < nparts; p0 += 16) {
-      const int n = min(16, nparts - p0);
+    for (int p0 = 0; p0 < nparts; p0 += 8) {
+      const int n = min(8, nparts - p0);
       float2 ml = make_float2(-INFINITY, 0.f);
-      if (lane < n) ml = *reinterpret_cast<const float2*>(a.ws_ml + row_of(p0 + lane) * 2);
-      float4 v[16];
+      if (lane < n) ml = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + row_of(p0 + lane) * 2));
+      float4 v[8];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 8; ++i) {
         v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (i < n) {
           const float* src = a.ws_acc + row_of(p0 + i) * D + lane * per;
-          if (per == 4) v[i] = *reinterpret_cast<const float4*>(src);
-          else { const float2 t = *reinterpret_cast<const float2*>(src); v[i].x = t.x; v[i].y = t.y; }
+          if (per == 4) v[i] = __ldcg(reinterpret_cast<const float4*>(src));
+          else { const float2 t = __ldcg(reinterpret_cast<const float2*>(src)); v[i].x = t.x; v[i].y = t.y; }
         }
       }
       const float Mn = fmaxf(M, warp_max(ml.x));
@@ -468,7 +462,7 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int
       const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
       L += w * ml.y;  // per lane; summed over the warp at the end
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
+      for (int i = 0; i < 8; ++i) {
         const float wi = __shfl_sync(0xffffffffu, w, i);
         o[0] += wi * v[i].x; o[1] += wi * v[i].y; o[2] += wi * v[i].z; o[3] += wi * v[i].w;
       }
@@ -500,6 +494,17 @@ __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int
   } else {
     *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
   }
+}
+
+// The merge kernel: one warp per (sequence, query head), after the whole decode grid.
+__global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int NSUB, int D) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hq = blockIdx.y * 8 + warp;
+  if (hq >= a.Hq) return;
+  merge_row(a, b, hq, a.ws_prefix[a.B], a.ws_prefix[b], a.ws_prefix[b + 1] - 1, NSUB, D, lane);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -164,6 +164,9 @@ int okc_gemm_bf16_rope_kv_append(const void* x, int ldx, const void* w, int ldw,
 }
 
 // ------------------------------------------------------------------------ attention
+// Workspace of the decode kernels: [error word | (m, l) partials | output partials | unit
+// prefix | two-term e4m3 queries + scales].
+
 size_t okc_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int num_ctas) {
   if (num_ctas <= 0) num_ctas = okc_host::num_sms();
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0) return 0;
@@ -173,17 +176,18 @@ size_t okc_attn_decode_workspace_bytes(int B, int Hq, int Hkv, int D, int num_ct
          (((size_t)B + 1) * 4 + 255) / 256 * 256 + (okc::attn_q8_ws_bytes(B, Hkv) + 255) / 256 * 256;
 }
 
-int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const void* v_cache,
-                              const int32_t* page_table, int table_ld, const int32_t* seq_lens,
-                              const float* k_scale, const float* v_scale, void* out, int ldo, int B, int Hq,
-                              int Hkv, int D, int page_size, int64_t num_pages, float sm_scale, int num_ctas,
-                              const void* gate, int ld_gate, float out_eps, void* workspace,
-                              size_t workspace_bytes, okc_stream_t stream) {
+int okc_attn_decode_fp8_ex(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                           const int32_t* page_table, int table_ld, const int32_t* seq_lens,
+                           const float* k_scale, const float* v_scale, void* out, int ldo, int B, int Hq,
+                           int Hkv, int D, int page_size, int64_t num_pages, float sm_scale, int num_ctas,
+                           int window, int q_per_seq, const void* gate, int ld_gate, float out_eps,
+                           void* workspace, size_t workspace_bytes, okc_stream_t stream) {
   if (gate && (ld_gate < Hq * D || (reinterpret_cast<uintptr_t>(gate) & 1))) return OKC_ERR_INVALID;
   if (!q || !k_cache || !v_cache || !page_table || !seq_lens || !k_scale || !v_scale || !out)
     return OKC_ERR_INVALID;
   if (B <= 0 || B > 4096 || Hkv <= 0 || Hq % Hkv || Hq / Hkv > 8 || table_ld <= 0 || num_pages <= 0)
     return OKC_ERR_INVALID;
+  if (window < 0 || q_per_seq <= 0 || B % q_per_seq) return OKC_ERR_INVALID;
   if (!(D == 64 || D == 128) || !(Hkv == 1 || Hkv == 2 || Hkv == 4 || Hkv == 8)) return OKC_ERR_INVALID;
   if (page_size <= 0 || !((32 % page_size) == 0 || (page_size % 32) == 0)) return OKC_ERR_INVALID;
   if (ldq % 8 || ldo % 8 || ldq < Hq * D || ldo < Hq * D) return OKC_ERR_INVALID;
@@ -192,6 +196,7 @@ int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const
   if (num_ctas <= 0) num_ctas = okc_host::num_sms();
   const size_t need = okc_attn_decode_workspace_bytes(B, Hq, Hkv, D, num_ctas);
   if (!workspace || workspace_bytes < need) return OKC_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(workspace) & 15) return OKC_ERR_ALIGNMENT;
   const size_t nsub = Hkv >= 8 ? 1 : 8 / Hkv;
   const size_t rows = (size_t)(num_ctas + B) * nsub * Hq;
   uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
@@ -209,7 +214,7 @@ int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const
   a.ldo = ldo;
   a.err = reinterpret_cast<int*>(ws);
   a.ws_ml = reinterpret_cast<float*>(ws + 256);
-  a.ws_acc = reinterpret_cast<float*>(ws + 256 + ((rows * 2 * 4 + 255) / 256) * 256);
+  a.ws_acc = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(a.ws_ml) + ((rows * 2 * 4 + 255) / 256) * 256);
   a.ws_prefix = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(a.ws_acc) + ((rows * D * 4 + 255) / 256) * 256);
   a.ws_q8 = reinterpret_cast<uint8_t*>(a.ws_prefix) + (((size_t)B + 1) * 4 + 255) / 256 * 256;
   a.ws_qf = reinterpret_cast<float*>(a.ws_q8 + (size_t)B * Hkv * 2048);
@@ -223,9 +228,20 @@ int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const
   a.gate = reinterpret_cast<const __nv_bfloat16*>(gate);
   a.ld_gate = ld_gate;
   a.out_eps = out_eps;
-  a.window = 0;
-  a.q_per_seq = 1;
+  a.window = window;
+  a.q_per_seq = q_per_seq;
   return okc::launch_attn_decode(a, D, Hkv, stream);
+}
+
+int okc_attn_decode_fp8_gated(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                              const int32_t* page_table, int table_ld, const int32_t* seq_lens,
+                              const float* k_scale, const float* v_scale, void* out, int ldo, int B, int Hq,
+                              int Hkv, int D, int page_size, int64_t num_pages, float sm_scale, int num_ctas,
+                              const void* gate, int ld_gate, float out_eps, void* workspace,
+                              size_t workspace_bytes, okc_stream_t stream) {
+  return okc_attn_decode_fp8_ex(q, ldq, k_cache, v_cache, page_table, table_ld, seq_lens, k_scale, v_scale, out,
+                                ldo, B, Hq, Hkv, D, page_size, num_pages, sm_scale, num_ctas, 0, 1, gate, ld_gate,
+                                out_eps, workspace, workspace_bytes, stream);
 }
 
 int okc_attn_decode_fp8(const void* q, int ldq, const void* k_cache, const void* v_cache,

@@ -173,10 +173,14 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                 page_table: torch.Tensor, seq_lens: torch.Tensor, k_scale: torch.Tensor,
                 v_scale: torch.Tensor, sm_scale: float, out: torch.Tensor | None = None,
                 num_ctas: int = 0, gate: torch.Tensor | None = None,
-                out_eps: float = 1e-5) -> torch.Tensor:
+                out_eps: float = 1e-5, window: int = 0, q_per_seq: int = 1) -> torch.Tensor:
     """Paged FP8 decode attention.  q bf16 [B, Hq, D]; caches e4m3 [pages, P, Hkv, D];
-    page_table int32 [B, max_pages]; seq_lens int32 [B]; scales fp32 [Hkv].  With `gate`
-    (bf16 [B, >= Hq*D], Muse's output gate) the result is rms(o) * sigmoid(gate) per head."""
+    page_table int32 [B / q_per_seq, max_pages]; seq_lens int32 [B]; scales fp32 [Hkv].  With
+    `gate` (bf16 [B, >= Hq*D], Muse's output gate) the result is rms(o) * sigmoid(gate) per
+    head.  `window` > 0 restricts a query at position p to the cached positions (p - window, p];
+    `q_per_seq` > 1 treats consecutive groups of that many rows as the query tokens of one
+    request (a verify block), each row with its own seq_lens (position + 1) and the request's
+    page-table row."""
     dev = _dev_index(q)
     _need(q, torch.bfloat16, "q")
     B, Hq, D = q.shape
@@ -192,12 +196,12 @@ def attn_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
     lib = _lib.load()
     nbytes = lib.okc_attn_decode_workspace_bytes(B, Hq, Hkv, D, num_ctas)
     ws = workspace(dev, "attn", nbytes)
-    st = lib.okc_attn_decode_fp8_gated(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
-                                       page_table.data_ptr(), page_table.stride(0), seq_lens.data_ptr(),
-                                       k_scale.data_ptr(), v_scale.data_ptr(), out.data_ptr(), out.stride(0),
-                                       B, Hq, Hkv, D, P, pages, float(sm_scale), num_ctas, _ptr(gate),
-                                       0 if gate is None else gate.stride(0), float(out_eps),
-                                       ws.data_ptr(), ws.numel(), _stream(dev))
+    st = lib.okc_attn_decode_fp8_ex(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                    page_table.data_ptr(), page_table.stride(0), seq_lens.data_ptr(),
+                                    k_scale.data_ptr(), v_scale.data_ptr(), out.data_ptr(), out.stride(0),
+                                    B, Hq, Hkv, D, P, pages, float(sm_scale), num_ctas, int(window),
+                                    int(q_per_seq), _ptr(gate), 0 if gate is None else gate.stride(0),
+                                    float(out_eps), ws.data_ptr(), ws.numel(), _stream(dev))
     check(st, "okc_attn_decode_fp8")
     return out
 

@@ -78,10 +78,13 @@ def kv_append(qkv: torch.Tensor, positions: torch.Tensor, page_table: torch.Tens
 
 def attend(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, page_table: torch.Tensor,
            seq_lens: torch.Tensor, k_scale: torch.Tensor, v_scale: torch.Tensor,
-           sm_scale: float) -> torch.Tensor:
-    """Decode attention of one query token per sequence over its first seq_lens[b] cached
-    keys: rows = table[b][t // P] * P + t % P, K = e4m3 * k_scale[h], V = e4m3 * v_scale[h],
-    softmax(q K^T * sm_scale) V with GQA grouping q.view(Hkv, G, D)
+           sm_scale: float, window: int = 0, q_per_seq: int = 1) -> torch.Tensor:
+    """Decode attention of one query token per row over its visible cached keys: positions
+    [n - window, n) for n = seq_lens[b] (all of [0, n) when window = 0: the causal / sliding-
+    window mask `t <= pos` and `t > pos - window` of muse_prefill_layer/submission.py:168-171,
+    with n = pos + 1), rows = table[b // q_per_seq][t // P] * P + t % P (q_per_seq query tokens
+    of a verify block share their request's table row), K = e4m3 * k_scale[h],
+    V = e4m3 * v_scale[h], softmax(q K^T * sm_scale) V with GQA grouping q.view(Hkv, G, D)
     (muse_prefill_layer/submission.py:158-175; bench_tail.py:97-105).
     q [B, Hq, D] (any float dtype, used as given); returns fp32 [B, Hq, D]."""
     B, hq, d = q.shape
@@ -94,10 +97,11 @@ def attend(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, page_t
     out = torch.zeros((B, hq, d), dtype=torch.float32)
     for b in range(B):
         n = int(seq_lens[b])
-        if n <= 0:
+        lo = max(0, n - window) if window else 0
+        if n <= lo:
             continue
-        t = torch.arange(n)
-        rows = page_table[b].long()[t // page] * page + t % page
+        t = torch.arange(lo, n)
+        rows = page_table[b // q_per_seq].long()[t // page] * page + t % page
         keys = kf[rows].float() * ks
         vals = vf[rows].float() * vs
         att = torch.einsum("kgd,tkd->kgt", q[b].float().view(hkv, g, d), keys) * sm_scale
@@ -107,23 +111,30 @@ def attend(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, page_t
 
 def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, page_table: torch.Tensor,
            seq_lens: torch.Tensor, k_scale: torch.Tensor, v_scale: torch.Tensor,
-           sm_scale: float) -> torch.Tensor:
+           sm_scale: float, window: int = 0, q_per_seq: int = 1) -> torch.Tensor:
     """attend() rounded to the bf16 output boundary."""
-    return attend(q, k_cache, v_cache, page_table, seq_lens, k_scale, v_scale, sm_scale).to(torch.bfloat16)
+    return attend(q, k_cache, v_cache, page_table, seq_lens, k_scale, v_scale, sm_scale, window,
+                  q_per_seq).to(torch.bfloat16)
 
 
 def muse_attention(qkv: torch.Tensor, positions: torch.Tensor, page_table: torch.Tensor,
                    k_cache: torch.Tensor, v_cache: torch.Tensor, k_scale: torch.Tensor,
                    v_scale: torch.Tensor, cfg: dict) -> torch.Tensor:
-    """The reference's full gated decode attention for q_len = 1 (muse_prefill_layer/
-    submission.py:137-176 with window 0): QK-RMSNorm, RoPE, queries rounded to bf16 after the
-    scale factor, FP8 append, attention over positions <= pos, then RMSNorm(out) * sigmoid(gate).
-    qkv [B, (2hq + 2hkv) d] holds q | k | v | gate.  Mutates the caches; returns bf16 [B, hq*d]."""
+    """The reference's gated decode attention (muse_prefill_layer/submission.py:137-176) for
+    q_len L tokens per request (1: decode, 8: a verify block) and sliding window cfg["window"]
+    (0: full): QK-RMSNorm, RoPE, queries rounded to bf16 after the scale factor, FP8 append of
+    every block token (request r's tokens are rows r*L .. r*L + L - 1, its table row r), then each
+    token attends positions (pos - window, pos], then RMSNorm(out) * sigmoid(gate).
+    qkv [B*L, (2hq + 2hkv) d] holds q | k | v | gate.  Mutates the caches; returns bf16
+    [B*L, hq*d]."""
     hq, hkv, d = cfg["num_q_heads"], cfg["num_kv_heads"], cfg["head_dim"]
-    q, _ = kv_append(qkv, positions, page_table, k_cache, v_cache, k_scale, v_scale, hq, hkv, d,
+    L = cfg.get("q_len", 1)
+    table_rows = page_table.repeat_interleave(L, dim=0) if L > 1 else page_table
+    q, _ = kv_append(qkv, positions, table_rows, k_cache, v_cache, k_scale, v_scale, hq, hkv, d,
                      cfg["rope_theta"], muse=True)
     q = (q * cfg["qk_scale_factor"]).to(torch.bfloat16)
     gate = qkv.float()[:, (hq + 2 * hkv) * d:]
     lens = positions.long() + 1
-    o = attend(q, k_cache, v_cache, page_table, lens, k_scale, v_scale, cfg["sm_scale"])
+    o = attend(q, k_cache, v_cache, page_table, lens, k_scale, v_scale, cfg["sm_scale"],
+               window=cfg.get("window", 0), q_per_seq=L)
     return (rms(o).reshape(-1, hq * d) * torch.sigmoid(gate)).to(torch.bfloat16)

@@ -8,7 +8,8 @@ Needs a checkout of the reference, named by $OKC_REFERENCE, and runs on CPU:
                      grid of muse_decode_layer/tests/test_nvfp4_gemv.py:56-69).
   route_perm.json    the Triton `_route` kernel of muse_moe_w4a16/submission.py:274-291 run under
                      Triton's CPU interpreter: per-expert pair lists, counts and tile tables.
-  prefill_ops.pt     `rms`, `rope`, `route` and the gated decode `attention` of
+  prefill_ops.pt     `rms`, `rope`, `route` and the gated decode `attention` (q_len 1 and 8,
+                     full and sliding-window layers) of
                      muse_prefill_layer/submission.py (its `nvfp4` import is stubbed: the
                      attention path never calls it), on small seeded inputs.
 
@@ -175,6 +176,34 @@ def prefill_ops():
         cases.append({"cfg": cfg, "x": x_in, "wqkv": wqkv, "table": table, "positions": positions,
                       "cache_loc": cache_loc, "k_cache_in": kc0, "v_cache_in": vc0, "k_cache_out": kc,
                       "v_cache_out": vc, "kv_scale": kv_scale, "out": o})
+    # sliding-window layers and speculative-verify blocks (q_len 8: every block token attends the
+    # cache and the block up to its own position), with the reference's own attention()
+    for page, kv_scale, theta, window, L, seed in [(16, 1.0, 500000.0, 16, 1, 4), (4, 0.5, 10000.0, 0, 8, 5),
+                                                    (1, 1 / 64, 500000.0, 20, 8, 6)]:
+        gg = torch.Generator().manual_seed(seed)
+        B, hq, hkv, d, hidden = 3, 16, 2, 64, 64
+        seq = torch.tensor([5, 37, 60])
+        max_pages = (int(seq.max()) + L + page - 1) // page
+        pages = B * max_pages
+        perm = torch.randperm(pages, generator=gg).to(torch.int32)
+        table = perm.view(B, max_pages).clone()
+        kc = (torch.randn((pages, page, hkv, d), generator=gg) / kv_scale).to(torch.float8_e4m3fn)
+        vc = (torch.randn((pages, page, hkv, d), generator=gg) / kv_scale).to(torch.float8_e4m3fn)
+        x_in = torch.randn((B * L, hidden), generator=gg).to(torch.bfloat16)
+        wqkv = (torch.randn(((2 * hq + 2 * hkv) * d, hidden), generator=gg) * 0.05).to(torch.bfloat16)
+        positions = (seq[:, None] + torch.arange(L)).reshape(-1).long()
+        rows = torch.arange(B).repeat_interleave(L)
+        cache_loc = table.long()[rows, positions // page] * page + positions % page
+        cfg = {"batch": B, "q_len": L, "num_q_heads": hq, "num_kv_heads": hkv, "head_dim": d,
+               "page_size": page, "window": window, "rope_theta": theta, "qk_scale_factor": 5.4730064863875,
+               "sm_scale": 0.125}
+        kc0, vc0 = kc.clone(), vc.clone()
+        data = {"config": cfg, "positions": positions, "page_table": table, "cache_loc": cache_loc,
+                "k_cache": kc, "v_cache": vc, "k_scale": torch.tensor(kv_scale), "v_scale": torch.tensor(kv_scale)}
+        o = ref.attention(data, x_in, {"qkv_gate": wqkv})
+        cases.append({"cfg": cfg, "x": x_in, "wqkv": wqkv, "table": table, "positions": positions,
+                      "seq_lens": seq.to(torch.int32), "cache_loc": cache_loc, "k_cache_in": kc0,
+                      "v_cache_in": vc0, "k_cache_out": kc, "v_cache_out": vc, "kv_scale": kv_scale, "out": o})
     out["attention_cases"] = cases
     return out
 

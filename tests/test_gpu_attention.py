@@ -65,6 +65,33 @@ def test_decode_shapes(ops, kernel, D, Hkv, G, page):
     assert ops.read_device_error("attn") == 0
 
 
+@pytest.mark.parametrize("D,Hkv,G,page", [(128, 8, 8, 16), (64, 2, 8, 1), (128, 4, 8, 64)])
+@pytest.mark.parametrize("window,L", [(100, 1), (2048, 1), (0, 8), (64, 8)])
+def test_window_and_verify(ops, kernel, D, Hkv, G, page, window, L):
+    """Sliding-window layers (a query at position p attends (p - window, p]) and verify blocks of L
+    query tokens per request (row i of request r: its own visible length, request r's table row)
+    against the oracle's mask of muse_prefill_layer/submission.py:168-171."""
+    from okc_b200 import synth
+    reqs = [37, 3000, 200, 5000, 2049]
+    g = torch.Generator(device="cuda").manual_seed(D + window + L + page)
+    pool = sum(math.ceil((n + L) / page) for n in reqs) + 5
+    table = synth.paged_layout(reqs, page, pool, g, "cuda", extra_tokens=L)
+    kc = torch.empty((pool, page, Hkv, D), dtype=torch.float8_e4m3fn, device="cuda")
+    vc = torch.empty_like(kc)
+    synth.fill_e4m3_normal(kc, g)
+    synth.fill_e4m3_normal(vc, g)
+    B, Hq = len(reqs) * L, Hkv * G
+    q = torch.randn((B, Hq, D), generator=g, device="cuda").to(torch.bfloat16)
+    ks = (torch.rand(Hkv, generator=g, device="cuda") * 1.5 + 0.5).float()
+    vs = (torch.rand(Hkv, generator=g, device="cuda") * 1.5 + 0.5).float()
+    lens = torch.tensor([n + i + 1 for n in reqs for i in range(L)], dtype=torch.int32, device="cuda")
+    out = ops.attn_decode(q, kc, vc, table, lens, ks, vs, D ** -0.5, window=window, q_per_seq=L)
+    exp = ref.decode(q.cpu(), kc.cpu(), vc.cpu(), table.cpu(), lens.cpu(), ks.cpu(), vs.cpu(), D ** -0.5,
+                     window=window, q_per_seq=L)
+    _check(out, exp, f"window {window} L {L} D{D} Hkv{Hkv} P{page}")
+    assert ops.read_device_error("attn") == 0
+
+
 def test_bad_page_id_is_flagged_not_faulted(ops, kernel):
     """A page-table entry outside [0, num_pages) is skipped by the copy engine and reported in
     the workspace error word; the sequences whose pages are valid stay correct."""

@@ -25,20 +25,23 @@ def _close(out, exp, what, rel=1e-2):
     assert (o - e).norm() / e.norm().clamp_min(1e-30) < rel, what
 
 
-@pytest.mark.parametrize("i", range(3))
+@pytest.mark.parametrize("i", range(6))
 def test_attention_problem_matches_reference_output(i):
+    """Cases 0-2: decode steps; 3: a sliding-window layer; 4-5: 8-token verify blocks (full and
+    sliding window), each against the reference's own attention() output."""
     from okc_b200.problems import muse_attention_decode as prob
     c = torch.load(GOLD / "prefill_ops.pt", weights_only=False)["attention_cases"][i]
     cfg = dict(c["cfg"])
+    L = cfg["q_len"]
     qkv = (c["x"] @ c["wqkv"].T).cuda()          # the reference computes qkv the same way
     s = torch.tensor(c["kv_scale"], dtype=torch.float32)
-    data = {"qkv": qkv.view(cfg["batch"], 1, -1), "positions": c["positions"].cuda(),
+    seq = c.get("seq_lens", c["positions"].to(torch.int32))
+    data = {"qkv": qkv.view(cfg["batch"], L, -1), "positions": c["positions"].cuda(),
             "cache_loc": c["cache_loc"].cuda(), "k_cache": c["k_cache_in"].clone().cuda(),
             "v_cache": c["v_cache_in"].clone().cuda(), "k_scale": s.cuda(), "v_scale": s.cuda(),
-            "page_table": c["table"].cuda(), "seq_lens": c["positions"].to(torch.int32).cuda(),
-            "config": cfg}
+            "page_table": c["table"].cuda(), "seq_lens": seq.cuda(), "config": cfg}
     out = prob.kernel_fn(data)
-    _close(out.view(cfg["batch"], -1), c["out"], f"golden case {i}")
+    _close(out.view(cfg["batch"] * L, -1), c["out"], f"golden case {i}")
     # the cache rows the reference wrote: v exactly, k within one e4m3 step (RoPE'd fp32 values)
     ref_v = c["v_cache_out"].view(torch.uint8).view(-1, 2 * 64)
     got_v = data["v_cache"].cpu().view(torch.uint8).view(-1, 2 * 64)
@@ -46,42 +49,45 @@ def test_attention_problem_matches_reference_output(i):
     torch.testing.assert_close(data["k_cache"].cpu().float(), c["k_cache_out"].float(), rtol=0.07, atol=2e-2)
 
 
-def _muse_data(B, ctx, page, kv_scale, theta, seed):
+def _muse_data(B, ctx, page, kv_scale, theta, seed, L=1, window=0):
     from okc_b200 import synth
     hq, hkv, d = 16, 2, 64
     g = torch.Generator(device="cuda").manual_seed(seed)
     lens = torch.randint(max(1, ctx // 2), ctx + 1, (B,), generator=g, device="cuda")
     lens_l = [int(v) for v in lens.tolist()]
-    pool = sum(math.ceil((n + 1) / page) for n in lens_l) + 3
-    table = synth.paged_layout(lens_l, page, pool, g, "cuda", extra_tokens=1)
+    pool = sum(math.ceil((n + L) / page) for n in lens_l) + 3
+    table = synth.paged_layout(lens_l, page, pool, g, "cuda", extra_tokens=L)
     kc = torch.empty((pool, page, hkv, d), dtype=torch.float8_e4m3fn, device="cuda")
     vc = torch.empty_like(kc)
     synth.fill_e4m3_normal(kc, g, torch.full((hkv,), kv_scale, device="cuda"))
     synth.fill_e4m3_normal(vc, g, torch.full((hkv,), kv_scale, device="cuda"))
-    qkv = torch.randn((B, (2 * hq + 2 * hkv) * d), generator=g, device="cuda")
+    qkv = torch.randn((B * L, (2 * hq + 2 * hkv) * d), generator=g, device="cuda")
     qkv[:, :hq * d] *= 2
     qkv = qkv.to(torch.bfloat16)
-    pos = lens.long()
-    cfg = {"batch": B, "q_len": 1, "num_q_heads": hq, "num_kv_heads": hkv, "head_dim": d, "page_size": page,
-           "window": 0, "rope_theta": theta, "qk_scale_factor": 5.4730064863875, "sm_scale": 0.125,
+    pos = (lens.long()[:, None] + torch.arange(L, device="cuda")).reshape(-1)  # the block's positions
+    cfg = {"batch": B, "q_len": L, "num_q_heads": hq, "num_kv_heads": hkv, "head_dim": d, "page_size": page,
+           "window": window, "rope_theta": theta, "qk_scale_factor": 5.4730064863875, "sm_scale": 0.125,
            "kv_scale": kv_scale}
     s = torch.tensor(kv_scale, dtype=torch.float32, device="cuda")
-    return {"qkv": qkv.view(B, 1, -1), "positions": pos, "k_cache": kc, "v_cache": vc, "k_scale": s, "v_scale": s,
+    return {"qkv": qkv.view(B, L, -1), "positions": pos, "k_cache": kc, "v_cache": vc, "k_scale": s, "v_scale": s,
             "page_table": table, "seq_lens": lens.to(torch.int32), "config": cfg}
 
 
-@pytest.mark.parametrize("B,ctx,page,kv_scale,theta", [(1, 10, 1, 1.0, 5e5), (3, 2047, 16, 1.0, 0.0),
-                                                        (4, 3000, 64, 1.0, 5e5), (2, 9000, 64, 1 / 64, 0.0),
-                                                        (16, 5000, 1, 1.0, 0.0), (5, 700, 16, 0.5, 1e4)])
-def test_attention_problem_reference_shapes(B, ctx, page, kv_scale, theta):
+@pytest.mark.parametrize("B,ctx,page,kv_scale,theta,L,window",
+                         [(1, 10, 1, 1.0, 5e5, 1, 0), (3, 2047, 16, 1.0, 0.0, 1, 0), (4, 3000, 64, 1.0, 5e5, 1, 0),
+                          (2, 9000, 64, 1 / 64, 0.0, 1, 0), (16, 5000, 1, 1.0, 0.0, 1, 0), (5, 700, 16, 0.5, 1e4, 1, 0),
+                          # the reference's scored workload: sliding-window (2048) layers, verify blocks of 8
+                          (8, 6000, 1, 1.0, 5e5, 1, 2048), (3, 4000, 1, 1 / 64, 5e5, 8, 2048),
+                          (2, 20000, 64, 1.0, 0.0, 8, 0), (5, 5000, 16, 1.0, 5e5, 8, 2048)])
+def test_attention_problem_reference_shapes(B, ctx, page, kv_scale, theta, L, window):
     from okc_b200.problems import muse_attention_decode as prob
-    data = _muse_data(B, ctx, page, kv_scale, theta, seed=B + ctx)
+    data = _muse_data(B, ctx, page, kv_scale, theta, seed=B + ctx, L=L, window=window)
     kc_ref, vc_ref = data["k_cache"].cpu().clone(), data["v_cache"].cpu().clone()
     cpu = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in data.items()}
-    exp = oatt.muse_attention(cpu["qkv"].view(B, -1), cpu["positions"], cpu["page_table"], kc_ref, vc_ref,
+    exp = oatt.muse_attention(cpu["qkv"].view(B * L, -1), cpu["positions"], cpu["page_table"], kc_ref, vc_ref,
                               cpu["k_scale"], cpu["v_scale"], data["config"])
     out = prob.kernel_fn(data)
-    _close(out.view(B, -1), exp, f"B{B} ctx{ctx} P{page} s{kv_scale} theta{theta}")
+    _close(out.view(B * L, -1), exp, f"B{B} ctx{ctx} P{page} s{kv_scale} theta{theta} L{L} window{window}")
 
 
 @pytest.mark.parametrize("layer,n,k", [("qkv_gate", 2304, 8192), ("o", 8192, 1024), ("pooler", 4096, 8192),

@@ -52,8 +52,10 @@ def test_muse_route(pre):
     assert torch.equal(w, pre["route_weights"])
 
 
-@pytest.mark.parametrize("i", range(3))
+@pytest.mark.parametrize("i", range(6))
 def test_gated_attention_and_cache_append(pre, i):
+    """Cases 0-2: decode (q_len 1, full attention); 3: a sliding-window layer; 4-5: verify blocks
+    of 8 tokens (full and sliding window), all against the reference's own attention()."""
     c = pre["attention_cases"][i]
     cfg = c["cfg"]
     qkv = c["x"] @ c["wqkv"].T
@@ -63,5 +65,6 @@ def test_gated_attention_and_cache_append(pre, i):
     # the append writes the same e4m3 bytes at the same rows
     assert torch.equal(kc.view(torch.uint8), c["k_cache_out"].view(torch.uint8))
     assert torch.equal(vc.view(torch.uint8), c["v_cache_out"].view(torch.uint8))
-    assert torch.equal(oatt.cache_slots(c["table"], c["positions"], cfg["page_size"]), c["cache_loc"])
+    rows = c["table"].repeat_interleave(cfg["q_len"], dim=0)
+    assert torch.equal(oatt.cache_slots(rows, c["positions"], cfg["page_size"]), c["cache_loc"])
     torch.testing.assert_close(out.float(), c["out"].float(), rtol=1e-2, atol=1e-2)
