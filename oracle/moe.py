@@ -18,7 +18,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from .numerics import bf16_round_np
+from .numerics import bf16_round, bf16_round_np
 
 E2M1_GRID = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
 
@@ -115,11 +115,34 @@ def permute(ids: torch.Tensor, expert_lo: int, e_local: int, bm: int):
 
 
 # ------------------------------------------------------------------------------ experts
+def finalize(y: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, gain: torch.Tensor,
+             expert_lo: int, e_local: int, eps: float = 1e-8, out_fp32: bool = False,
+             rounding: str = "rne") -> torch.Tensor:
+    """Muse's post-expert RMSNorm and routing-weighted sum (muse_moe_w4a16/submission.py:295-308,
+    `post_expert_norm` of muse_prefill_layer/submission.py:114-116): for each slot
+    scaled = bf16(y * gain) with gain = 1 + post_norm_w in fp32, normed = scaled *
+    rsqrt(mean(scaled^2) + eps), out[t] = bf16(sum over local slots of w * normed); slots routed
+    to other ranks are masked.  y bf16 [T*topk, H].  `rounding` picks the bf16 rounding (see
+    numerics.bf16_round)."""
+    T, topk = ids.shape
+    H = y.shape[1]
+    scaled = bf16_round(y.float() * gain.float()[None, :], rounding).view(T, topk, H)
+    inv = torch.rsqrt(scaled.pow(2).sum(-1) / H + eps)
+    e = ids.long() - expert_lo
+    local = (e >= 0) & (e < e_local)
+    route = torch.where(local, wts.float(), torch.zeros_like(wts.float()))
+    scaled = torch.where(local[:, :, None], scaled, torch.zeros_like(scaled))
+    out = (scaled * (inv * route)[:, :, None]).sum(1)
+    return out if out_fp32 else bf16_round(out, rounding).to(torch.bfloat16)
+
+
 def experts(x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, w13: torch.Tensor,
             w13_sf: torch.Tensor, w13_gs: torch.Tensor, w2: torch.Tensor, w2_sf: torch.Tensor,
-            w2_gs: torch.Tensor, expert_lo: int = 0, return_y: bool = False):
+            w2_gs: torch.Tensor, expert_lo: int = 0, return_y: bool = False,
+            post_gain: torch.Tensor | None = None, post_eps: float = 1e-8):
     """out[t] = bf16(sum_slot w[t,slot] * y[t*topk + slot]) over local slots, with
-    y = bf16(bf16(silu(bf16(x W_g^T)) * bf16(x W_u^T)) W2^T) per routed expert."""
+    y = bf16(bf16(silu(bf16(x W_g^T)) * bf16(x W_u^T)) W2^T) per routed expert; with
+    `post_gain` (fp32 [H] = 1 + post_norm_w) the slots are post-normed first (finalize)."""
     T, H = x.shape
     topk = ids.shape[1]
     e_local, two_i, _ = w13.shape
@@ -137,6 +160,9 @@ def experts(x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, w13: torch.Te
         inter = (torch.nn.functional.silu(g) * u).to(torch.bfloat16).float()
         w2d = dequantize(w2[e], w2_sf[e], w2_gs[e]).float()
         y[p] = (inter @ w2d.T).to(torch.bfloat16)
+    if post_gain is not None:
+        out = finalize(y, ids, wts, post_gain, expert_lo, e_local, post_eps)
+        return (out, y) if return_y else out
     local = ((flat >= 0) & (flat < e_local)).reshape(T, topk)
     wl = torch.where(local, wts.float(), torch.zeros_like(wts.float()))
     out = torch.zeros((T, H), dtype=torch.float32)

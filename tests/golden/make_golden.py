@@ -12,6 +12,12 @@ Needs a checkout of the reference, named by $OKC_REFERENCE, and runs on CPU:
                      full and sliding-window layers) of
                      muse_prefill_layer/submission.py (its `nvfp4` import is stubbed: the
                      attention path never calls it), on small seeded inputs.
+  moe_boundary.pt    the Triton `_finalize` (post-expert RMSNorm + routing-weighted sum) of
+                     muse_moe_w4a16/submission.py:295-308 and `_boundary` (gated residual
+                     stream + next RMSNorm) of muse_decode_layer/decode/boundaries.py:17-37, both
+                     under Triton's CPU interpreter.  That interpreter rounds fp32 -> bf16 toward
+                     zero (the GPU rounds to nearest even), so the tests pin the oracle's formula
+                     against these with its rounding set to "trunc".
 
     python tests/golden/make_golden.py
 """
@@ -121,6 +127,55 @@ print(json.dumps(cases))
 '''
 
 
+# ------------------------------------------------------------- _finalize, _boundary
+FINALIZE_BOUNDARY_SNIPPET = r'''
+import importlib.util, sys, torch
+spec = importlib.util.spec_from_file_location("moe_ref", sys.argv[1])
+m = importlib.util.module_from_spec(spec); spec.loader.exec_module(m)
+spec = importlib.util.spec_from_file_location("bnd_ref", sys.argv[2])
+bnd = importlib.util.module_from_spec(spec); spec.loader.exec_module(bnd)
+out = {"source": "muse_moe_w4a16/submission.py:295-308 (_finalize), "
+                 "muse_decode_layer/decode/boundaries.py:17-37 (_boundary), Triton interpreter"}
+g = torch.Generator().manual_seed(7)
+# post-expert RMSNorm + routing-weighted sum: 3 tokens, top-8, hidden 4096, local experts [8, 40)
+M = 3
+y = (torch.randn((M * 8, 4096), generator=g) * 3).to(torch.bfloat16)
+ids = torch.randint(0, 64, (M, 8), generator=g).to(torch.int32)
+w = torch.rand((M, 8), generator=g)
+post_norm_w = (torch.randn(4096, generator=g) * 0.1).to(torch.bfloat16)
+norm_w = post_norm_w.float() + 1.0
+fin = torch.empty((M, 4096), dtype=torch.bfloat16)
+m._finalize[(M,)](y, w, ids, norm_w, fin, 8, 32, num_warps=8)
+out.update(fin_y=y, fin_ids=ids, fin_w=w, fin_post_norm_w=post_norm_w, fin_local_start=8, fin_local_count=32,
+           fin_out=fin)
+# gated residual boundaries: attention (unscaled branch) and FFN (branch * (1 + post_ffn_norm))
+T = 3
+stream = torch.randn((T, 8192), generator=g) * 2
+branch = (torch.randn((T, 8192), generator=g) * 0.5).to(torch.bfloat16)
+gate = torch.randn(8192, generator=g)
+beta = torch.sigmoid(gate / 0.3)
+alpha = torch.sqrt(torch.clamp(torch.sigmoid(-gate / 0.3) * (1. + beta), min=1e-3))
+post_w = (torch.randn(8192, generator=g) * 0.1).to(torch.bfloat16)
+pre_w = (torch.randn(8192, generator=g) * 0.1).to(torch.bfloat16)
+for name, scaled in (("attn", False), ("ffn", True)):
+    hidden = torch.empty((T, 8192), dtype=torch.bfloat16)
+    s_out = torch.empty((T, 8192), dtype=torch.float32)
+    router = torch.empty((T, 8192), dtype=torch.float32)
+    bnd._boundary[(T,)](stream, branch, alpha, beta, post_w, pre_w, hidden, s_out, router, 8192, scaled, True,
+                        num_warps=8)
+    out[name + "_hidden"], out[name + "_stream_out"], out[name + "_router"] = hidden, s_out, router
+out.update(bnd_stream=stream, bnd_branch=branch, bnd_alpha=alpha, bnd_beta=beta, bnd_gate=gate,
+           bnd_post_w=post_w, bnd_pre_w=pre_w)
+torch.save(out, sys.argv[3])
+'''
+
+
+def finalize_boundary(path):
+    env = dict(os.environ, TRITON_INTERPRET="1")
+    subprocess.run([sys.executable, "-c", FINALIZE_BOUNDARY_SNIPPET, str(REF / "muse_moe_w4a16/submission.py"),
+                    str(REF / "muse_decode_layer/decode/boundaries.py"), str(path)], env=env, check=True)
+
+
 def route_cases():
     env = dict(os.environ, TRITON_INTERPRET="1")
     out = subprocess.run([sys.executable, "-c", ROUTE_SNIPPET, str(REF / "muse_moe_w4a16/submission.py")],
@@ -215,6 +270,7 @@ def main():
     (HERE / "route_perm.json").write_text(json.dumps(route_cases()))
     import torch
     torch.save(prefill_ops(), HERE / "prefill_ops.pt")
+    finalize_boundary(HERE / "moe_boundary.pt")
     print("wrote", *(p.name for p in sorted(HERE.glob("*")) if p.suffix in (".json", ".pt")))
 
 
