@@ -84,6 +84,26 @@ int okc_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, int ldy, in
                      float eps, int unit_offset, okc_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
+ * Gated residual boundary between a layer's branches.  Replaces `_boundary` /
+ * `_residual_boundary` of muse_decode_layer/decode/boundaries.py:17-50 (the stream update of
+ * muse_prefill_layer/submission.py:205-215).  Per row t:
+ *   b       = branch[t] (bf16, row stride ld_branch); with post_w != NULL first
+ *             b = bf16(b * (1 + post_w))  (the final, post-FFN boundary);
+ *   b       = b * rsqrt(mean(b^2) + post_eps)                    (the reference: 1e-8);
+ *   stream' = alpha * stream_in[t] + beta * b                    (fp32, stream_out[t]);
+ *   hidden  = bf16(stream' * rsqrt(mean(stream'^2) + pre_eps) * (1 + pre_w))  (1e-5);
+ *   router_out[t] = the same hidden unrounded, fp32 (skipped when router_out is NULL).
+ * stream fp32 [T,H] contiguous (stream_out may equal stream_in), alpha/beta fp32 [H], post_w /
+ * pre_w bf16 [H], hidden bf16 [T,H]; H % 8 == 0, H <= 16384, every pointer 16-byte aligned.
+ * Each product and sum is rounded on its own (no fused multiply-add), as the reference
+ * compiles it.
+ * ---------------------------------------------------------------------------------- */
+int okc_residual_boundary(const float* stream_in, const void* branch, int ld_branch,
+                          const float* alpha, const float* beta, const void* post_w,
+                          const void* pre_w, void* hidden, float* stream_out, float* router_out,
+                          int T, int H, float post_eps, float pre_eps, okc_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
  * QKV projection with the RoPE + FP8 KV-append fused into its epilogue (the tcgen05 path,
  * M <= 256): qkv = x · W^T (fp32 accumulate, rounded to bf16 as the unfused path does), then
  * exactly okc_rope_kv_append_ex's arithmetic with qk_norm = 0: q (rotated, x q_scale) to
@@ -258,6 +278,19 @@ int okc_moe_experts_w4a16_ex(const void* x, const int32_t* ids, const float* wei
                              const void* w2, const void* w2_sf, const float* w2_gs,
                              void* out, int T, int topk, int H, int I, int expert_lo, int E_local,
                              int out_fp32, void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
+/* Same, with Muse's post-expert RMSNorm (`_finalize`, muse_moe_w4a16/submission.py:295-308):
+ * with post_gain != NULL (fp32 [H] = 1 + post_norm_w, as the reference's prepare stores it)
+ * each local slot is first scaled = bf16(y * post_gain) and normalised by
+ * rsqrt(mean(scaled^2) + post_eps) (the reference: 1e-8), then weighted and summed.
+ * post_gain needs H <= 8192 and topk <= 16; NULL gives okc_moe_experts_w4a16_ex. */
+int okc_moe_experts_w4a16_post(const void* x, const int32_t* ids, const float* weights,
+                               const int32_t* counts, const int32_t* offsets, const int32_t* pairs,
+                               const void* w13, const void* w13_sf, const float* w13_gs,
+                               const void* w2, const void* w2_sf, const float* w2_gs,
+                               void* out, int T, int topk, int H, int I, int expert_lo, int E_local,
+                               int out_fp32, const float* post_gain, float post_eps, void* workspace,
+                               size_t workspace_bytes, okc_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
  * Tensor-parallel exchange over NVLink peer memory (multi-GPU layer step).  No reference

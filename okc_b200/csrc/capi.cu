@@ -87,6 +87,20 @@ int okc_rmsnorm_bf16(const void* x, int ldx, const void* w, void* y, int ldy, in
   return okc::launch_rmsnorm(x, ldx, w, y, ldy, T, H, eps, unit_offset, stream);
 }
 
+int okc_residual_boundary(const float* stream_in, const void* branch, int ld_branch, const float* alpha,
+                          const float* beta, const void* post_w, const void* pre_w, void* hidden, float* stream_out,
+                          float* router_out, int T, int H, float post_eps, float pre_eps, okc_stream_t stream) {
+  if (!stream_in || !branch || !alpha || !beta || !pre_w || !hidden || !stream_out || T <= 0 || H <= 0 ||
+      H % 8 || H > 16384 || ld_branch < H || ld_branch % 8)
+    return OKC_ERR_INVALID;
+  if (!aligned16(stream_in) || !aligned16(branch) || !aligned16(alpha) || !aligned16(beta) || !aligned16(pre_w) ||
+      !aligned16(hidden) || !aligned16(stream_out) || (post_w && !aligned16(post_w)) ||
+      (router_out && !aligned16(router_out)))
+    return OKC_ERR_ALIGNMENT;
+  return okc::launch_residual_boundary(stream_in, branch, ld_branch, alpha, beta, post_w, pre_w, hidden, stream_out,
+                                       router_out, T, H, post_eps, pre_eps, stream);
+}
+
 // ------------------------------------------------------------------- RoPE + append
 int okc_rope_kv_append_ex(const void* qkv, int ldqkv, const int64_t* positions, const int32_t* page_table,
                           int table_ld, int max_pages, const float* inv_freq, const float* k_scale,
@@ -295,6 +309,19 @@ int okc_moe_experts_w4a16_ex(const void* x, const int32_t* ids, const float* wei
                              const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
                              int E_local, int out_fp32, void* workspace, size_t workspace_bytes,
                              okc_stream_t stream) {
+  return okc_moe_experts_w4a16_post(x, ids, weights, counts, offsets, pairs, w13, w13_sf, w13_gs, w2, w2_sf, w2_gs,
+                                    out, T, topk, H, I, expert_lo, E_local, out_fp32, nullptr, 0.0f, workspace,
+                                    workspace_bytes, stream);
+}
+
+int okc_moe_experts_w4a16_post(const void* x, const int32_t* ids, const float* weights, const int32_t* counts,
+                               const int32_t* offsets, const int32_t* pairs, const void* w13,
+                               const void* w13_sf, const float* w13_gs, const void* w2, const void* w2_sf,
+                               const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
+                               int E_local, int out_fp32, const float* post_gain, float post_eps, void* workspace,
+                               size_t workspace_bytes, okc_stream_t stream) {
+  if (post_gain && (H > 8192 || topk > 16)) return OKC_ERR_INVALID;
+  if (post_gain && !aligned16(post_gain)) return OKC_ERR_ALIGNMENT;
   if (!x || !ids || !weights || !counts || !offsets || !pairs || !w13 || !w13_sf || !w13_gs || !w2 ||
       !w2_sf || !w2_gs || !out)
     return OKC_ERR_INVALID;
@@ -302,7 +329,8 @@ int okc_moe_experts_w4a16_ex(const void* x, const int32_t* ids, const float* wei
   if (!aligned16(x) || !aligned16(w13) || !aligned16(w2) || !aligned16(out)) return OKC_ERR_ALIGNMENT;
   if (!workspace || workspace_bytes < okc::moe_experts_ws_bytes(T, topk, H, I)) return OKC_ERR_WORKSPACE;
   return okc::launch_moe_experts(x, ids, weights, counts, offsets, pairs, w13, w13_sf, w13_gs, w2, w2_sf,
-                                 w2_gs, out, T, topk, H, I, expert_lo, E_local, workspace, stream, out_fp32);
+                                 w2_gs, out, T, topk, H, I, expert_lo, E_local, workspace, stream, out_fp32,
+                                 post_gain, post_eps);
 }
 
 

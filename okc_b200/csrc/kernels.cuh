@@ -66,6 +66,10 @@ size_t tc_gemm_ws_bytes(int M, int N, int K);
 bool tc_gemm_supported(int M, int N, int K, int ldx, int ldw);
 int launch_rmsnorm(const void* x, int ldx, const void* w, void* y, int ldy, int T, int H, float eps,
                    int unit_offset, cudaStream_t stream);
+int launch_residual_boundary(const float* stream_in, const void* branch, int ldb, const float* alpha,
+                             const float* beta, const void* post_w, const void* pre_w, void* hidden,
+                             float* stream_out, float* router_out, int T, int H, float post_eps, float pre_eps,
+                             cudaStream_t stream);
 int launch_attn_decode(AttnArgs& a, int D, int Hkv, cudaStream_t stream);
 int launch_rope_append(const void* qkv, int ldqkv, const int64_t* positions,
                        const int32_t* page_table, int table_ld, int max_pages, const float* inv_freq,
@@ -83,6 +87,7 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
                        const int32_t* offsets, const int32_t* pairs, const void* w13,
                        const void* w13_sf, const float* w13_gs, const void* w2, const void* w2_sf,
                        const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
-                       int E, void* ws, cudaStream_t stream, int out_fp32 = 0);
+                       int E, void* ws, cudaStream_t stream, int out_fp32 = 0,
+                       const float* post_gain = nullptr, float post_eps = 1e-8f);
 
 }  // namespace okc

@@ -18,6 +18,7 @@
 //                  over a thread-block cluster (DSMEM reduction) when few experts are active.
 // down_kernel      y[p] = bf16(gs * inter[p] · W2^T), same decode.
 // combine_kernel   out[t] = bf16(sum_slot w[t, slot] * y[t*topk + slot]) over local slots.
+// combine_postnorm_kernel  the same with Muse's post-expert RMSNorm of each slot first.
 // Roofline: HBM, algorithmic bytes = (#experts hit) * (W13 + sf + W2 + sf) bytes + activations.
 // Mirrors muse_moe_w4a16/submission.py:163-308 and muse_decode_layer/decode/nvfp4_gemv.py:9-75.
 #include <cooperative_groups.h>
@@ -1056,6 +1057,117 @@ __global__ void __launch_bounds__(64) combine_kernel(const __nv_bfloat16* __rest
   *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)t * H + d) = o;
 }
 
+__device__ __forceinline__ float bf16_rn(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Post-expert RMSNorm and weighted sum (muse_moe_w4a16/submission.py:295-308): per local slot
+// scaled = bf16(y * gain) (gain = 1 + post_norm_w, fp32), inv = rsqrt(sum(scaled^2) / H + eps),
+// out[t] = sum over local slots of (w * inv) * scaled.  One CTA of 256 threads per token, H <= 8192
+// (four 16-byte vectors a thread), topk <= 16.  Pass 1 reduces every slot's sum of squares; pass 2
+// re-reads the slot rows, just written by the down projection and still in L2.
+constexpr int kPostVec = 4;
+
+__global__ void __launch_bounds__(256) combine_postnorm_kernel(const __nv_bfloat16* __restrict__ y,
+                                                               const int32_t* __restrict__ ids,
+                                                               const float* __restrict__ wts,
+                                                               const float* __restrict__ gain,
+                                                               void* __restrict__ out, int topk, int H,
+                                                               int expert_lo, int E, float eps, int out_fp32) {
+  const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  __shared__ float red[8][16];
+  __shared__ float coef[16];
+  float g[kPostVec][8];
+#pragma unroll
+  for (int j = 0; j < kPostVec; ++j) {
+    const int i = (j * 256 + tid) * 8;
+    if (i < H) {
+      const float4 a = *reinterpret_cast<const float4*>(gain + i);
+      const float4 b = *reinterpret_cast<const float4*>(gain + i + 4);
+      g[j][0] = a.x; g[j][1] = a.y; g[j][2] = a.z; g[j][3] = a.w;
+      g[j][4] = b.x; g[j][5] = b.y; g[j][6] = b.z; g[j][7] = b.w;
+    }
+  }
+  for (int s = 0; s < topk; ++s) {
+    const int e = ids[(size_t)t * topk + s] - expert_lo;
+    float p = 0.f;
+    if (e >= 0 && e < E) {  // slots routed to other ranks were never written
+      const __nv_bfloat16* row = y + ((size_t)t * topk + s) * H;
+#pragma unroll
+      for (int j = 0; j < kPostVec; ++j) {
+        const int i = (j * 256 + tid) * 8;
+        if (i >= H) break;
+        const uint4 v = *reinterpret_cast<const uint4*>(row + i);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float a = bf16_rn(__fmul_rn(bf16_lo(u[k]), g[j][2 * k]));
+          const float b = bf16_rn(__fmul_rn(bf16_hi(u[k]), g[j][2 * k + 1]));
+          p = fmaf(a, a, p);
+          p = fmaf(b, b, p);
+        }
+      }
+    }
+    p = warp_sum(p);
+    if (lane == 0) red[warp][s] = p;
+  }
+  __syncthreads();
+  if (tid < topk) {
+    const int e = ids[(size_t)t * topk + tid] - expert_lo;
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += red[w][tid];
+    coef[tid] = (e >= 0 && e < E) ? wts[(size_t)t * topk + tid] * rsqrtf(tot / (float)H + eps) : 0.f;
+  }
+  __syncthreads();
+  float acc[kPostVec][8];
+#pragma unroll
+  for (int j = 0; j < kPostVec; ++j)
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[j][k] = 0.f;
+  for (int s = 0; s < topk; ++s) {
+    const int e = ids[(size_t)t * topk + s] - expert_lo;
+    if (e < 0 || e >= E) continue;
+    const float c = coef[s];
+    const __nv_bfloat16* row = y + ((size_t)t * topk + s) * H;
+#pragma unroll
+    for (int j = 0; j < kPostVec; ++j) {
+      const int i = (j * 256 + tid) * 8;
+      if (i >= H) break;
+      const uint4 v = *reinterpret_cast<const uint4*>(row + i);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc[j][2 * k] = fmaf(bf16_rn(__fmul_rn(bf16_lo(u[k]), g[j][2 * k])), c, acc[j][2 * k]);
+        acc[j][2 * k + 1] = fmaf(bf16_rn(__fmul_rn(bf16_hi(u[k]), g[j][2 * k + 1])), c, acc[j][2 * k + 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kPostVec; ++j) {
+    const int i = (j * 256 + tid) * 8;
+    if (i >= H) break;
+    if (out_fp32) {  // this rank's share of an expert-parallel sum
+      float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)t * H + i);
+      o4[0] = make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+      o4[1] = make_float4(acc[j][4], acc[j][5], acc[j][6], acc[j][7]);
+    } else {
+      uint4 o;
+      o.x = pack_bf16x2(acc[j][0], acc[j][1]); o.y = pack_bf16x2(acc[j][2], acc[j][3]);
+      o.z = pack_bf16x2(acc[j][4], acc[j][5]); o.w = pack_bf16x2(acc[j][6], acc[j][7]);
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(out) + (size_t)t * H + i) = o;
+    }
+  }
+}
+
+static int launch_combine(const __nv_bfloat16* y, const int32_t* ids, const float* wts, const float* gain,
+                          float eps, void* out, int T, int topk, int H, int expert_lo, int E, int out_fp32,
+                          cudaStream_t stream) {
+  if (gain)
+    combine_postnorm_kernel<<<T, 256, 0, stream>>>(y, ids, wts, gain, out, topk, H, expert_lo, E, eps, out_fp32);
+  else
+    combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, out, topk, H, expert_lo, E, out_fp32);
+  return okc_host::launch_status();
+}
+
 // ---------------------------------------------------------------------------------------
 // Router, cluster form: a cluster of 8 CTAs serves RT_TT tokens; CTA r of the cluster computes
 // experts [r*E/8, (r+1)*E/8) (warp w: expert r*E/8 + w, + 8 per extra round) for every token of
@@ -1229,7 +1341,8 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
                        const int32_t* offsets, const int32_t* pairs, const void* w13,
                        const void* w13_sf, const float* w13_gs, const void* w2, const void* w2_sf,
                        const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
-                       int E, void* ws, cudaStream_t stream, int out_fp32) {
+                       int E, void* ws, cudaStream_t stream, int out_fp32, const float* post_gain,
+                       float post_eps) {
   uint8_t* base = reinterpret_cast<uint8_t*>(ws) + 256;
   __half* xh = reinterpret_cast<__half*>(base);
   base += ((size_t)T * H * 2 + 255) / 256 * 256;
@@ -1251,9 +1364,7 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
     st = launch_moe_rows<false>(T, w2, w2_sf, E, inter, counts, offsets, pairs, w2_gs, nullptr, y, topk, I, H, I,
                                 err, stream);
     if (st) return st;
-    combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, out, topk, H, expert_lo, E,
-                                                                 out_fp32);
-    return okc_host::launch_status();
+    return launch_combine(y, ids, wts, post_gain, post_eps, out, T, topk, H, expert_lo, E, out_fp32, stream);
   }
   // Measured on B200: the pipelined kernel wins up to 64 tokens, the per-expert kernel above.
   const bool pipe_ok = pipe_env && T <= 64 && H % 1024 == 0 && I % 512 == 0 && I % 16 == 0 && H % 32 == 0 &&
@@ -1276,8 +1387,7 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
                               I, E, sp2, expert_lo, stream);
     if (st) return st;
   }
-  combine_kernel<<<dim3(T, (H + 511) / 512), 64, 0, stream>>>(y, ids, wts, out, topk, H, expert_lo, E, out_fp32);
-  return okc_host::launch_status();
+  return launch_combine(y, ids, wts, post_gain, post_eps, out, T, topk, H, expert_lo, E, out_fp32, stream);
 }
 
 }  // namespace okc

@@ -106,6 +106,36 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, unit_offset: bool = Fa
     return out
 
 
+def residual_boundary(stream: torch.Tensor, branch: torch.Tensor, alpha: torch.Tensor, beta: torch.Tensor,
+                      post_w: torch.Tensor | None, pre_w: torch.Tensor, post_eps: float = 1e-8,
+                      pre_eps: float = 1e-5, stream_out: torch.Tensor | None = None,
+                      router: bool = False):
+    """Muse's gated residual boundary (okc_residual_boundary): returns (hidden bf16 [T, H],
+    stream' fp32 [T, H], router fp32 [T, H] or None).  `stream_out` may be `stream` (in place)."""
+    dev = _dev_index(stream)
+    _need(stream, torch.float32, "stream")
+    _need(branch, torch.bfloat16, "branch")
+    _need(alpha, torch.float32, "alpha")
+    _need(beta, torch.float32, "beta")
+    _need(pre_w, torch.bfloat16, "pre_w")
+    if post_w is not None:
+        _need(post_w, torch.bfloat16, "post_w")
+    T, H = stream.shape
+    if not stream.is_contiguous():
+        raise _lib.OkcError("stream: must be contiguous")
+    hidden = torch.empty((T, H), dtype=torch.bfloat16, device=stream.device)
+    if stream_out is None:
+        stream_out = torch.empty_like(stream)
+    r = torch.empty((T, H), dtype=torch.float32, device=stream.device) if router else None
+    st = _lib.load().okc_residual_boundary(stream.data_ptr(), branch.data_ptr(), branch.stride(0), alpha.data_ptr(),
+                                           beta.data_ptr(), post_w.data_ptr() if post_w is not None else None,
+                                           pre_w.data_ptr(), hidden.data_ptr(), stream_out.data_ptr(),
+                                           r.data_ptr() if r is not None else None, T, H, float(post_eps),
+                                           float(pre_eps), _stream(dev))
+    check(st, "okc_residual_boundary")
+    return hidden, stream_out, r
+
+
 # ------------------------------------------------------------------------- attention
 def rope_inv_freq(theta: float, D: int, device) -> torch.Tensor:
     """inv_freq[i] = 1 / theta^(2i/D) in fp32, computed exactly as the reference does
@@ -246,9 +276,11 @@ def moe_permute(ids: torch.Tensor, expert_lo: int, E_local: int, bm: int = 8) ->
 def moe_experts(x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, perm: dict,
                 w13: torch.Tensor, w13_sf: torch.Tensor, w13_gs: torch.Tensor,
                 w2: torch.Tensor, w2_sf: torch.Tensor, w2_gs: torch.Tensor, expert_lo: int,
-                out: torch.Tensor | None = None, out_fp32: bool = False) -> torch.Tensor:
+                out: torch.Tensor | None = None, out_fp32: bool = False,
+                post_gain: torch.Tensor | None = None, post_eps: float = 1e-8) -> torch.Tensor:
     """Routing-weighted sum of the local experts' SwiGLU MLPs ([T, H]; bf16, or with out_fp32
-    the unrounded fp32 share of an expert-parallel sum)."""
+    the unrounded fp32 share of an expert-parallel sum).  With `post_gain` (fp32 [H] =
+    1 + post_norm_w) each slot gets Muse's post-expert RMSNorm first."""
     dev = _dev_index(x)
     _need(x, torch.bfloat16, "x")
     T, H = x.shape
@@ -259,11 +291,14 @@ def moe_experts(x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, perm: dic
         out = torch.empty((T, H), dtype=torch.float32 if out_fp32 else torch.bfloat16, device=x.device)
     lib = _lib.load()
     ws = workspace(dev, "moe", lib.okc_moe_experts_workspace_bytes(T, topk, H, I))
-    st = lib.okc_moe_experts_w4a16_ex(x.data_ptr(), ids.data_ptr(), wts.data_ptr(), perm["counts"].data_ptr(),
-                                      perm["offsets"].data_ptr(), perm["pairs"].data_ptr(), w13.data_ptr(),
-                                      w13_sf.data_ptr(), w13_gs.data_ptr(), w2.data_ptr(), w2_sf.data_ptr(),
-                                      w2_gs.data_ptr(), out.data_ptr(), T, topk, H, I, expert_lo, E_local,
-                                      int(out_fp32), ws.data_ptr(), ws.numel(), _stream(dev))
+    if post_gain is not None:
+        _need(post_gain, torch.float32, "post_gain")
+    st = lib.okc_moe_experts_w4a16_post(x.data_ptr(), ids.data_ptr(), wts.data_ptr(), perm["counts"].data_ptr(),
+                                        perm["offsets"].data_ptr(), perm["pairs"].data_ptr(), w13.data_ptr(),
+                                        w13_sf.data_ptr(), w13_gs.data_ptr(), w2.data_ptr(), w2_sf.data_ptr(),
+                                        w2_gs.data_ptr(), out.data_ptr(), T, topk, H, I, expert_lo, E_local,
+                                        int(out_fp32), post_gain.data_ptr() if post_gain is not None else None,
+                                        float(post_eps), ws.data_ptr(), ws.numel(), _stream(dev))
     check(st, "okc_moe_experts_w4a16")
     return out
 

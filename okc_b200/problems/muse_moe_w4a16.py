@@ -2,9 +2,10 @@
 """Routed NVFP4 (W4A16) experts with the reference problem's surface
 (muse_moe_w4a16/submission.py:22-49, 352-398): `prepare(weights)` keeps the bank as stored
 (no repack), `kernel_fn(data, state)` takes hidden_states [M, H] bf16, topk_ids [M, k] int32
-(global ids) and topk_weights [M, k] fp32 and returns bf16 [M, H]: the routing-weighted sum of
-the local experts' SwiGLU MLP outputs.  The plain W4A16 MoE contract has no post-expert RMSNorm, so the Muse
-`post_norm_w` is not applied (it is the reference's `_finalize` extra, submission.py:295-308)."""
+(global ids) and topk_weights [M, k] fp32 and returns bf16 [M, H]: the routing-weighted sum over
+the local experts of their SwiGLU MLP outputs, each first passed through the post-expert
+RMSNorm with weight 1 + post_norm_w (`_finalize`, submission.py:295-308) when the bank carries
+`post_norm_w` (a bank without it gives the plain W4A16 sum)."""
 
 from __future__ import annotations
 
@@ -14,7 +15,10 @@ from okc_b200 import ops
 
 
 def prepare(weights: dict) -> dict:
-    return {k: v.contiguous() for k, v in weights.items()}
+    state = {k: v.contiguous() for k, v in weights.items()}
+    if "post_norm_w" in weights:  # the reference's prepare keeps 1 + w in fp32 (submission.py:364)
+        state["norm_w"] = (weights["post_norm_w"].float() + 1.0).contiguous()
+    return state
 
 
 def kernel_fn(data: dict, state: dict) -> torch.Tensor:
@@ -26,7 +30,8 @@ def kernel_fn(data: dict, state: dict) -> torch.Tensor:
     sl = slice(lo, lo + n)
     perm = ops.moe_permute(ids, lo, n)
     return ops.moe_experts(x, ids, wts, perm, state["w13"][sl], state["w13_sf"][sl], state["w13_gs"][sl],
-                           state["w2"][sl], state["w2_sf"][sl], state["w2_gs"][sl], lo)
+                           state["w2"][sl], state["w2_sf"][sl], state["w2_gs"][sl], lo,
+                           post_gain=state.get("norm_w"))
 
 
 custom_kernel = kernel_fn

@@ -51,6 +51,16 @@ def test_validation_without_device(lib):
                                    None, 0, None) == _lib.OKC_ERR_INVALID  # D = 96
     assert lib.okc_moe_route(16, 16, 16, 16, None, 1, 100, 64, 8, 1, None) == _lib.OKC_ERR_INVALID  # H % 256
     assert lib.okc_moe_permute(16, 20000, 8, 0, 64, 8, 16, 16, 16, 16, 100, None) == _lib.OKC_ERR_INVALID
+    # residual boundary: H > 16384, ld_branch < H, a misaligned pointer
+    assert lib.okc_residual_boundary(16, 16, 16392, 16, 16, None, 16, 16, 16, None, 1, 16392, 1e-8, 1e-5,
+                                     None) == _lib.OKC_ERR_INVALID
+    assert lib.okc_residual_boundary(16, 16, 4088, 16, 16, None, 16, 16, 16, None, 1, 4096, 1e-8, 1e-5,
+                                     None) == _lib.OKC_ERR_INVALID
+    assert lib.okc_residual_boundary(16, 16, 4096, 16, 16, 24, 16, 16, 16, None, 1, 4096, 1e-8, 1e-5,
+                                     None) == _lib.OKC_ERR_ALIGNMENT
+    # post-expert norm: H above the combine's 8192
+    assert lib.okc_moe_experts_w4a16_post(*([16] * 13), 4, 8, 16384, 1536, 0, 32, 0, 16, 1e-8, 16, 1 << 30,
+                                          None) == _lib.OKC_ERR_INVALID
 
 
 def test_workspace_queries(lib):

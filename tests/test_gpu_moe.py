@@ -119,3 +119,57 @@ def test_experts_expert_parallel_slice(ops, bank):
     exp = ref.experts(x.cpu(), ids.cpu(), wts.cpu(), cpu["w13"][sl], cpu["w13_sf"][sl], cpu["w13_gs"][sl],
                       cpu["w2"][sl], cpu["w2_sf"][sl], cpu["w2_gs"][sl], expert_lo=lo)
     torch.testing.assert_close(out.float().cpu(), exp.float(), rtol=2e-2, atol=2e-2)
+
+
+def _r256(n):
+    return (n + 255) // 256 * 256
+
+
+@pytest.mark.parametrize("T,lo,E", [(1, 0, 64), (8, 0, 64), (64, 0, 64), (256, 0, 64), (8, 16, 8)])
+def test_experts_post_expert_norm(ops, bank, T, lo, E):
+    """Muse's post-expert RMSNorm (`_finalize`, muse_moe_w4a16/submission.py:295-308): the whole
+    path against the oracle (the experts' tolerance), and the combine alone, bf16-step exact,
+    against oracle.moe.finalize applied to the expert rows the kernel left in its workspace."""
+    H = bank["x"].shape[1]
+    I = bank["w2"].shape[2] * 2
+    x = bank["x"][:T]
+    ids, wts = ops.moe_route(x, bank["router"], 8)
+    g = torch.Generator().manual_seed(7)
+    post_norm_w = (torch.randn(H, generator=g) * 0.1).to(torch.bfloat16)
+    gain = (post_norm_w.float() + 1.0).cuda()
+    perm = ops.moe_permute(ids, lo, E)
+    sl = slice(lo, lo + E)
+    out = ops.moe_experts(x, ids, wts, perm, bank["w13"][sl], bank["w13_sf"][sl], bank["w13_gs"][sl],
+                          bank["w2"][sl], bank["w2_sf"][sl], bank["w2_gs"][sl], lo, post_gain=gain)
+    torch.cuda.synchronize()
+    ws = ops.workspace(torch.cuda.current_device(), "moe", 0)
+    off = 256 + _r256(T * H * 2) + _r256(T * 8 * I * 2)
+    y = ws[off: off + T * 8 * H * 2].view(torch.bfloat16).view(T * 8, H).cpu()
+    local = ((ids.cpu().long() - lo >= 0) & (ids.cpu().long() - lo < E)).reshape(-1)
+    y = torch.where(local[:, None], y, torch.zeros_like(y))  # rows of other ranks' slots are stale
+    fin = ref.finalize(y, ids.cpu(), wts.cpu(), gain.cpu(), lo, E)
+    o, f = out.float().cpu(), fin.float()
+    # one bf16 step of the result, plus an absolute 1e-5 for sums that cancel to near zero (eight
+    # fp32 terms of magnitude <= ~4 summed in another order differ by up to ~2e-6)
+    step = torch.exp2(torch.floor(torch.log2(torch.maximum(o.abs(), f.abs()).clamp_min(2 ** -100))) - 7)
+    bad = (o - f).abs() > step + 1e-5
+    assert not bool(bad.any()), (f"{int(bad.sum())} elements off, e.g. {o[bad][:4].tolist()} vs {f[bad][:4].tolist()}")
+    cpu = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in bank.items()}
+    exp = ref.experts(x.cpu(), ids.cpu(), wts.cpu(), cpu["w13"][sl], cpu["w13_sf"][sl], cpu["w13_gs"][sl],
+                      cpu["w2"][sl], cpu["w2_sf"][sl], cpu["w2_gs"][sl], expert_lo=lo, post_gain=gain.cpu())
+    torch.testing.assert_close(o, exp.float(), rtol=2e-2, atol=2e-2)
+    assert (o - exp.float()).norm() / exp.float().norm() < 1e-2
+
+
+def test_experts_post_norm_fp32_share(ops, bank):
+    """out_fp32 with the post-norm: the unrounded share equals the bf16 output before rounding."""
+    T = 8
+    x = bank["x"][:T]
+    ids, wts = ops.moe_route(x, bank["router"], 8)
+    gain = torch.full((x.shape[1],), 1.25, device="cuda")
+    perm = ops.moe_permute(ids, 0, 64)
+    args = (x, ids, wts, perm, bank["w13"], bank["w13_sf"], bank["w13_gs"], bank["w2"], bank["w2_sf"],
+            bank["w2_gs"], 0)
+    b = ops.moe_experts(*args, post_gain=gain)
+    f = ops.moe_experts(*args, post_gain=gain, out_fp32=True)
+    assert torch.equal(f.to(torch.bfloat16), b)

@@ -122,3 +122,28 @@ def test_moe_problem_global_ids_local_slice():
     exp = omoe.experts(c["x"], ids.cpu(), wts.cpu(), c["w13"][sl], c["w13_sf"][sl], c["w13_gs"][sl], c["w2"][sl],
                        c["w2_sf"][sl], c["w2_gs"][sl], expert_lo=16)
     _close(out, exp, "moe problem")
+
+
+@pytest.mark.parametrize("M", [4, 64])
+def test_moe_problem_post_norm(M):
+    """The problem module with the bank's post_norm_w: Muse's `_finalize` applied (prepare keeps
+    1 + w in fp32 as the reference does)."""
+    from okc_b200 import synth
+    from okc_b200.problems import muse_moe_w4a16 as prob
+    bank = synth.moe_case(T=M, E=64, H=4096, I=1536, device="cuda", seed=6)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    post = (torch.randn(4096, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    weights = {k: bank[k] for k in ("w13", "w13_sf", "w13_gs", "w2", "w2_sf", "w2_gs")}
+    weights["post_norm_w"] = post
+    state = prob.prepare(weights)
+    ids = torch.stack([torch.randperm(64, generator=g, device="cuda")[:8] for _ in range(M)]).to(torch.int32)
+    wts = torch.rand((M, 8), generator=g, device="cuda")
+    wts = wts / wts.sum(1, keepdim=True)
+    cfg = {"bs": M, "d_hidden": 4096, "d_expert": 1536, "n_experts": 64, "local_start": 0, "local_count": 32,
+           "top_k": 8, "sharding": "ep2"}
+    out = prob.kernel_fn({"hidden_states": bank["x"], "topk_ids": ids, "topk_weights": wts, "config": cfg}, state)
+    c = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in bank.items()}
+    sl = slice(0, 32)
+    exp = omoe.experts(c["x"], ids.cpu(), wts.cpu(), c["w13"][sl], c["w13_sf"][sl], c["w13_gs"][sl], c["w2"][sl],
+                       c["w2_sf"][sl], c["w2_gs"][sl], expert_lo=0, post_gain=post.cpu().float() + 1.0)
+    _close(out, exp, "moe problem post-norm")
