@@ -83,6 +83,13 @@ int launch_moe_permute(const int32_t* ids, int n, int expert_lo, int E, int bm, 
                        int32_t* offsets, int32_t* pairs, int32_t* tiles, int max_tiles, int* err,
                        cudaStream_t stream);
 size_t moe_experts_ws_bytes(int T, int topk, int H, int I);
+bool moe_tc_ok(int H, int I, int E);
+int launch_moe_rows_f16(const void* src, const int32_t* pairs, const int32_t* offsets, int E, int topk, int K,
+                        int max_rows, __half* dst, float* rs, cudaStream_t stream);
+template <bool GATED>
+int launch_moe_tc(const void* w, const void* sf, int E, const __half* act, int rows, const float* rs,
+                  const int32_t* counts, const int32_t* offsets, const int32_t* pairs, const float* gs,
+                  __nv_bfloat16* inter, __nv_bfloat16* y, int K, int NR, int I, int* err, cudaStream_t stream);
 int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, const int32_t* counts,
                        const int32_t* offsets, const int32_t* pairs, const void* w13,
                        const void* w13_sf, const float* w13_gs, const void* w2, const void* w2_sf,

@@ -1331,10 +1331,23 @@ static int launch_expert(int T, const __half* xin, const int32_t* counts, const 
 size_t moe_experts_ws_bytes(int T, int topk, int H, int I) {
   const size_t npairs = (size_t)T * topk;
   size_t b = 256;
-  b += ((size_t)T * H * 2 + 255) / 256 * 256;        // x in f16
+  b += (npairs * H * 2 + 255) / 256 * 256;            // x in f16: per token, or gathered per pair
   b += (npairs * I * 2 + 255) / 256 * 256;            // inter f16 (compact order)
   b += (npairs * H * 2 + 255) / 256 * 256;            // y bf16 (by pair id)
+  b += (npairs * 4 + 255) / 256 * 256;                // per-pair activation scales (gate/up)
+  b += (npairs * I * 2 + 255) / 256 * 256;            // inter as scaled f16 (tcgen05 down GEMM)
+  b += (npairs * 4 + 255) / 256 * 256;                // its per-pair scales
   return b;
+}
+
+// The tcgen05 expert kernels (moe_tc.cu) from this many tokens on; OKC_MOE_TC=0/1 forces
+// either family (tuning and tests).
+constexpr int kMoeTcMinT = 96;
+
+static int moe_tc_choice(int T) {
+  const char* e = getenv("OKC_MOE_TC");
+  if (e && (e[0] == '0' || e[0] == '1')) return e[0] - '0';
+  return T >= kMoeTcMinT ? 1 : 0;
 }
 
 int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, const int32_t* counts,
@@ -1343,19 +1356,41 @@ int launch_moe_experts(const void* x, const int32_t* ids, const float* wts, cons
                        const float* w2_gs, void* out, int T, int topk, int H, int I, int expert_lo,
                        int E, void* ws, cudaStream_t stream, int out_fp32, const float* post_gain,
                        float post_eps) {
+  const size_t npairs = (size_t)T * topk;
   uint8_t* base = reinterpret_cast<uint8_t*>(ws) + 256;
   __half* xh = reinterpret_cast<__half*>(base);
-  base += ((size_t)T * H * 2 + 255) / 256 * 256;
+  base += (npairs * H * 2 + 255) / 256 * 256;
   __half* inter = reinterpret_cast<__half*>(base);
-  base += ((size_t)T * topk * I * 2 + 255) / 256 * 256;
+  base += (npairs * I * 2 + 255) / 256 * 256;
   __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(base);
+  base += (npairs * H * 2 + 255) / 256 * 256;
+  float* rs = reinterpret_cast<float*>(base);
+  base += (npairs * 4 + 255) / 256 * 256;
+  __half* inter_h = reinterpret_cast<__half*>(base);
+  base += (npairs * I * 2 + 255) / 256 * 256;
+  float* rs2 = reinterpret_cast<float*>(base);
+  int* err = reinterpret_cast<int*>(ws);
+  int st;
+  if (moe_tc_choice(T) && moe_tc_ok(H, I, E)) {
+    __nv_bfloat16* inter_b = reinterpret_cast<__nv_bfloat16*>(inter);
+    st = launch_moe_rows_f16(x, pairs, offsets, E, topk, H, (int)npairs, xh, rs, stream);
+    if (st) return st;
+    st = launch_moe_tc<true>(w13, w13_sf, E, xh, (int)npairs, rs, counts, offsets, pairs, w13_gs, inter_b, nullptr,
+                             H, I, I, err, stream);
+    if (st) return st;
+    st = launch_moe_rows_f16(inter_b, pairs, offsets, E, 0, I, (int)npairs, inter_h, rs2, stream);
+    if (st) return st;
+    st = launch_moe_tc<false>(w2, w2_sf, E, inter_h, (int)npairs, rs2, counts, offsets, pairs, w2_gs, nullptr, y,
+                              I, H, I, err, stream);
+    if (st) return st;
+    return launch_combine(y, ids, wts, post_gain, post_eps, out, T, topk, H, expert_lo, E, out_fp32, stream);
+  }
   const size_t n = (size_t)T * H;
   int blocks = (int)((n / 8 + 255) / 256);
   if (blocks > 4096) blocks = 4096;
   to_f16_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x), xh, n);
-  int st = okc_host::launch_status();
+  st = okc_host::launch_status();
   if (st) return st;
-  int* err = reinterpret_cast<int*>(ws);
   const int pipe_env = getenv("OKC_MOE_PIPE") ? atoi(getenv("OKC_MOE_PIPE")) : 2;
   if (pipe_env == 2 && moe_rows_ok(T, H, I)) {
     st = launch_moe_rows<true>(T, w13, w13_sf, E, xh, counts, offsets, pairs, w13_gs, inter, nullptr, topk, H, I, I,

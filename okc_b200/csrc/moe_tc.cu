@@ -1,0 +1,494 @@
+// NVFP4 (W4A16) expert GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM), for batches
+// whose experts see tens of tokens (the T >= 32 MoE steps; the row-owning mma.sync kernel in
+// moe.cu serves the few-token decode steps).  Same contract as the moe.cu expert kernels
+// (muse_moe_w4a16/submission.py:163-248): gate/up h = bf16(acc * gs), inter = bf16(silu(g) * u),
+// down y = bf16(acc * gs), fp32 accumulation.
+//
+//  * moe_rows_f16_kernel turns bf16 activation rows into f16 rows scaled by 2^s_j, s_j chosen per
+//    row so that its largest magnitude lands in [2^14, 2^15): every bf16 value of the row is then
+//    exact in f16 (no overflow; only values below 2^-28 of the row maximum reach f16 subnormals),
+//    and the epilogue multiplies by rs[j] = 2^-s_j.  Since the dequantised weights (e2m1 x e4m3,
+//    at most 5 significant bits) are exact in f16 too, the f16 MMAs form exactly the products a
+//    bf16 MMA of the reference's operands would.  Before the gate/up GEMM it gathers the local
+//    (token, slot) pairs expert-major (row j = x[pairs[j] / topk]); before the down GEMM it
+//    converts the bf16 intermediate rows in place order.
+//  * A unit = (active expert, chunk of <= 64 of its pairs, block of weight rows): 64 gate + the
+//    matching 64 up rows (GATED) or 128 down rows, over the full K.  Units of all experts are
+//    split evenly over a persistent grid (one CTA per SM).
+//  * Warp 0 streams the unit's packed codes and e4m3 scales with 2-D TMA boxes (256 K per stage:
+//    one 128-byte row of codes, 128-byte swizzle, plus 16 scale bytes per row) into a 3-deep raw
+//    ring.  Warp 2 loads the matching activation tiles (64 K x 16/32/64 rows of xg or inter,
+//    f16, 128-byte swizzle) into an 8-deep ring; the activations of a chunk stay in L2.
+//  * Warps 3..10 (two groups of four, alternate 64-K slices) dequantise: lane = one weight row,
+//    cvt.rn.f16x2.e2m1x2 then x the e4m3 group scale in f16 (exact: an e2m1 x e4m3 product has
+//    at most 5 significant bits), written straight into the UMMA K-major SWIZZLE_128B layout of
+//    a 128 x 64 f16 A tile (4-deep ring), then fence.proxy.async and an mbarrier arrive.  f16
+//    rather than bf16 because the e2m1 -> f16x2 conversion is a single instruction; the same
+//    product in bf16 takes about four more integer operations per pair, which would make the
+//    dequantisation, not HBM, the bound.
+//  * Warp 1 (one thread) issues tcgen05.mma kind::f16 (M = 128 weight rows, N = the chunk's
+//    tokens rounded up to 16, K = 16 per instruction) into a double-buffered TMEM accumulator.
+//    For GATED the A rows are ordered so that each 32-lane quarter holds 16 gate rows and the
+//    same 16 up rows: lanes l and l + 16 of an epilogue warp hold g and u of one column.
+//  * Warps 11..14 drain TMEM (tcgen05.ld 32x32b), apply the row scale and gs, and store inter
+//    (bf16, compact pair order) or y (bf16, scattered to the pair's row).
+// Every wait is bounded (mbar_wait); on expiry a role sets the abort flag, the others stop at
+// their next wait, copies and MMAs in flight are waited for (bounded), TMEM is freed.
+#include "kernels.cuh"
+#include "tcgen05.cuh"
+
+namespace okc {
+
+constexpr int kMtNT = 64;                          // pairs per unit (MMA N <= 64)
+constexpr int kMtKC = 256;                         // K per raw stage
+constexpr int kMtRaw = 3;                          // raw ring depth
+constexpr int kMtNA = 4;                           // f16 A-tile ring depth
+constexpr int kMtNB = 8;                           // activation-tile ring depth
+constexpr int kMtCodes = 128 * (kMtKC / 2);        // 16 KB of codes per raw stage
+constexpr int kMtRawBytes = kMtCodes + 128 * (kMtKC / 16);  // + 2 KB of scales
+constexpr int kMtATile = 128 * 128;                // 128 rows x 64 K f16
+constexpr int kMtBTile = kMtNT * 128;              // <= 64 rows x 64 K f16
+constexpr int kMtThreads = 15 * 32;
+constexpr int kMtBody = kMtRaw * kMtRawBytes + kMtNA * kMtATile + kMtNB * kMtBTile;
+constexpr int kMtBars = 2 * kMtRaw + 2 * kMtNA + 2 * kMtNB + 2 + 2 + 1;
+constexpr int kMtSmem = 1024 + kMtBody + kMtBars * 8 + 16 + (2 * 257 + 2 * 256) * 4;
+static_assert(kMtRawBytes % 1024 == 0 && kMtATile % 1024 == 0 && kMtBTile % 1024 == 0, "1024-aligned tiles");
+
+__device__ __forceinline__ void mt_tma_u8(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                          uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void mt_fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+// One word of packed codes (bytes b0..b3 = K pairs (2i, 2i+1), low nibble first) -> four f16x2.
+__device__ __forceinline__ uint4 mt_e2m1_word(uint32_t w) {
+  uint4 r;
+  asm("{\n .reg .b8 b0, b1, b2, b3;\n mov.b32 {b0, b1, b2, b3}, %4;\n"
+      " cvt.rn.f16x2.e2m1x2 %0, b0;\n cvt.rn.f16x2.e2m1x2 %1, b1;\n"
+      " cvt.rn.f16x2.e2m1x2 %2, b2;\n cvt.rn.f16x2.e2m1x2 %3, b3;\n}"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "r"(w));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t mt_hmul2(uint32_t a, uint32_t b) {
+  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
+__device__ __forceinline__ uint32_t mt_scale_h2(uint32_t sf_byte) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)sf_byte, __NV_E4M3);
+  return (uint32_t)h.x | ((uint32_t)h.x << 16);
+}
+
+struct MtUnit {
+  int e, rb, row0, n;  // expert, weight-row block, first compact pair row, pairs (<= 64)
+};
+
+// Unit u: active expert i with upre[i] <= u < upre[i+1], then chunk-major, row block minor.
+__device__ __forceinline__ MtUnit mt_unit(const int* act, const int* upre, const int* cnt, const int* off,
+                                          int nact, int nrb, int u) {
+  int lo = 0, hi = nact - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (upre[mid] <= u) lo = mid; else hi = mid - 1;
+  }
+  MtUnit t;
+  const int v = u - upre[lo];
+  const int ch = v / nrb;
+  t.e = act[lo];
+  t.rb = v - ch * nrb;
+  t.row0 = off[t.e] + ch * kMtNT;
+  t.n = min(kMtNT, cnt[t.e] - ch * kMtNT);
+  return t;
+}
+
+template <bool GATED>
+__global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
+    const __grid_constant__ CUtensorMap cmap, const __grid_constant__ CUtensorMap smap,
+    const __grid_constant__ CUtensorMap b16, const __grid_constant__ CUtensorMap b32,
+    const __grid_constant__ CUtensorMap b64, const int32_t* __restrict__ counts,
+    const int32_t* __restrict__ offsets, const int32_t* __restrict__ pairs, const float* __restrict__ gs,
+    const float* __restrict__ rs, __nv_bfloat16* __restrict__ inter_out, __nv_bfloat16* __restrict__ y_out, int K,
+    int NR, int I, int E, int* err) {
+  extern __shared__ uint8_t mt_raw_smem[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mt_raw_smem) + 1023) & ~uintptr_t(1023));
+  uint8_t* rawr = base;
+  uint8_t* atiles = rawr + kMtRaw * kMtRawBytes;
+  uint8_t* btiles = atiles + kMtNA * kMtATile;
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(btiles + kMtNB * kMtBTile);
+  uint64_t* raw_empty = raw_full + kMtRaw;
+  uint64_t* a_full = raw_empty + kMtRaw;
+  uint64_t* a_empty = a_full + kMtNA;
+  uint64_t* b_full = a_empty + kMtNA;
+  uint64_t* b_empty = b_full + kMtNB;
+  uint64_t* acc_full = b_empty + kMtNB;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* act = reinterpret_cast<int*>(tmem_slot + 4);  // [257] active experts, [E] = count
+  int* upre = act + 257;                             // [257] unit prefix over active experts
+  int* cnt = upre + 257;                             // [256] counts
+  int* off = cnt + 256;                              // [256] offsets
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows_w = GATED ? 2 * I : NR;
+  const int nrb = GATED ? I / 64 : NR / 128;
+  const int nk = K / kMtKC;
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kMtRaw; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 8); }
+    for (int i = 0; i < kMtNA; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
+    for (int i = 0; i < kMtNB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(128));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  pdl_wait();
+  if (warp == 0) {  // active experts and their unit prefix
+    int carry = 0, ncarry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      const int c = e < E ? counts[e] : 0;
+      if (e < E) { cnt[e] = c; off[e] = offsets[e]; }
+      const bool on = c > 0;
+      const unsigned bal = __ballot_sync(0xffffffffu, on);
+      const int nu = on ? ((c + kMtNT - 1) / kMtNT) * nrb : 0;
+      int v = nu;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      if (on) {
+        const int i = ncarry + __popc(bal & ((1u << lane) - 1u));
+        act[i] = e;
+        upre[i] = carry + v - nu;
+      }
+      carry += __shfl_sync(0xffffffffu, v, 31);
+      ncarry += __popc(bal);
+    }
+    if (lane == 0) { act[256] = ncarry; upre[ncarry] = carry; }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const int nact = act[256];
+  const int U = nact > 0 ? upre[nact] : 0;
+  int u0, u1;
+  {
+    const int q = U / (int)gridDim.x, r = U % (int)gridDim.x, c = blockIdx.x;
+    u0 = c * q + min(c, r);
+    u1 = u0 + q + (c < r ? 1 : 0);
+  }
+
+  if (warp == 0) {
+    // ------------------------------ weight producer ------------------------------
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      uint32_t r = 0;
+      for (int u = u0; u < u1 && !*abort_flag; ++u) {
+        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
+        const int wrow = t.e * rows_w + t.rb * (GATED ? 64 : 128);
+        for (int ks = 0; ks < nk; ++ks, ++r) {
+          const int s = (int)(r % kMtRaw);
+          if (!mbar_wait(&raw_empty[s], ((r / kMtRaw) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; break; }
+          mbar_arrive_expect_tx(&raw_full[s], kMtRawBytes);
+          uint8_t* d = rawr + s * kMtRawBytes;
+          if (GATED) {
+            mt_tma_u8(d, &cmap, ks * (kMtKC / 2), wrow, &raw_full[s], pol);
+            mt_tma_u8(d + kMtCodes / 2, &cmap, ks * (kMtKC / 2), wrow + I, &raw_full[s], pol);
+            mt_tma_u8(d + kMtCodes, &smap, ks * (kMtKC / 16), wrow, &raw_full[s], pol);
+            mt_tma_u8(d + kMtCodes + 64 * 16, &smap, ks * (kMtKC / 16), wrow + I, &raw_full[s], pol);
+          } else {
+            mt_tma_u8(d, &cmap, ks * (kMtKC / 2), wrow, &raw_full[s], pol);
+            mt_tma_u8(d + kMtCodes, &smap, ks * (kMtKC / 16), wrow, &raw_full[s], pol);
+          }
+        }
+      }
+      for (uint32_t i = r > (uint32_t)kMtRaw ? r - kMtRaw : 0u; i < r; ++i)  // copies in flight land
+        if (!mbar_wait(&raw_full[i % kMtRaw], (i / kMtRaw) & 1u, err)) break;
+    }
+  } else if (warp == 2) {
+    // ---------------------------- activation producer ----------------------------
+    if (lane == 0) {
+      uint32_t q = 0;
+      for (int u = u0; u < u1 && !*abort_flag; ++u) {
+        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
+        const CUtensorMap* map = t.n <= 16 ? &b16 : (t.n <= 32 ? &b32 : &b64);
+        const uint32_t bytes = (t.n <= 16 ? 16u : (t.n <= 32 ? 32u : 64u)) * 128u;
+        bool ok = true;
+        for (int kq = 0; kq < 4 * nk; ++kq, ++q) {
+          const int s = (int)(q % kMtNB);
+          if (!mbar_wait(&b_empty[s], ((q / kMtNB) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; ok = false; break; }
+          mbar_arrive_expect_tx(&b_full[s], bytes);
+          tma_load_2d(btiles + s * kMtBTile, map, kq * 64, t.row0, &b_full[s]);
+        }
+        if (!ok) break;
+      }
+      for (uint32_t i = q > (uint32_t)kMtNB ? q - kMtNB : 0u; i < q; ++i)
+        if (!mbar_wait(&b_full[i % kMtNB], (i / kMtNB) & 1u, err)) break;
+    }
+  } else if (warp == 1) {
+    // ---------------------------------- MMA issuer ----------------------------------
+    if (lane == 0) {
+      uint32_t q = 0;
+      int ui = 0;
+      bool ok = true;
+      for (int u = u0; u < u1 && ok; ++u, ++ui) {
+        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
+        const int nm = (t.n + 15) & ~15;
+        const uint32_t idesc = umma_idesc_f16(nm);
+        const int buf = ui & 1;
+        if (!mbar_wait(&acc_empty[buf], ((uint32_t)(ui >> 1) & 1u) ^ 1u, err, abort_flag)) { ok = false; break; }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        for (int kq = 0; kq < 4 * nk; ++kq, ++q) {
+          const int sa = (int)(q % kMtNA), sb = (int)(q % kMtNB);
+          if (!mbar_wait(&a_full[sa], (q / kMtNA) & 1u, err, abort_flag) ||
+              !mbar_wait(&b_full[sb], (q / kMtNB) & 1u, err, abort_flag)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint64_t da = umma_desc_sw128(smem_u32(atiles + sa * kMtATile));
+          const uint64_t db = umma_desc_sw128(smem_u32(btiles + sb * kMtBTile));
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            umma_bf16(tmem + buf * 64, da + 2 * j, db + 2 * j, idesc, (kq | j) ? 1u : 0u);
+          umma_commit(&a_empty[sa]);
+          umma_commit(&b_empty[sb]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        umma_commit(&acc_full[0]);
+        umma_commit(&acc_full[1]);
+      }
+      umma_commit(drain);  // arrives once every MMA issued above has completed
+      mbar_wait(drain, 0u, err);
+    }
+  } else if (warp <= 10) {
+    // -------------------------------- dequantisation --------------------------------
+    const int dw = warp - 3, grp = dw >> 2, rq = dw & 3;
+    const int m = 32 * rq + lane;  // A row = TMEM lane
+    const int rho = GATED ? (lane < 16 ? 16 * rq + lane : 64 + 16 * rq + lane - 16) : m;  // raw row
+    const int sw = rho & 7, msw = m & 7;
+    uint8_t* arow = atiles + (m >> 3) * 1024 + msw * 128;
+    uint32_t q = 0;
+    bool ok = true;
+    for (int u = u0; u < u1 && ok; ++u) {
+      for (int kq = 0; kq < 4 * nk; ++kq, ++q) {
+        if ((int)(q & 1u) != grp) continue;
+        const uint32_t r = q >> 2;
+        const int a = (int)(q & 3u);
+        const int sr = (int)(r % kMtRaw), sa = (int)(q % kMtNA);
+        if (!mbar_wait(&raw_full[sr], (r / kMtRaw) & 1u, err, abort_flag) ||
+            !mbar_wait(&a_empty[sa], ((q / kMtNA) & 1u) ^ 1u, err, abort_flag)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        const uint8_t* rw = rawr + sr * kMtRawBytes;
+        const uint8_t* crow = rw + rho * 128;
+        const uint4 c0 = *reinterpret_cast<const uint4*>(crow + (((2 * a) ^ sw) << 4));
+        const uint4 c1 = *reinterpret_cast<const uint4*>(crow + (((2 * a + 1) ^ sw) << 4));
+        const uint32_t sc = *reinterpret_cast<const uint32_t*>(rw + kMtCodes + rho * 16 + 4 * a);
+        const uint32_t sd[4] = {mt_scale_h2(sc & 0xffu), mt_scale_h2((sc >> 8) & 0xffu),
+                                mt_scale_h2((sc >> 16) & 0xffu), mt_scale_h2(sc >> 24)};
+        const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        uint8_t* at = arow + sa * kMtATile;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // 8 K values: code bytes 4j..4j+3, scale group j / 2
+          const uint32_t s = sd[j >> 1];
+          uint4 o = mt_e2m1_word(wv[j]);
+          o.x = mt_hmul2(o.x, s);
+          o.y = mt_hmul2(o.y, s);
+          o.z = mt_hmul2(o.z, s);
+          o.w = mt_hmul2(o.w, s);
+          *reinterpret_cast<uint4*>(at + ((j ^ msw) << 4)) = o;
+        }
+        mt_fence_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&a_full[sa]);
+          if (a >= 2) mbar_arrive(&raw_empty[sr]);  // this warp's second and last slice of stage r
+        }
+      }
+    }
+  } else {
+    // ------------------------------------ epilogue ------------------------------------
+    const int q4 = warp & 3;
+    const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
+    int ui = 0;
+    for (int u = u0; u < u1; ++u, ++ui) {
+      const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
+      const int buf = ui & 1;
+      if (!mbar_wait(&acc_full[buf], (uint32_t)(ui >> 1) & 1u, err, abort_flag) || *abort_flag) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const float gsc = gs[t.e];
+      const uint32_t taddr = tmem + lane_base + buf * 64;
+      for (int c0 = 0; c0 < t.n; c0 += 16) {
+        float v[16];
+        tmem_ld16(taddr + c0, v);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = c0 + jj;
+          if (j >= t.n) break;
+          const float acc = v[jj] * rs[t.row0 + j];  // exact: a power of two
+          if (GATED) {
+            const float h = __bfloat162float(__float2bfloat16_rn(acc * gsc));
+            const float up = __shfl_down_sync(0xffffffffu, h, 16);
+            if (lane < 16)
+              inter_out[(size_t)(t.row0 + j) * I + t.rb * 64 + 16 * q4 + lane] =
+                  __float2bfloat16_rn(h / (1.f + expf(-h)) * up);
+          } else {
+            y_out[(size_t)pairs[t.row0 + j] * NR + t.rb * 128 + 32 * q4 + lane] = __float2bfloat16_rn(acc * gsc);
+          }
+        }
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128));
+  }
+}
+
+// dst[j] = f16(src[r_j] * 2^s_j), rs[j] = 2^-s_j for the local pairs j < offsets[E], with
+// r_j = pairs[j] / topk (gather, topk > 0) or j (topk == 0); one warp per row: a pass for the row
+// maximum, a second (L1-resident) pass to scale, convert and store.
+__global__ void __launch_bounds__(256) moe_rows_f16_kernel(const __nv_bfloat16* __restrict__ src,
+                                                           const int32_t* __restrict__ pairs,
+                                                           const int32_t* __restrict__ offsets, int E, int topk,
+                                                           int K, __half* __restrict__ dst, float* __restrict__ rs) {
+  pdl_trigger();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int n = offsets[E];
+  for (int j = blockIdx.x * 8 + (threadIdx.x >> 5); j < n; j += gridDim.x * 8) {
+    const __nv_bfloat16* xr = src + (size_t)(topk > 0 ? pairs[j] / topk : j) * K;
+    float amax = 0.f;
+    for (int k = lane * 8; k < K; k += 256) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) amax = fmaxf(amax, fmaxf(fabsf(bf16_lo(w[h])), fabsf(bf16_hi(w[h]))));
+    }
+    amax = warp_max(amax);
+    // s = 14 - floor(log2 amax), clamped so that both 2^s and 2^-s are normal floats
+    int s = 0;
+    if (amax > 0.f) {
+      const int e2 = (int)((__float_as_uint(amax) >> 23) & 0xffu) - 127;
+      s = min(100, max(-113, 14 - e2));
+    }
+    const float up = __uint_as_float((uint32_t)(127 + s) << 23);
+    if (lane == 0) rs[j] = __uint_as_float((uint32_t)(127 - s) << 23);
+    __half* gr = dst + (size_t)j * K;
+    for (int k = lane * 8; k < K; k += 256) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        __half2 p = __floats2half2_rn(bf16_lo(w[h]) * up, bf16_hi(w[h]) * up);
+        o[h] = *reinterpret_cast<uint32_t*>(&p);
+      }
+      *reinterpret_cast<uint4*>(gr + k) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+static bool mt_u8_map(CUtensorMap* m, const void* base, long long inner, long long rows, int box_x, int box_y,
+                      bool swizzle) {
+  auto fn = tensor_map_encoder();
+  if (!fn || !okc_host::aligned16(base) || inner % 16 || rows <= 0 || rows >= (1LL << 31)) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)inner};
+  cuuint32_t box[2] = {(cuuint32_t)box_x, (cuuint32_t)box_y};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static bool mt_f16_map(CUtensorMap* m, const void* base, long long inner, long long rows, int box_rows) {
+  auto fn = tensor_map_encoder();
+  if (!fn || !okc_host::aligned16(base) || inner % 64 || rows <= 0 || rows >= (1LL << 31)) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)inner * 2};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool moe_tc_ok(int H, int I, int E) {
+  return H % kMtKC == 0 && I % kMtKC == 0 && I % 64 == 0 && H % 128 == 0 && H <= 8192 && E <= 256 &&
+         tensor_map_encoder() != nullptr;
+}
+
+int launch_moe_rows_f16(const void* src, const int32_t* pairs, const int32_t* offsets, int E, int topk, int K,
+                        int max_rows, __half* dst, float* rs, cudaStream_t stream) {
+  int blocks = (max_rows + 7) / 8;
+  const int cap = 4 * okc_host::num_sms();
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return okc_host::launch_k(moe_rows_f16_kernel, dim3(blocks), dim3(256), 0, stream, dim3(1),
+                            reinterpret_cast<const __nv_bfloat16*>(src), pairs, offsets, E, topk, K, dst, rs);
+}
+
+// GATED: act = xg [rows][K = H], weights W13; else act = inter [rows][K = I], weights W2.
+template <bool GATED>
+int launch_moe_tc(const void* w, const void* sf, int E, const __half* act, int rows, const float* rs,
+                  const int32_t* counts, const int32_t* offsets, const int32_t* pairs, const float* gs,
+                  __nv_bfloat16* inter, __nv_bfloat16* y, int K, int NR, int I, int* err, cudaStream_t stream) {
+  const long long wrows = (long long)E * (GATED ? 2 * I : NR);
+  const int box_rows = GATED ? 64 : 128;
+  CUtensorMap cm, sm, m16, m32, m64;
+  if (!mt_u8_map(&cm, w, K / 2, wrows, kMtKC / 2, box_rows, true) ||
+      !mt_u8_map(&sm, sf, K / 16, wrows, kMtKC / 16, box_rows, false) || !mt_f16_map(&m16, act, K, rows, 16) ||
+      !mt_f16_map(&m32, act, K, rows, 32) || !mt_f16_map(&m64, act, K, rows, 64))
+    return OKC_ERR_INVALID;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(moe_tc_kernel<GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMtSmem) !=
+        cudaSuccess)
+      return OKC_ERR_LAUNCH;
+    configured = true;
+  }
+  return okc_host::launch_k(moe_tc_kernel<GATED>, dim3(okc_host::num_sms()), dim3(kMtThreads), kMtSmem, stream,
+                            dim3(1), cm, sm, m16, m32, m64, counts, offsets, pairs, gs, rs, inter, y, K, NR, I, E,
+                            err);
+}
+
+template int launch_moe_tc<true>(const void*, const void*, int, const __half*, int, const float*, const int32_t*,
+                                 const int32_t*, const int32_t*, const float*, __nv_bfloat16*, __nv_bfloat16*, int,
+                                 int, int, int*, cudaStream_t);
+template int launch_moe_tc<false>(const void*, const void*, int, const __half*, int, const float*, const int32_t*,
+                                  const int32_t*, const int32_t*, const float*, __nv_bfloat16*, __nv_bfloat16*, int,
+                                  int, int, int*, cudaStream_t);
+
+}  // namespace okc

@@ -143,7 +143,7 @@ def test_experts_post_expert_norm(ops, bank, T, lo, E):
                           bank["w2"][sl], bank["w2_sf"][sl], bank["w2_gs"][sl], lo, post_gain=gain)
     torch.cuda.synchronize()
     ws = ops.workspace(torch.cuda.current_device(), "moe", 0)
-    off = 256 + _r256(T * H * 2) + _r256(T * 8 * I * 2)
+    off = 256 + _r256(T * 8 * H * 2) + _r256(T * 8 * I * 2)
     y = ws[off: off + T * 8 * H * 2].view(torch.bfloat16).view(T * 8, H).cpu()
     local = ((ids.cpu().long() - lo >= 0) & (ids.cpu().long() - lo < E)).reshape(-1)
     y = torch.where(local[:, None], y, torch.zeros_like(y))  # rows of other ranks' slots are stale
@@ -173,3 +173,45 @@ def test_experts_post_norm_fp32_share(ops, bank):
     b = ops.moe_experts(*args, post_gain=gain)
     f = ops.moe_experts(*args, post_gain=gain, out_fp32=True)
     assert torch.equal(f.to(torch.bfloat16), b)
+
+
+@pytest.mark.parametrize("T,tc", [(8, "1"), (16, "1"), (32, "1"), (32, "0"), (64, "1"), (64, "0"), (256, "1")])
+def test_experts_kernel_families(ops, bank, T, tc, monkeypatch):
+    """The tcgen05 expert kernels (OKC_MOE_TC=1: gather + dequantise-to-shared-memory +
+    tcgen05.mma) and the mma.sync kernels (0) against the same oracle, on both sides of the
+    switch (96 tokens)."""
+    monkeypatch.setenv("OKC_MOE_TC", tc)
+    x = bank["x"][:T]
+    ids, wts = ops.moe_route(x, bank["router"], 8)
+    perm = ops.moe_permute(ids, 0, 64)
+    out = ops.moe_experts(x, ids, wts, perm, bank["w13"], bank["w13_sf"], bank["w13_gs"],
+                          bank["w2"], bank["w2_sf"], bank["w2_gs"], 0)
+    assert ops.read_device_error("moe") == 0
+    cpu = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in bank.items()}
+    exp = ref.experts(x.cpu(), ids.cpu(), wts.cpu(), cpu["w13"], cpu["w13_sf"], cpu["w13_gs"],
+                      cpu["w2"], cpu["w2_sf"], cpu["w2_gs"])
+    o, e = out.float().cpu(), exp.float()
+    torch.testing.assert_close(o, e, rtol=2e-2, atol=2e-2)
+    assert (o - e).norm() / e.norm() < 1e-2
+
+
+def test_experts_tc_activation_range(ops, bank, monkeypatch):
+    """Activations far outside the f16 range go through the tcgen05 path as the same inputs
+    scaled back: the per-row power-of-two scaling before each GEMM is exact, so x * 2^k gives
+    the reference's outputs for x * 2^k (checked against the oracle at 2^-20 and 2^12, where a
+    plain f16 conversion would flush or overflow)."""
+    monkeypatch.setenv("OKC_MOE_TC", "1")
+    T = 32
+    cpu = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in bank.items()}
+    for k in (-20, 12):
+        x = (bank["x"][:T].float() * 2.0 ** k).to(torch.bfloat16)
+        ids, wts = ops.moe_route(bank["x"][:T], bank["router"], 8)
+        perm = ops.moe_permute(ids, 0, 64)
+        out = ops.moe_experts(x, ids, wts, perm, bank["w13"], bank["w13_sf"], bank["w13_gs"], bank["w2"],
+                              bank["w2_sf"], bank["w2_gs"], 0)
+        assert ops.read_device_error("moe") == 0
+        exp = ref.experts(x.cpu(), ids.cpu(), wts.cpu(), cpu["w13"], cpu["w13_sf"], cpu["w13_gs"],
+                          cpu["w2"], cpu["w2_sf"], cpu["w2_gs"]).float()
+        o = out.float().cpu()
+        assert torch.isfinite(o).all()
+        assert (o - exp).norm() / exp.norm() < 1e-2, f"scale 2^{k}"
