@@ -1,6 +1,6 @@
-// NVFP4 (W4A16) expert GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM), for batches
-// whose experts see tens of tokens (the T >= 32 MoE steps; the row-owning mma.sync kernel in
-// moe.cu serves the few-token decode steps).  Same contract as the moe.cu expert kernels
+// NVFP4 (W4A16) expert GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM), for MoE steps
+// whose experts see tens of tokens (the row-owning mma.sync kernel in moe.cu serves the
+// few-token decode steps).  Same contract as the moe.cu expert kernels
 // (muse_moe_w4a16/submission.py:163-248): gate/up h = bf16(acc * gs), inter = bf16(silu(g) * u),
 // down y = bf16(acc * gs), fp32 accumulation.
 //
@@ -11,27 +11,31 @@
 //    at most 5 significant bits) are exact in f16 too, the f16 MMAs form exactly the products a
 //    bf16 MMA of the reference's operands would.  Before the gate/up GEMM it gathers the local
 //    (token, slot) pairs expert-major (row j = x[pairs[j] / topk]); before the down GEMM it
-//    converts the bf16 intermediate rows in place order.
-//  * A unit = (active expert, chunk of <= 64 of its pairs, block of weight rows): 64 gate + the
-//    matching 64 up rows (GATED) or 128 down rows, over the full K.  Units of all experts are
-//    split evenly over a persistent grid (one CTA per SM).
+//    converts the bf16 intermediate rows.
+//  * Operand roles follow the measured issue costs on B200 (one thread issuing kind::f16 MMAs:
+//    ~58 cycles per instruction up to N = 128, ~145 per commit; an M = 128, N = 256, K = 16 MMA
+//    runs 128 cycles on the tensor pipe): the A operand (M = 128) is a chunk of up to 128 of an
+//    expert's pairs (activations, padded), the B operand (N = 256) is 256 dequantised weight
+//    rows, so each MMA covers 4096 weight values and the tensor pipe, not instruction issue, sets
+//    the pace: ~32 weight values per cycle per SM, about 4.6 TB/s of NVFP4 at 148 SMs.
+//  * A unit = (active expert, chunk of <= 128 pairs, block of 256 weight rows: 128 gate + the same
+//    128 up rows (GATED) or 256 down rows) over the full K.  Units of all experts are split
+//    evenly over a persistent grid (one CTA per SM).
 //  * Warp 0 streams the unit's packed codes and e4m3 scales with 2-D TMA boxes (256 K per stage:
-//    one 128-byte row of codes, 128-byte swizzle, plus 16 scale bytes per row) into a 3-deep raw
-//    ring.  Warp 2 loads the matching activation tiles (64 K x 16/32/64 rows of xg or inter,
-//    f16, 128-byte swizzle) into an 8-deep ring; the activations of a chunk stay in L2.
-//  * Warps 3..10 (two groups of four, alternate 64-K slices) dequantise: lane = one weight row,
-//    cvt.rn.f16x2.e2m1x2 then x the e4m3 group scale in f16 (exact: an e2m1 x e4m3 product has
-//    at most 5 significant bits), written straight into the UMMA K-major SWIZZLE_128B layout of
-//    a 128 x 64 f16 A tile (4-deep ring), then fence.proxy.async and an mbarrier arrive.  f16
-//    rather than bf16 because the e2m1 -> f16x2 conversion is a single instruction; the same
-//    product in bf16 takes about four more integer operations per pair, which would make the
-//    dequantisation, not HBM, the bound.
-//  * Warp 1 (one thread) issues tcgen05.mma kind::f16 (M = 128 weight rows, N = the chunk's
-//    tokens rounded up to 16, K = 16 per instruction) into a double-buffered TMEM accumulator.
-//    For GATED the A rows are ordered so that each 32-lane quarter holds 16 gate rows and the
-//    same 16 up rows: lanes l and l + 16 of an epilogue warp hold g and u of one column.
-//  * Warps 11..14 drain TMEM (tcgen05.ld 32x32b), apply the row scale and gs, and store inter
-//    (bf16, compact pair order) or y (bf16, scattered to the pair's row).
+//    one 128-byte row of codes per weight row, 128-byte swizzle, and 16 scale bytes per row) into
+//    a 2-deep raw ring (36 KB a stage).  Warp 2 loads the activation tile of each 64-K slice
+//    (f16, 128-byte swizzle, a 16/32/64/128-row box sized to the chunk) into the slice's slot.
+//  * Warps 3..10 dequantise, lane = one of the 256 weight rows: cvt.rn.f16x2.e2m1x2, x the e4m3
+//    group scale in f16 (exact), stored straight into the UMMA K-major SWIZZLE_128B layout of the
+//    slot's 256 x 64 f16 B tile; fence.proxy.async, then an arrive on the slot's full barrier
+//    (which also waits for the activation tile's bytes).  3 slots of 48 KB.  f16 rather than bf16
+//    because the e2m1 -> f16x2 conversion is one instruction; the same product in bf16 takes
+//    about four more integer operations per pair.
+//  * Warp 1 (one thread) issues 4 MMAs per slice into a double-buffered TMEM accumulator
+//    (2 x 256 columns) and frees the slot with one tcgen05.commit.
+//  * Warps 11..14 drain TMEM (tcgen05.ld 32x32b: lane = pair, column = weight row), apply the row
+//    scale and gs, and store inter (bf16, compact pair order; gate column j and up column
+//    128 + j meet in one thread) or y (bf16, the pair's row).
 // Every wait is bounded (mbar_wait); on expiry a role sets the abort flag, the others stop at
 // their next wait, copies and MMAs in flight are waited for (bounded), TMEM is freed.
 #include "kernels.cuh"
@@ -39,20 +43,22 @@
 
 namespace okc {
 
-constexpr int kMtNT = 64;                          // pairs per unit (MMA N <= 64)
+constexpr int kMtNT = 128;                         // pairs per unit (MMA M)
+constexpr int kMtNW = 256;                         // weight rows per unit (MMA N)
 constexpr int kMtKC = 256;                         // K per raw stage
-constexpr int kMtRaw = 3;                          // raw ring depth
-constexpr int kMtNA = 4;                           // f16 A-tile ring depth
-constexpr int kMtNB = 8;                           // activation-tile ring depth
-constexpr int kMtCodes = 128 * (kMtKC / 2);        // 16 KB of codes per raw stage
-constexpr int kMtRawBytes = kMtCodes + 128 * (kMtKC / 16);  // + 2 KB of scales
-constexpr int kMtATile = 128 * 128;                // 128 rows x 64 K f16
-constexpr int kMtBTile = kMtNT * 128;              // <= 64 rows x 64 K f16
+constexpr int kMtRaw = 2;                          // raw ring depth
+constexpr int kMtNS = 3;                           // slice slots (activation tile + weight tile)
+constexpr int kMtCodes = kMtNW * (kMtKC / 2);      // 32 KB of codes per raw stage
+constexpr int kMtRawBytes = kMtCodes + kMtNW * (kMtKC / 16);  // + 4 KB of scales
+constexpr int kMtATile = kMtNT * 128;              // 128 pairs x 64 K f16
+constexpr int kMtBTile = kMtNW * 128;              // 256 weight rows x 64 K f16
+constexpr int kMtSlot = kMtATile + kMtBTile;
 constexpr int kMtThreads = 15 * 32;
-constexpr int kMtBody = kMtRaw * kMtRawBytes + kMtNA * kMtATile + kMtNB * kMtBTile;
-constexpr int kMtBars = 2 * kMtRaw + 2 * kMtNA + 2 * kMtNB + 2 + 2 + 1;
+constexpr int kMtBody = kMtRaw * kMtRawBytes + kMtNS * kMtSlot;
+constexpr int kMtBars = 2 * kMtRaw + 2 * kMtNS + 2 + 2 + 1;
 constexpr int kMtSmem = 1024 + kMtBody + kMtBars * 8 + 16 + (2 * 257 + 2 * 256) * 4;
 static_assert(kMtRawBytes % 1024 == 0 && kMtATile % 1024 == 0 && kMtBTile % 1024 == 0, "1024-aligned tiles");
+static_assert(kMtSmem <= 232448, "shared memory");
 
 __device__ __forceinline__ void mt_tma_u8(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
                                           uint64_t policy) {
@@ -65,9 +71,9 @@ __device__ __forceinline__ void mt_tma_u8(void* dst, const CUtensorMap* map, int
 
 __device__ __forceinline__ void mt_fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int n) {
-  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M x N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 // One word of packed codes (bytes b0..b3 = K pairs (2i, 2i+1), low nibble first) -> four f16x2.
@@ -91,8 +97,16 @@ __device__ __forceinline__ uint32_t mt_scale_h2(uint32_t sf_byte) {
   return (uint32_t)h.x | ((uint32_t)h.x << 16);
 }
 
+__device__ __forceinline__ void mt_tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 struct MtUnit {
-  int e, rb, row0, n;  // expert, weight-row block, first compact pair row, pairs (<= 64)
+  int e, rb, row0, n;  // expert, weight-row block, first compact pair row, pairs (<= 128)
 };
 
 // Unit u: active expert i with upre[i] <= u < upre[i+1], then chunk-major, row block minor.
@@ -116,41 +130,37 @@ __device__ __forceinline__ MtUnit mt_unit(const int* act, const int* upre, const
 template <bool GATED>
 __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
     const __grid_constant__ CUtensorMap cmap, const __grid_constant__ CUtensorMap smap,
-    const __grid_constant__ CUtensorMap b16, const __grid_constant__ CUtensorMap b32,
-    const __grid_constant__ CUtensorMap b64, const int32_t* __restrict__ counts,
-    const int32_t* __restrict__ offsets, const int32_t* __restrict__ pairs, const float* __restrict__ gs,
-    const float* __restrict__ rs, __nv_bfloat16* __restrict__ inter_out, __nv_bfloat16* __restrict__ y_out, int K,
-    int NR, int I, int E, int* err) {
+    const __grid_constant__ CUtensorMap a16, const __grid_constant__ CUtensorMap a32,
+    const __grid_constant__ CUtensorMap a64, const __grid_constant__ CUtensorMap a128,
+    const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets, const int32_t* __restrict__ pairs,
+    const float* __restrict__ gs, const float* __restrict__ rs, __nv_bfloat16* __restrict__ inter_out,
+    __nv_bfloat16* __restrict__ y_out, int K, int NR, int I, int E, int* err) {
   extern __shared__ uint8_t mt_raw_smem[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mt_raw_smem) + 1023) & ~uintptr_t(1023));
   uint8_t* rawr = base;
-  uint8_t* atiles = rawr + kMtRaw * kMtRawBytes;
-  uint8_t* btiles = atiles + kMtNA * kMtATile;
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(btiles + kMtNB * kMtBTile);
+  uint8_t* slots = rawr + kMtRaw * kMtRawBytes;
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(slots + kMtNS * kMtSlot);
   uint64_t* raw_empty = raw_full + kMtRaw;
-  uint64_t* a_full = raw_empty + kMtRaw;
-  uint64_t* a_empty = a_full + kMtNA;
-  uint64_t* b_full = a_empty + kMtNA;
-  uint64_t* b_empty = b_full + kMtNB;
-  uint64_t* acc_full = b_empty + kMtNB;
+  uint64_t* full = raw_empty + kMtRaw;
+  uint64_t* empty = full + kMtNS;
+  uint64_t* acc_full = empty + kMtNS;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* act = reinterpret_cast<int*>(tmem_slot + 4);  // [257] active experts, [E] = count
+  int* act = reinterpret_cast<int*>(tmem_slot + 4);  // [257] active experts, [256] = count
   int* upre = act + 257;                             // [257] unit prefix over active experts
   int* cnt = upre + 257;                             // [256] counts
   int* off = cnt + 256;                              // [256] offsets
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows_w = GATED ? 2 * I : NR;
-  const int nrb = GATED ? I / 64 : NR / 128;
+  const int nrb = GATED ? I / 128 : NR / 256;
   const int nk = K / kMtKC;
   pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMtRaw; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 8); }
-    for (int i = 0; i < kMtNA; ++i) { mbar_init(&a_full[i], 4); mbar_init(&a_empty[i], 1); }
-    for (int i = 0; i < kMtNB; ++i) { mbar_init(&b_full[i], 1); mbar_init(&b_empty[i], 1); }
+    for (int i = 0; i < kMtNS; ++i) { mbar_init(&full[i], 9); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -158,7 +168,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(128));
+                 "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   pdl_wait();
@@ -207,17 +217,17 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       uint32_t r = 0;
       for (int u = u0; u < u1 && !*abort_flag; ++u) {
         const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
-        const int wrow = t.e * rows_w + t.rb * (GATED ? 64 : 128);
+        const int wrow = t.e * rows_w + t.rb * (GATED ? 128 : 256);
         for (int ks = 0; ks < nk; ++ks, ++r) {
           const int s = (int)(r % kMtRaw);
           if (!mbar_wait(&raw_empty[s], ((r / kMtRaw) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; break; }
           mbar_arrive_expect_tx(&raw_full[s], kMtRawBytes);
           uint8_t* d = rawr + s * kMtRawBytes;
-          if (GATED) {
+          if (GATED) {  // rows 0-127: gate rows, 128-255: the same up rows
             mt_tma_u8(d, &cmap, ks * (kMtKC / 2), wrow, &raw_full[s], pol);
             mt_tma_u8(d + kMtCodes / 2, &cmap, ks * (kMtKC / 2), wrow + I, &raw_full[s], pol);
             mt_tma_u8(d + kMtCodes, &smap, ks * (kMtKC / 16), wrow, &raw_full[s], pol);
-            mt_tma_u8(d + kMtCodes + 64 * 16, &smap, ks * (kMtKC / 16), wrow + I, &raw_full[s], pol);
+            mt_tma_u8(d + kMtCodes + 128 * 16, &smap, ks * (kMtKC / 16), wrow + I, &raw_full[s], pol);
           } else {
             mt_tma_u8(d, &cmap, ks * (kMtKC / 2), wrow, &raw_full[s], pol);
             mt_tma_u8(d + kMtCodes, &smap, ks * (kMtKC / 16), wrow, &raw_full[s], pol);
@@ -231,47 +241,43 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
     // ---------------------------- activation producer ----------------------------
     if (lane == 0) {
       uint32_t q = 0;
-      for (int u = u0; u < u1 && !*abort_flag; ++u) {
+      bool ok = true;
+      for (int u = u0; u < u1 && ok && !*abort_flag; ++u) {
         const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
-        const CUtensorMap* map = t.n <= 16 ? &b16 : (t.n <= 32 ? &b32 : &b64);
-        const uint32_t bytes = (t.n <= 16 ? 16u : (t.n <= 32 ? 32u : 64u)) * 128u;
-        bool ok = true;
+        const int box = t.n <= 16 ? 16 : (t.n <= 32 ? 32 : (t.n <= 64 ? 64 : 128));
+        const CUtensorMap* map = box == 16 ? &a16 : (box == 32 ? &a32 : (box == 64 ? &a64 : &a128));
         for (int kq = 0; kq < 4 * nk; ++kq, ++q) {
-          const int s = (int)(q % kMtNB);
-          if (!mbar_wait(&b_empty[s], ((q / kMtNB) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; ok = false; break; }
-          mbar_arrive_expect_tx(&b_full[s], bytes);
-          tma_load_2d(btiles + s * kMtBTile, map, kq * 64, t.row0, &b_full[s]);
+          const int s = (int)(q % kMtNS);
+          if (!mbar_wait(&empty[s], ((q / kMtNS) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], (uint32_t)box * 128u);
+          tma_load_2d(slots + s * kMtSlot, map, kq * 64, t.row0, &full[s]);
         }
-        if (!ok) break;
       }
-      for (uint32_t i = q > (uint32_t)kMtNB ? q - kMtNB : 0u; i < q; ++i)
-        if (!mbar_wait(&b_full[i % kMtNB], (i / kMtNB) & 1u, err)) break;
+      // the activation copies issued land before the CTA can leave: a slot's full phase
+      // completes only with them (and the dequant arrivals, bounded by the same wait)
+      for (uint32_t i = q > (uint32_t)kMtNS ? q - kMtNS : 0u; i < q; ++i)
+        if (!mbar_wait(&full[i % kMtNS], (i / kMtNS) & 1u, err)) break;
     }
   } else if (warp == 1) {
     // ---------------------------------- MMA issuer ----------------------------------
     if (lane == 0) {
+      const uint32_t idesc = umma_idesc_f16(kMtNT, kMtNW);
       uint32_t q = 0;
       int ui = 0;
       bool ok = true;
       for (int u = u0; u < u1 && ok; ++u, ++ui) {
-        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
-        const int nm = (t.n + 15) & ~15;
-        const uint32_t idesc = umma_idesc_f16(nm);
         const int buf = ui & 1;
         if (!mbar_wait(&acc_empty[buf], ((uint32_t)(ui >> 1) & 1u) ^ 1u, err, abort_flag)) { ok = false; break; }
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         for (int kq = 0; kq < 4 * nk; ++kq, ++q) {
-          const int sa = (int)(q % kMtNA), sb = (int)(q % kMtNB);
-          if (!mbar_wait(&a_full[sa], (q / kMtNA) & 1u, err, abort_flag) ||
-              !mbar_wait(&b_full[sb], (q / kMtNB) & 1u, err, abort_flag)) { ok = false; break; }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint64_t da = umma_desc_sw128(smem_u32(atiles + sa * kMtATile));
-          const uint64_t db = umma_desc_sw128(smem_u32(btiles + sb * kMtBTile));
+          const int s = (int)(q % kMtNS);
+          if (!mbar_wait(&full[s], (q / kMtNS) & 1u, err, abort_flag)) { ok = false; break; }
+          const uint32_t sa = smem_u32(slots + s * kMtSlot);
+          const uint64_t da = umma_desc_sw128(sa), db = umma_desc_sw128(sa + kMtATile);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
-            umma_bf16(tmem + buf * 64, da + 2 * j, db + 2 * j, idesc, (kq | j) ? 1u : 0u);
-          umma_commit(&a_empty[sa]);
-          umma_commit(&b_empty[sb]);
+            umma_bf16(tmem + buf * kMtNW, da + 2 * j, db + 2 * j, idesc, (kq | j) ? 1u : 0u);
+          umma_commit(&empty[s]);
         }
         if (ok) umma_commit(&acc_full[buf]);
       }
@@ -285,55 +291,54 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
     }
   } else if (warp <= 10) {
     // -------------------------------- dequantisation --------------------------------
-    const int dw = warp - 3, grp = dw >> 2, rq = dw & 3;
-    const int m = 32 * rq + lane;  // A row = TMEM lane
-    const int rho = GATED ? (lane < 16 ? 16 * rq + lane : 64 + 16 * rq + lane - 16) : m;  // raw row
-    const int sw = rho & 7, msw = m & 7;
-    uint8_t* arow = atiles + (m >> 3) * 1024 + msw * 128;
+    const int n = 32 * (warp - 3) + lane;  // weight row of the unit = B row
+    const int nsw = n & 7;
+    const uint8_t* crow0 = rawr + n * 128;                   // codes, 128-byte swizzled rows
+    const uint8_t* srow0 = rawr + kMtCodes + n * 16;         // scales
+    uint8_t* brow0 = slots + kMtATile + (n >> 3) * 1024 + nsw * 128;
     uint32_t q = 0;
     bool ok = true;
     for (int u = u0; u < u1 && ok; ++u) {
       for (int kq = 0; kq < 4 * nk; ++kq, ++q) {
-        if ((int)(q & 1u) != grp) continue;
         const uint32_t r = q >> 2;
         const int a = (int)(q & 3u);
-        const int sr = (int)(r % kMtRaw), sa = (int)(q % kMtNA);
+        const int sr = (int)(r % kMtRaw), s = (int)(q % kMtNS);
         if (!mbar_wait(&raw_full[sr], (r / kMtRaw) & 1u, err, abort_flag) ||
-            !mbar_wait(&a_empty[sa], ((q / kMtNA) & 1u) ^ 1u, err, abort_flag)) {
+            !mbar_wait(&empty[s], ((q / kMtNS) & 1u) ^ 1u, err, abort_flag)) {
           *abort_flag = 1;
           ok = false;
           break;
         }
-        const uint8_t* rw = rawr + sr * kMtRawBytes;
-        const uint8_t* crow = rw + rho * 128;
-        const uint4 c0 = *reinterpret_cast<const uint4*>(crow + (((2 * a) ^ sw) << 4));
-        const uint4 c1 = *reinterpret_cast<const uint4*>(crow + (((2 * a + 1) ^ sw) << 4));
-        const uint32_t sc = *reinterpret_cast<const uint32_t*>(rw + kMtCodes + rho * 16 + 4 * a);
+        const uint8_t* crow = crow0 + sr * kMtRawBytes;
+        const uint4 c0 = *reinterpret_cast<const uint4*>(crow + (((2 * a) ^ nsw) << 4));
+        const uint4 c1 = *reinterpret_cast<const uint4*>(crow + (((2 * a + 1) ^ nsw) << 4));
+        const uint32_t sc = *reinterpret_cast<const uint32_t*>(srow0 + sr * kMtRawBytes + 4 * a);
         const uint32_t sd[4] = {mt_scale_h2(sc & 0xffu), mt_scale_h2((sc >> 8) & 0xffu),
                                 mt_scale_h2((sc >> 16) & 0xffu), mt_scale_h2(sc >> 24)};
         const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-        uint8_t* at = arow + sa * kMtATile;
+        uint8_t* bt = brow0 + s * kMtSlot;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {  // 8 K values: code bytes 4j..4j+3, scale group j / 2
-          const uint32_t s = sd[j >> 1];
+          const uint32_t sj = sd[j >> 1];
           uint4 o = mt_e2m1_word(wv[j]);
-          o.x = mt_hmul2(o.x, s);
-          o.y = mt_hmul2(o.y, s);
-          o.z = mt_hmul2(o.z, s);
-          o.w = mt_hmul2(o.w, s);
-          *reinterpret_cast<uint4*>(at + ((j ^ msw) << 4)) = o;
+          o.x = mt_hmul2(o.x, sj);
+          o.y = mt_hmul2(o.y, sj);
+          o.z = mt_hmul2(o.z, sj);
+          o.w = mt_hmul2(o.w, sj);
+          *reinterpret_cast<uint4*>(bt + ((j ^ nsw) << 4)) = o;
         }
         mt_fence_async_smem();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&a_full[sa]);
-          if (a >= 2) mbar_arrive(&raw_empty[sr]);  // this warp's second and last slice of stage r
+          mbar_arrive(&full[s]);
+          if (a == 3) mbar_arrive(&raw_empty[sr]);  // last slice of raw stage r
         }
       }
     }
   } else {
     // ------------------------------------ epilogue ------------------------------------
     const int q4 = warp & 3;
+    const int m = 32 * q4 + lane;  // pair of the chunk = TMEM lane
     const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
     int ui = 0;
     for (int u = u0; u < u1; ++u, ++ui) {
@@ -341,24 +346,50 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       const int buf = ui & 1;
       if (!mbar_wait(&acc_full[buf], (uint32_t)(ui >> 1) & 1u, err, abort_flag) || *abort_flag) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const float gsc = gs[t.e];
-      const uint32_t taddr = tmem + lane_base + buf * 64;
-      for (int c0 = 0; c0 < t.n; c0 += 16) {
-        float v[16];
-        tmem_ld16(taddr + c0, v);
+      if (32 * q4 < t.n) {  // warp-uniform: this quarter holds pairs of the chunk
+        const bool mine = m < t.n;
+        const float sc = mine ? rs[t.row0 + m] * gs[t.e] : 0.f;
+        const uint32_t taddr = tmem + lane_base + buf * kMtNW;
+        if (GATED) {
+          __nv_bfloat16* dst = inter_out + (size_t)(t.row0 + (mine ? m : 0)) * I + t.rb * 128;
+#pragma unroll 1
+          for (int c0 = 0; c0 < 128; c0 += 16) {
+            uint32_t g[16], v[16];
+            mt_tmem_ld16(taddr + c0, g);
+            mt_tmem_ld16(taddr + 128 + c0, v);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            uint32_t o[8];
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) {
-          const int j = c0 + jj;
-          if (j >= t.n) break;
-          const float acc = v[jj] * rs[t.row0 + j];  // exact: a power of two
-          if (GATED) {
-            const float h = __bfloat162float(__float2bfloat16_rn(acc * gsc));
-            const float up = __shfl_down_sync(0xffffffffu, h, 16);
-            if (lane < 16)
-              inter_out[(size_t)(t.row0 + j) * I + t.rb * 64 + 16 * q4 + lane] =
-                  __float2bfloat16_rn(h / (1.f + expf(-h)) * up);
-          } else {
-            y_out[(size_t)pairs[t.row0 + j] * NR + t.rb * 128 + 32 * q4 + lane] = __float2bfloat16_rn(acc * gsc);
+            for (int i = 0; i < 8; ++i) {
+              float a2[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const float hg = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * i + h]) * sc));
+                const float hu = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[2 * i + h]) * sc));
+                a2[h] = hg / (1.f + expf(-hg)) * hu;
+              }
+              o[i] = pack_bf16x2(a2[0], a2[1]);
+            }
+            if (mine) {
+              *reinterpret_cast<uint4*>(dst + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+              *reinterpret_cast<uint4*>(dst + c0 + 8) = make_uint4(o[4], o[5], o[6], o[7]);
+            }
+          }
+        } else {
+          __nv_bfloat16* dst = y_out + (size_t)(mine ? pairs[t.row0 + m] : 0) * NR + t.rb * 256;
+#pragma unroll 1
+          for (int c0 = 0; c0 < 256; c0 += 16) {
+            uint32_t v[16];
+            mt_tmem_ld16(taddr + c0, v);
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            uint32_t o[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              o[i] = pack_bf16x2(__uint_as_float(v[2 * i]) * sc, __uint_as_float(v[2 * i + 1]) * sc);
+            if (mine) {
+              *reinterpret_cast<uint4*>(dst + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+              *reinterpret_cast<uint4*>(dst + c0 + 8) = make_uint4(o[4], o[5], o[6], o[7]);
+            }
           }
         }
       }
@@ -372,7 +403,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
   __syncthreads();
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
   }
 }
 
@@ -446,7 +477,7 @@ static bool mt_f16_map(CUtensorMap* m, const void* base, long long inner, long l
 }
 
 bool moe_tc_ok(int H, int I, int E) {
-  return H % kMtKC == 0 && I % kMtKC == 0 && I % 64 == 0 && H % 128 == 0 && H <= 8192 && E <= 256 &&
+  return H % kMtKC == 0 && I % kMtKC == 0 && I % 128 == 0 && H % 256 == 0 && H <= 8192 && E <= 256 &&
          tensor_map_encoder() != nullptr;
 }
 
@@ -460,17 +491,19 @@ int launch_moe_rows_f16(const void* src, const int32_t* pairs, const int32_t* of
                             reinterpret_cast<const __nv_bfloat16*>(src), pairs, offsets, E, topk, K, dst, rs);
 }
 
-// GATED: act = xg [rows][K = H], weights W13; else act = inter [rows][K = I], weights W2.
+// GATED: act = xg [rows][K = H], weights W13, out inter; else act = inter as f16 [rows][K = I],
+// weights W2, out y.  rs: the activation rows' scales.
 template <bool GATED>
 int launch_moe_tc(const void* w, const void* sf, int E, const __half* act, int rows, const float* rs,
                   const int32_t* counts, const int32_t* offsets, const int32_t* pairs, const float* gs,
                   __nv_bfloat16* inter, __nv_bfloat16* y, int K, int NR, int I, int* err, cudaStream_t stream) {
   const long long wrows = (long long)E * (GATED ? 2 * I : NR);
-  const int box_rows = GATED ? 64 : 128;
-  CUtensorMap cm, sm, m16, m32, m64;
+  const int box_rows = GATED ? 128 : 256;
+  CUtensorMap cm, sm, m16, m32, m64, m128;
   if (!mt_u8_map(&cm, w, K / 2, wrows, kMtKC / 2, box_rows, true) ||
       !mt_u8_map(&sm, sf, K / 16, wrows, kMtKC / 16, box_rows, false) || !mt_f16_map(&m16, act, K, rows, 16) ||
-      !mt_f16_map(&m32, act, K, rows, 32) || !mt_f16_map(&m64, act, K, rows, 64))
+      !mt_f16_map(&m32, act, K, rows, 32) || !mt_f16_map(&m64, act, K, rows, 64) ||
+      !mt_f16_map(&m128, act, K, rows, 128))
     return OKC_ERR_INVALID;
   static bool configured = false;
   if (!configured) {
@@ -480,8 +513,8 @@ int launch_moe_tc(const void* w, const void* sf, int E, const __half* act, int r
     configured = true;
   }
   return okc_host::launch_k(moe_tc_kernel<GATED>, dim3(okc_host::num_sms()), dim3(kMtThreads), kMtSmem, stream,
-                            dim3(1), cm, sm, m16, m32, m64, counts, offsets, pairs, gs, rs, inter, y, K, NR, I, E,
-                            err);
+                            dim3(1), cm, sm, m16, m32, m64, m128, counts, offsets, pairs, gs, rs, inter, y, K, NR,
+                            I, E, err);
 }
 
 template int launch_moe_tc<true>(const void*, const void*, int, const __half*, int, const float*, const int32_t*,
