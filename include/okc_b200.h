@@ -237,6 +237,28 @@ int okc_attn_decode_fp8_noalloc_error(okc_stream_t stream);
  * Replaces `route` muse_prefill_layer/submission.py:179-184 and the routing call of
  * muse_decode_layer/decode/runtime.py:55-63 (softmax top-k of the bf16 logits).
  * ---------------------------------------------------------------------------------- */
+/* ------------------------------------------------------------------------------------
+ * Muse routing: score = sigmoid((logits[t][e] (+ logits_lo[t][e] when given)) * logit_scale),
+ * ids = top-k of score + bias[e] (bias may be NULL; it only chooses; ties -> lower id),
+ * weights = score / (sum of the chosen scores + score_eps) * route_scale.  logits fp32 [T][ld];
+ * logits_out fp32 [T][E] (the summed logits; may be NULL).  E <= 256, topk <= 32.  Replaces
+ * `route` of muse_prefill_layer/submission.py:179-184 and FusedMuseSparkRouting as
+ * muse_decode_layer/decode/runtime.py:30-32,63 configures it (logit_scale 0.1767766952966369,
+ * score_eps 1e-15, route_scale 1).
+ * ---------------------------------------------------------------------------------- */
+int okc_moe_route_sigmoid(const float* logits, int ld, const float* logits_lo, const float* bias,
+                          int32_t* ids, float* weights, float* logits_out, int T, int E, int topk,
+                          float logit_scale, float score_eps, float route_scale, okc_stream_t stream);
+
+/* FP32 router projection through bf16 halves: w_hilo bf16 [2E][K] holds hi = bf16(router) in
+ * rows 0..E-1 and lo = bf16(router - hi) in rows E..2E-1 (the reference's prepare,
+ * muse_bf16_proj/projection/runtime.py:42-47); logits[t][e] = x·hi[e] + x·lo[e], two
+ * independent fp32 accumulations summed at the end (`_gemm` ROUTER,
+ * muse_bf16_proj/projection/kernels/gemm.py:8-39).  x bf16 [T][ldx]; logits fp32 [T][ldl]. */
+size_t okc_router_logits_workspace_bytes(int T, int E, int K);
+int okc_router_logits(const void* x, int ldx, const void* w_hilo, float* logits, int ldl, int T, int E,
+                      int K, void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
 int okc_moe_route(const void* x, const void* wr, int32_t* ids, float* weights,
                   float* logits_out, int T, int H, int E, int topk, int renormalize,
                   okc_stream_t stream);

@@ -81,6 +81,9 @@ SIGNATURES: dict[str, tuple] = {
     "okc_moe_experts_w4a16_post": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i,
                                         _i, _p, _f, _p, _sz, _p]),
     "okc_residual_boundary": (_i, [_p, _p, _i, _p, _p, _p, _p, _p, _p, _p, _i, _i, _f, _f, _p]),
+    "okc_moe_route_sigmoid": (_i, [_p, _i, _p, _p, _p, _p, _p, _i, _i, _i, _f, _f, _f, _p]),
+    "okc_router_logits_workspace_bytes": (_sz, [_i, _i, _i]),
+    "okc_router_logits": (_i, [_p, _i, _p, _p, _i, _i, _i, _i, _p, _sz, _p]),
     "okc_moe_experts_w4a16": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p,
                                    _i, _i, _i, _i, _i, _i, _p, _sz, _p]),
 }

@@ -278,6 +278,30 @@ int okc_moe_route(const void* x, const void* wr, int32_t* ids, float* weights, f
   return okc::launch_moe_route(x, wr, ids, weights, logits_out, T, H, E, topk, renormalize, stream);
 }
 
+int okc_moe_route_sigmoid(const float* logits, int ld, const float* logits_lo, const float* bias, int32_t* ids,
+                          float* weights, float* logits_out, int T, int E, int topk, float logit_scale,
+                          float score_eps, float route_scale, okc_stream_t stream) {
+  if (!logits || !ids || !weights || T <= 0 || E <= 0 || E > 256 || topk <= 0 || topk > 32 || topk > E || ld < E)
+    return OKC_ERR_INVALID;
+  return okc::launch_route_sigmoid(logits, ld, logits_lo, bias, ids, weights, logits_out, T, E, topk, logit_scale,
+                                   score_eps, route_scale, stream);
+}
+
+size_t okc_router_logits_workspace_bytes(int T, int E, int K) {
+  return okc_gemm_bf16_workspace_bytes(T, 2 * E, K) + ((size_t)T * 2 * E * 4 + 255) / 256 * 256;
+}
+
+int okc_router_logits(const void* x, int ldx, const void* w_hilo, float* logits, int ldl, int T, int E, int K,
+                      void* workspace, size_t workspace_bytes, okc_stream_t stream) {
+  if (!x || !w_hilo || !logits || T <= 0 || E <= 0 || K <= 0 || ldl < E) return OKC_ERR_INVALID;
+  if (!workspace || workspace_bytes < okc_router_logits_workspace_bytes(T, E, K)) return OKC_ERR_WORKSPACE;
+  const size_t gws = okc_gemm_bf16_workspace_bytes(T, 2 * E, K);
+  float* y = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + gws);
+  int st = okc_gemm_bf16_ex(x, ldx, w_hilo, K, y, 2 * E, nullptr, T, 2 * E, K, 1, 0, 0, workspace, gws, stream);
+  if (st) return st;
+  return okc::launch_add_halves(y, logits, ldl, T, E, stream);
+}
+
 int okc_moe_permute(const int32_t* ids, int T, int topk, int expert_lo, int E_local, int bm,
                     int32_t* counts, int32_t* offsets, int32_t* pairs, int32_t* tiles, int max_tiles,
                     okc_stream_t stream) {

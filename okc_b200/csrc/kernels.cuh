@@ -83,6 +83,10 @@ int launch_moe_permute(const int32_t* ids, int n, int expert_lo, int E, int bm, 
                        int32_t* offsets, int32_t* pairs, int32_t* tiles, int max_tiles, int* err,
                        cudaStream_t stream);
 size_t moe_experts_ws_bytes(int T, int topk, int H, int I);
+int launch_route_sigmoid(const float* logits, int ld, const float* lo, const float* bias, int32_t* ids, float* wts,
+                         float* logits_out, int T, int E, int topk, float scale, float eps, float route_scale,
+                         cudaStream_t stream);
+int launch_add_halves(const float* y, float* out, int ldo, int T, int E, cudaStream_t stream);
 bool moe_tc_ok(int H, int I, int E);
 int launch_moe_rows_f16(const void* src, const int32_t* pairs, const int32_t* offsets, int E, int topk, int K,
                         int max_rows, __half* dst, float* rs, cudaStream_t stream);

@@ -1271,6 +1271,90 @@ int launch_moe_route(const void* x, const void* wr, int32_t* ids, float* wts, fl
   return okc_host::launch_status();
 }
 
+// Muse routing (muse_prefill_layer/submission.py:179-184, FusedMuseSparkRouting with
+// route_scale 1, router_output_multiplier 0.1767766952966369, division eps 1e-15): one warp per
+// token; score = sigmoid(logit * scale) in fp32; the top-k of score + bias (the bias only
+// chooses; ties -> lower expert id); weight = score / (sum of the chosen scores + eps) *
+// route_scale.  With `lo` the logit is lo-added first (logits[t][e] + lo[t][e]: the two halves of
+// the fp32 router split into bf16 hi and lo parts, high += low as the reference's `_gemm`).
+__global__ void __launch_bounds__(256) route_sigmoid_kernel(const float* __restrict__ logits, int ld,
+                                                            const float* __restrict__ lo,
+                                                            const float* __restrict__ bias, int32_t* __restrict__ ids,
+                                                            float* __restrict__ wts, float* __restrict__ logits_out,
+                                                            int T, int E, int topk, float scale, float eps,
+                                                            float route_scale) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= T) return;
+  constexpr int kMaxPer = 8;  // E <= 256
+  float sc[kMaxPer], key[kMaxPer];
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = lane + 32 * i;
+    sc[i] = 0.f;
+    key[i] = -INFINITY;
+    if (e < E) {
+      float z = logits[(size_t)t * ld + e];
+      if (lo) z += lo[(size_t)t * ld + e];
+      if (logits_out) logits_out[(size_t)t * E + e] = z;
+      sc[i] = 1.f / (1.f + expf(-(z * scale)));
+      key[i] = bias ? sc[i] + bias[e] : sc[i];
+    }
+  }
+  float chosen = 0.f, sum = 0.f;
+  int cid = 0;
+  for (int s = 0; s < topk; ++s) {
+    float bv = -INFINITY, bs = 0.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && (key[i] > bv || (key[i] == bv && e < bi))) { bv = key[i]; bi = e; bs = sc[i]; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; bs = os; }
+    }
+    sum += bs;  // in selection order, the same on every lane
+    if (lane == s) { chosen = bs; cid = bi; }
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i)
+      if (lane + 32 * i == bi) key[i] = -INFINITY;
+  }
+  if (lane < topk) {
+    ids[(size_t)t * topk + lane] = cid;
+    wts[(size_t)t * topk + lane] = chosen / (sum + eps) * route_scale;
+  }
+}
+
+int launch_route_sigmoid(const float* logits, int ld, const float* lo, const float* bias, int32_t* ids, float* wts,
+                         float* logits_out, int T, int E, int topk, float scale, float eps, float route_scale,
+                         cudaStream_t stream) {
+  return okc_host::launch_k(route_sigmoid_kernel, dim3((T + 7) / 8), dim3(256), 0, stream, dim3(1), logits, ld, lo,
+                            bias, ids, wts, logits_out, T, E, topk, scale, eps, route_scale);
+}
+
+// out[t][e] = y[t][e] + y[t][E + e]: the fp32 router logits from the GEMM of x with the stacked
+// bf16 hi / lo halves of the router (two independent fp32 accumulations, then high += low).
+__global__ void __launch_bounds__(256) add_halves_kernel(const float* __restrict__ y, float* __restrict__ out,
+                                                         int ldo, int T, int E) {
+  pdl_trigger();
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * E) return;
+  const int t = i / E, e = i - t * E;
+  out[(size_t)t * ldo + e] = y[(size_t)t * 2 * E + e] + y[(size_t)t * 2 * E + E + e];
+}
+
+int launch_add_halves(const float* y, float* out, int ldo, int T, int E, cudaStream_t stream) {
+  return okc_host::launch_k(add_halves_kernel, dim3((T * E + 255) / 256), dim3(256), 0, stream, dim3(1), y, out, ldo,
+                            T, E);
+}
+
 int launch_moe_permute(const int32_t* ids, int n, int expert_lo, int E, int bm, int32_t* counts,
                        int32_t* offsets, int32_t* pairs, int32_t* tiles, int max_tiles, int* err,
                        cudaStream_t stream) {

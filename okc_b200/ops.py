@@ -253,6 +253,41 @@ def moe_route(x: torch.Tensor, wr: torch.Tensor, topk: int, renormalize: bool = 
     return (ids, wts, logits) if return_logits else (ids, wts)
 
 
+def route_sigmoid(logits: torch.Tensor, bias: torch.Tensor | None, topk: int,
+                  logits_lo: torch.Tensor | None = None, scale: float = 0.1767766952966369,
+                  eps: float = 1e-15, route_scale: float = 1.0):
+    """Muse's sigmoid + bias routing (okc_moe_route_sigmoid): ids int32 [T, k], weights fp32."""
+    dev = _dev_index(logits)
+    _need(logits, torch.float32, "logits")
+    T, E = logits.shape
+    ids = torch.empty((T, topk), dtype=torch.int32, device=logits.device)
+    wts = torch.empty((T, topk), dtype=torch.float32, device=logits.device)
+    st = _lib.load().okc_moe_route_sigmoid(logits.data_ptr(), logits.stride(0),
+                                           logits_lo.data_ptr() if logits_lo is not None else None,
+                                           bias.data_ptr() if bias is not None else None, ids.data_ptr(),
+                                           wts.data_ptr(), None, T, E, topk, float(scale), float(eps),
+                                           float(route_scale), _stream(dev))
+    check(st, "okc_moe_route_sigmoid")
+    return ids, wts
+
+
+def router_logits(x: torch.Tensor, w_hilo: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """fp32 logits of the bf16 x against the fp32 router held as stacked bf16 [hi; lo] halves."""
+    dev = _dev_index(x)
+    _need(x, torch.bfloat16, "x")
+    _need(w_hilo, torch.bfloat16, "w_hilo")
+    T, K = x.shape
+    E = w_hilo.shape[0] // 2
+    if out is None:
+        out = torch.empty((T, E), dtype=torch.float32, device=x.device)
+    lib = _lib.load()
+    ws = workspace(dev, "router", lib.okc_router_logits_workspace_bytes(T, E, K))
+    st = lib.okc_router_logits(x.data_ptr(), x.stride(0), w_hilo.data_ptr(), out.data_ptr(), out.stride(0), T, E, K,
+                               ws.data_ptr(), ws.numel(), _stream(dev))
+    check(st, "okc_router_logits")
+    return out
+
+
 def moe_max_tiles(T: int, topk: int, E_local: int, bm: int) -> int:
     n = T * topk
     return min(E_local, n) + (n + bm - 1) // bm

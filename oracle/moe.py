@@ -85,13 +85,30 @@ def route(x: torch.Tensor, wr: torch.Tensor, topk: int, renormalize: bool = True
     return torch.from_numpy(ids), torch.from_numpy(wts), torch.from_numpy(lg)
 
 
+def route_sigmoid(logits: torch.Tensor, bias: torch.Tensor | None, topk: int,
+                  scale: float = 0.1767766952966369, eps: float = 1e-15, route_scale: float = 1.0):
+    """Muse's routing from fp32 logits (muse_prefill_layer/submission.py:179-184): sigmoid
+    scores, the bias only chooses, the chosen scores renormalised (ties: the lower id, which is
+    what a stable descending sort gives)."""
+    scores = torch.sigmoid(logits.float() * scale)
+    key = scores + bias.float() if bias is not None else scores
+    ids = torch.sort(key, dim=-1, descending=True, stable=True).indices[:, :topk]
+    picked = scores.gather(1, ids)
+    return ids.to(torch.int32), picked / (picked.sum(-1, keepdim=True) + eps) * route_scale
+
+
 def muse_route(h: torch.Tensor, router: torch.Tensor, bias: torch.Tensor, topk: int):
     """Muse's routing: sigmoid scores, bias only to choose, chosen scores renormalised
     (muse_prefill_layer/submission.py:179-184)."""
-    scores = torch.sigmoid((h.float() @ router.T) * 0.1767766952966369)
-    ids = (scores + bias).topk(topk, dim=-1).indices
-    picked = scores.gather(1, ids)
-    return ids, picked / (picked.sum(-1, keepdim=True) + 1e-15)
+    return route_sigmoid(h.float() @ router.float().T, bias, topk)
+
+
+def router_hilo(router: torch.Tensor) -> torch.Tensor:
+    """The reference's split of the fp32 router into bf16 halves, stacked [hi; lo]
+    (muse_bf16_proj/projection/runtime.py:42-47)."""
+    hi = router.to(torch.bfloat16)
+    lo = (router - hi.float()).to(torch.bfloat16)
+    return torch.cat([hi, lo], 0)
 
 
 # -------------------------------------------------------------------------- permutation
