@@ -1,5 +1,5 @@
 // NVFP4 (W4A16) expert GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM), for MoE steps
-// whose experts see tens of tokens (the row-owning mma.sync kernel in moe.cu serves the
+// whose experts see more than a few tokens (the row-owning mma.sync kernel in moe.cu serves the
 // few-token decode steps).  Same contract as the moe.cu expert kernels
 // (muse_moe_w4a16/submission.py:163-248): gate/up h = bf16(acc * gs), inter = bf16(silu(g) * u),
 // down y = bf16(acc * gs), fp32 accumulation.
@@ -12,30 +12,30 @@
 //    bf16 MMA of the reference's operands would.  Before the gate/up GEMM it gathers the local
 //    (token, slot) pairs expert-major (row j = x[pairs[j] / topk]); before the down GEMM it
 //    converts the bf16 intermediate rows.
-//  * Operand roles follow the measured issue costs on B200 (one thread issuing kind::f16 MMAs:
-//    ~58 cycles per instruction up to N = 128, ~145 per commit; an M = 128, N = 256, K = 16 MMA
-//    runs 128 cycles on the tensor pipe): the A operand (M = 128) is a chunk of up to 128 of an
-//    expert's pairs (activations, padded), the B operand (N = 256) is 256 dequantised weight
-//    rows, so each MMA covers 4096 weight values and the tensor pipe, not instruction issue, sets
-//    the pace: ~32 weight values per cycle per SM, about 4.6 TB/s of NVFP4 at 148 SMs.
-//  * A unit = (active expert, chunk of <= 128 pairs, block of 256 weight rows: 128 gate + the same
-//    128 up rows (GATED) or 256 down rows) over the full K.  Units of all experts are split
-//    evenly over a persistent grid (one CTA per SM).
+//  * The dequantised weights never touch shared memory: they are the MMA's A operand in tensor
+//    memory (lane = weight row, column c = the f16 pair of K 2c, 2c+1), written by tcgen05.st
+//    from the registers that decoded them.  Shared memory only carries the packed codes (one
+//    TMA write, one read) and the activation tiles, so its bandwidth is not the limit; per 64
+//    K the tensor pipe then needs 4 MMAs (M = 128 weight rows, N = the chunk's pairs, K = 16),
+//    issued from one thread at ~50 cycles each.
+//  * A unit = (active expert, chunk of <= 64 of its pairs, 128 weight rows: 64 gate + the same 64
+//    up rows (GATED) or 128 down rows) over the full K.  Units of all experts are split evenly
+//    over a persistent grid (one CTA per SM).
 //  * Warp 0 streams the unit's packed codes and e4m3 scales with 2-D TMA boxes (256 K per stage:
-//    one 128-byte row of codes per weight row, 128-byte swizzle, and 16 scale bytes per row) into
-//    a 2-deep raw ring (36 KB a stage).  Warp 2 loads the activation tile of each 64-K slice
-//    (f16, 128-byte swizzle, a 16/32/64/128-row box sized to the chunk) into the slice's slot.
-//  * Warps 3..10 dequantise, lane = one of the 256 weight rows: cvt.rn.f16x2.e2m1x2, x the e4m3
-//    group scale in f16 (exact), stored straight into the UMMA K-major SWIZZLE_128B layout of the
-//    slot's 256 x 64 f16 B tile; fence.proxy.async, then an arrive on the slot's full barrier
-//    (which also waits for the activation tile's bytes).  3 slots of 48 KB.  f16 rather than bf16
-//    because the e2m1 -> f16x2 conversion is one instruction; the same product in bf16 takes
-//    about four more integer operations per pair.
-//  * Warp 1 (one thread) issues 4 MMAs per slice into a double-buffered TMEM accumulator
-//    (2 x 256 columns) and frees the slot with one tcgen05.commit.
-//  * Warps 11..14 drain TMEM (tcgen05.ld 32x32b: lane = pair, column = weight row), apply the row
-//    scale and gs, and store inter (bf16, compact pair order; gate column j and up column
-//    128 + j meet in one thread) or y (bf16, the pair's row).
+//    one 128-byte row of codes per weight row, 128-byte swizzle, plus 16 scale bytes a row) into
+//    a 6-deep raw ring.  Warp 2 loads the stage's activation tiles (4 boxes of 64 K x 16/32/64
+//    rows, f16, 128-byte swizzle) into one of 3 stage slots.
+//  * Warps 3..10 dequantise, two per TMEM lane quarter (one per 128-K half of a stage), lane =
+//    one weight row: cvt.rn.f16x2.e2m1x2, x the e4m3 group scale in f16 (exact), tcgen05.st into
+//    the stage's A slot (128 columns; 3 slots), tcgen05.wait::st, tcgen05.fence, mbarrier arrive.
+//    f16 rather than bf16 because the e2m1 -> f16x2 conversion is one instruction; the same
+//    product in bf16 takes about four more integer operations per pair.
+//  * Warp 1 (one thread) issues the 16 MMAs of a stage into a double-buffered TMEM accumulator and
+//    frees the stage's A slot and activation tiles with one tcgen05.commit.  For GATED the A rows
+//    are ordered so that each 32-lane quarter holds 16 gate rows and the same 16 up rows: lanes
+//    l and l + 16 of an epilogue warp hold g and u of one output column.
+//  * Warps 11..14 drain TMEM (tcgen05.ld 32x32b), apply the row scale and gs, and store inter
+//    (bf16, compact pair order) or y (bf16, scattered to the pair's row).
 // Every wait is bounded (mbar_wait); on expiry a role sets the abort flag, the others stop at
 // their next wait, copies and MMAs in flight are waited for (bounded), TMEM is freed.
 #include "kernels.cuh"
@@ -43,22 +43,22 @@
 
 namespace okc {
 
-constexpr int kMtNT = 128;                         // pairs per unit (MMA M)
-constexpr int kMtNW = 256;                         // weight rows per unit (MMA N)
-constexpr int kMtKC = 256;                         // K per raw stage
-constexpr int kMtRaw = 2;                          // raw ring depth
-constexpr int kMtNS = 3;                           // slice slots (activation tile + weight tile)
-constexpr int kMtCodes = kMtNW * (kMtKC / 2);      // 32 KB of codes per raw stage
-constexpr int kMtRawBytes = kMtCodes + kMtNW * (kMtKC / 16);  // + 4 KB of scales
-constexpr int kMtATile = kMtNT * 128;              // 128 pairs x 64 K f16
-constexpr int kMtBTile = kMtNW * 128;              // 256 weight rows x 64 K f16
-constexpr int kMtSlot = kMtATile + kMtBTile;
+constexpr int kMtNT = 64;                          // pairs per unit (MMA N <= 64)
+constexpr int kMtKC = 256;                         // K per stage
+constexpr int kMtRaw = 6;                          // raw ring depth
+constexpr int kMtNS = 3;                           // stage slots: A in TMEM + activation tiles
+constexpr int kMtCodes = 128 * (kMtKC / 2);        // 16 KB of codes per raw stage
+constexpr int kMtRawBytes = kMtCodes + 128 * (kMtKC / 16);  // + 2 KB of scales
+constexpr int kMtAtom = kMtNT * 128;               // <= 64 pairs x 64 K f16
+constexpr int kMtAct = 4 * kMtAtom;                // a stage's activation tiles
 constexpr int kMtThreads = 15 * 32;
-constexpr int kMtBody = kMtRaw * kMtRawBytes + kMtNS * kMtSlot;
+constexpr int kMtBody = kMtRaw * kMtRawBytes + kMtNS * kMtAct;
 constexpr int kMtBars = 2 * kMtRaw + 2 * kMtNS + 2 + 2 + 1;
 constexpr int kMtSmem = 1024 + kMtBody + kMtBars * 8 + 16 + (2 * 257 + 2 * 256) * 4;
-static_assert(kMtRawBytes % 1024 == 0 && kMtATile % 1024 == 0 && kMtBTile % 1024 == 0, "1024-aligned tiles");
+constexpr uint32_t kMtAcol = 128;                  // TMEM: accumulators in columns 0..127, A slots after
+static_assert(kMtRawBytes % 1024 == 0 && kMtAtom % 1024 == 0, "1024-aligned tiles");
 static_assert(kMtSmem <= 232448, "shared memory");
+static_assert(kMtAcol + kMtNS * 128 <= 512, "tensor memory");
 
 __device__ __forceinline__ void mt_tma_u8(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
                                           uint64_t policy) {
@@ -69,11 +69,18 @@ __device__ __forceinline__ void mt_tma_u8(void* dst, const CUtensorMap* map, int
       : "memory");
 }
 
-__device__ __forceinline__ void mt_fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int n) {
+  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
 
-// kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M x N.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
-  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+// D (TMEM) (+)= A (TMEM: lane = row, column = f16 pair along K) x B (shared memory descriptor)^T.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t b, uint32_t idesc,
+                                            uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(b), "r"(idesc), "r"(acc));
 }
 
 // One word of packed codes (bytes b0..b3 = K pairs (2i, 2i+1), low nibble first) -> four f16x2.
@@ -92,21 +99,25 @@ __device__ __forceinline__ uint32_t mt_hmul2(uint32_t a, uint32_t b) {
   return *reinterpret_cast<uint32_t*>(&r);
 }
 
-__device__ __forceinline__ uint32_t mt_scale_h2(uint32_t sf_byte) {
-  const __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)sf_byte, __NV_E4M3);
-  return (uint32_t)h.x | ((uint32_t)h.x << 16);
+// Two e4m3 scale bytes -> f16x2 of each one duplicated: (s0, s0), (s1, s1).
+__device__ __forceinline__ void mt_scales2(uint32_t two, uint32_t& d0, uint32_t& d1) {
+  uint32_t h;
+  asm("{\n .reg .b16 t;\n cvt.u16.u32 t, %1;\n cvt.rn.f16x2.e4m3x2 %0, t;\n}" : "=r"(h) : "r"(two));
+  d0 = prmt(h, 0u, 0x1010u);
+  d1 = prmt(h, 0u, 0x3232u);
 }
 
-__device__ __forceinline__ void mt_tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+__device__ __forceinline__ void mt_tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
 }
 
 struct MtUnit {
-  int e, rb, row0, n;  // expert, weight-row block, first compact pair row, pairs (<= 128)
+  int e, rb, row0, n;  // expert, weight-row block, first compact pair row, pairs (<= 64)
 };
 
 // Unit u: active expert i with upre[i] <= u < upre[i+1], then chunk-major, row block minor.
@@ -131,19 +142,19 @@ template <bool GATED>
 __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
     const __grid_constant__ CUtensorMap cmap, const __grid_constant__ CUtensorMap smap,
     const __grid_constant__ CUtensorMap a16, const __grid_constant__ CUtensorMap a32,
-    const __grid_constant__ CUtensorMap a64, const __grid_constant__ CUtensorMap a128,
-    const int32_t* __restrict__ counts, const int32_t* __restrict__ offsets, const int32_t* __restrict__ pairs,
-    const float* __restrict__ gs, const float* __restrict__ rs, __nv_bfloat16* __restrict__ inter_out,
-    __nv_bfloat16* __restrict__ y_out, int K, int NR, int I, int E, int* err) {
+    const __grid_constant__ CUtensorMap a64, const int32_t* __restrict__ counts,
+    const int32_t* __restrict__ offsets, const int32_t* __restrict__ pairs, const float* __restrict__ gs,
+    const float* __restrict__ rs, __nv_bfloat16* __restrict__ inter_out, __nv_bfloat16* __restrict__ y_out, int K,
+    int NR, int I, int E, int* err) {
   extern __shared__ uint8_t mt_raw_smem[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mt_raw_smem) + 1023) & ~uintptr_t(1023));
   uint8_t* rawr = base;
-  uint8_t* slots = rawr + kMtRaw * kMtRawBytes;
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(slots + kMtNS * kMtSlot);
+  uint8_t* actt = rawr + kMtRaw * kMtRawBytes;
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(actt + kMtNS * kMtAct);
   uint64_t* raw_empty = raw_full + kMtRaw;
-  uint64_t* full = raw_empty + kMtRaw;
-  uint64_t* empty = full + kMtNS;
-  uint64_t* acc_full = empty + kMtNS;
+  uint64_t* sfull = raw_empty + kMtRaw;
+  uint64_t* sempty = sfull + kMtNS;
+  uint64_t* acc_full = sempty + kMtNS;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -155,12 +166,12 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rows_w = GATED ? 2 * I : NR;
-  const int nrb = GATED ? I / 128 : NR / 256;
+  const int nrb = GATED ? I / 64 : NR / 128;
   const int nk = K / kMtKC;
   pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMtRaw; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 8); }
-    for (int i = 0; i < kMtNS; ++i) { mbar_init(&full[i], 9); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < kMtNS; ++i) { mbar_init(&sfull[i], 9); mbar_init(&sempty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -217,17 +228,17 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       uint32_t r = 0;
       for (int u = u0; u < u1 && !*abort_flag; ++u) {
         const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
-        const int wrow = t.e * rows_w + t.rb * (GATED ? 128 : 256);
+        const int wrow = t.e * rows_w + t.rb * (GATED ? 64 : 128);
         for (int ks = 0; ks < nk; ++ks, ++r) {
           const int s = (int)(r % kMtRaw);
           if (!mbar_wait(&raw_empty[s], ((r / kMtRaw) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; break; }
           mbar_arrive_expect_tx(&raw_full[s], kMtRawBytes);
           uint8_t* d = rawr + s * kMtRawBytes;
-          if (GATED) {  // rows 0-127: gate rows, 128-255: the same up rows
+          if (GATED) {  // raw rows 0-63: gate rows, 64-127: the same up rows
             mt_tma_u8(d, &cmap, ks * (kMtKC / 2), wrow, &raw_full[s], pol);
             mt_tma_u8(d + kMtCodes / 2, &cmap, ks * (kMtKC / 2), wrow + I, &raw_full[s], pol);
             mt_tma_u8(d + kMtCodes, &smap, ks * (kMtKC / 16), wrow, &raw_full[s], pol);
-            mt_tma_u8(d + kMtCodes + 128 * 16, &smap, ks * (kMtKC / 16), wrow + I, &raw_full[s], pol);
+            mt_tma_u8(d + kMtCodes + 64 * 16, &smap, ks * (kMtKC / 16), wrow + I, &raw_full[s], pol);
           } else {
             mt_tma_u8(d, &cmap, ks * (kMtKC / 2), wrow, &raw_full[s], pol);
             mt_tma_u8(d + kMtCodes, &smap, ks * (kMtKC / 16), wrow, &raw_full[s], pol);
@@ -244,40 +255,45 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       bool ok = true;
       for (int u = u0; u < u1 && ok && !*abort_flag; ++u) {
         const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
-        const int box = t.n <= 16 ? 16 : (t.n <= 32 ? 32 : (t.n <= 64 ? 64 : 128));
-        const CUtensorMap* map = box == 16 ? &a16 : (box == 32 ? &a32 : (box == 64 ? &a64 : &a128));
-        for (int kq = 0; kq < 4 * nk; ++kq, ++q) {
+        const int box = t.n <= 16 ? 16 : (t.n <= 32 ? 32 : 64);
+        const CUtensorMap* map = box == 16 ? &a16 : (box == 32 ? &a32 : &a64);
+        for (int ks = 0; ks < nk; ++ks, ++q) {
           const int s = (int)(q % kMtNS);
-          if (!mbar_wait(&empty[s], ((q / kMtNS) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; ok = false; break; }
-          mbar_arrive_expect_tx(&full[s], (uint32_t)box * 128u);
-          tma_load_2d(slots + s * kMtSlot, map, kq * 64, t.row0, &full[s]);
+          if (!mbar_wait(&sempty[s], ((q / kMtNS) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; ok = false; break; }
+          mbar_arrive_expect_tx(&sfull[s], (uint32_t)box * 128u * 4u);
+          uint8_t* d = actt + s * kMtAct;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tma_load_2d(d + j * kMtAtom, map, ks * kMtKC + 64 * j, t.row0, &sfull[s]);
         }
       }
-      // the activation copies issued land before the CTA can leave: a slot's full phase
-      // completes only with them (and the dequant arrivals, bounded by the same wait)
+      // the copies issued land before the CTA can leave: a slot's full phase completes only
+      // with them (and the dequant arrivals, bounded by the same wait)
       for (uint32_t i = q > (uint32_t)kMtNS ? q - kMtNS : 0u; i < q; ++i)
-        if (!mbar_wait(&full[i % kMtNS], (i / kMtNS) & 1u, err)) break;
+        if (!mbar_wait(&sfull[i % kMtNS], (i / kMtNS) & 1u, err)) break;
     }
   } else if (warp == 1) {
     // ---------------------------------- MMA issuer ----------------------------------
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_f16(kMtNT, kMtNW);
       uint32_t q = 0;
       int ui = 0;
       bool ok = true;
       for (int u = u0; u < u1 && ok; ++u, ++ui) {
+        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
+        const uint32_t idesc = umma_idesc_f16((t.n + 15) & ~15);
         const int buf = ui & 1;
         if (!mbar_wait(&acc_empty[buf], ((uint32_t)(ui >> 1) & 1u) ^ 1u, err, abort_flag)) { ok = false; break; }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        for (int kq = 0; kq < 4 * nk; ++kq, ++q) {
+        for (int ks = 0; ks < nk; ++ks, ++q) {
           const int s = (int)(q % kMtNS);
-          if (!mbar_wait(&full[s], (q / kMtNS) & 1u, err, abort_flag)) { ok = false; break; }
-          const uint32_t sa = smem_u32(slots + s * kMtSlot);
-          const uint64_t da = umma_desc_sw128(sa), db = umma_desc_sw128(sa + kMtATile);
+          if (!mbar_wait(&sfull[s], (q / kMtNS) & 1u, err, abort_flag)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const uint32_t sa = smem_u32(actt + s * kMtAct);
+          const uint32_t ta = tmem + kMtAcol + (uint32_t)s * 128u;
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            umma_bf16(tmem + buf * kMtNW, da + 2 * j, db + 2 * j, idesc, (kq | j) ? 1u : 0u);
-          umma_commit(&empty[s]);
+          for (int k16 = 0; k16 < 16; ++k16) {
+            const uint64_t db = umma_desc_sw128(sa + (k16 >> 2) * kMtAtom) + 2 * (k16 & 3);
+            umma_f16_ts(tmem + buf * 64, ta + 8 * k16, db, idesc, (ks | k16) ? 1u : 0u);
+          }
+          umma_commit(&sempty[s]);
         }
         if (ok) umma_commit(&acc_full[buf]);
       }
@@ -291,54 +307,58 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
     }
   } else if (warp <= 10) {
     // -------------------------------- dequantisation --------------------------------
-    const int n = 32 * (warp - 3) + lane;  // weight row of the unit = B row
-    const int nsw = n & 7;
-    const uint8_t* crow0 = rawr + n * 128;                   // codes, 128-byte swizzled rows
-    const uint8_t* srow0 = rawr + kMtCodes + n * 16;         // scales
-    uint8_t* brow0 = slots + kMtATile + (n >> 3) * 1024 + nsw * 128;
+    const int qd = warp & 3, half = (warp - 3) >> 2;
+    const int m = 32 * qd + lane;  // A row = TMEM lane
+    const int rho = GATED ? (lane < 16 ? 16 * qd + lane : 64 + 16 * qd + lane - 16) : m;  // raw row
+    const int sw = rho & 7;
+    const uint32_t tbase = tmem + ((uint32_t)(32 * qd) << 16) + kMtAcol + 64u * half;
     uint32_t q = 0;
     bool ok = true;
     for (int u = u0; u < u1 && ok; ++u) {
-      for (int kq = 0; kq < 4 * nk; ++kq, ++q) {
-        const uint32_t r = q >> 2;
-        const int a = (int)(q & 3u);
-        const int sr = (int)(r % kMtRaw), s = (int)(q % kMtNS);
-        if (!mbar_wait(&raw_full[sr], (r / kMtRaw) & 1u, err, abort_flag) ||
-            !mbar_wait(&empty[s], ((q / kMtNS) & 1u) ^ 1u, err, abort_flag)) {
+      for (int ks = 0; ks < nk; ++ks, ++q) {
+        const int sr = (int)(q % kMtRaw), s = (int)(q % kMtNS);
+        if (!mbar_wait(&raw_full[sr], (q / kMtRaw) & 1u, err, abort_flag) ||
+            !mbar_wait(&sempty[s], ((q / kMtNS) & 1u) ^ 1u, err, abort_flag)) {
           *abort_flag = 1;
           ok = false;
           break;
         }
-        const uint8_t* crow = crow0 + sr * kMtRawBytes;
-        const uint4 c0 = *reinterpret_cast<const uint4*>(crow + (((2 * a) ^ nsw) << 4));
-        const uint4 c1 = *reinterpret_cast<const uint4*>(crow + (((2 * a + 1) ^ nsw) << 4));
-        const uint32_t sc = *reinterpret_cast<const uint32_t*>(srow0 + sr * kMtRawBytes + 4 * a);
-        const uint32_t sd[4] = {mt_scale_h2(sc & 0xffu), mt_scale_h2((sc >> 8) & 0xffu),
-                                mt_scale_h2((sc >> 16) & 0xffu), mt_scale_h2(sc >> 24)};
-        const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-        uint8_t* bt = brow0 + s * kMtSlot;
+        const uint8_t* rw = rawr + sr * kMtRawBytes;
+        const uint8_t* crow = rw + rho * 128;
+        const uint2 sc8 = *reinterpret_cast<const uint2*>(rw + kMtCodes + rho * 16 + 8 * half);
+        uint32_t sd[8];
+        mt_scales2(sc8.x & 0xffffu, sd[0], sd[1]);
+        mt_scales2(sc8.x >> 16, sd[2], sd[3]);
+        mt_scales2(sc8.y & 0xffffu, sd[4], sd[5]);
+        mt_scales2(sc8.y >> 16, sd[6], sd[7]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {  // 8 K values: code bytes 4j..4j+3, scale group j / 2
-          const uint32_t sj = sd[j >> 1];
-          uint4 o = mt_e2m1_word(wv[j]);
-          o.x = mt_hmul2(o.x, sj);
-          o.y = mt_hmul2(o.y, sj);
-          o.z = mt_hmul2(o.z, sj);
-          o.w = mt_hmul2(o.w, sj);
-          *reinterpret_cast<uint4*>(bt + ((j ^ nsw) << 4)) = o;
+        for (int i = 0; i < 4; ++i) {  // 16 code bytes = K [128 half + 32 i, + 32), scale groups 2i, 2i+1
+          const uint4 c = *reinterpret_cast<const uint4*>(crow + (((4 * half + i) ^ sw) << 4));
+          const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
+          uint32_t o[16];
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t sj = sd[2 * i + (wi >> 1)];
+            const uint4 h = mt_e2m1_word(wv[wi]);
+            o[4 * wi + 0] = mt_hmul2(h.x, sj);
+            o[4 * wi + 1] = mt_hmul2(h.y, sj);
+            o[4 * wi + 2] = mt_hmul2(h.z, sj);
+            o[4 * wi + 3] = mt_hmul2(h.w, sj);
+          }
+          mt_tmem_st16(tbase + (uint32_t)s * 128u + 16u * i, o);
         }
-        mt_fence_async_smem();
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&full[s]);
-          if (a == 3) mbar_arrive(&raw_empty[sr]);  // last slice of raw stage r
+          mbar_arrive(&sfull[s]);
+          mbar_arrive(&raw_empty[sr]);
         }
       }
     }
   } else {
     // ------------------------------------ epilogue ------------------------------------
     const int q4 = warp & 3;
-    const int m = 32 * q4 + lane;  // pair of the chunk = TMEM lane
     const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
     int ui = 0;
     for (int u = u0; u < u1; ++u, ++ui) {
@@ -346,50 +366,24 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       const int buf = ui & 1;
       if (!mbar_wait(&acc_full[buf], (uint32_t)(ui >> 1) & 1u, err, abort_flag) || *abort_flag) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      if (32 * q4 < t.n) {  // warp-uniform: this quarter holds pairs of the chunk
-        const bool mine = m < t.n;
-        const float sc = mine ? rs[t.row0 + m] * gs[t.e] : 0.f;
-        const uint32_t taddr = tmem + lane_base + buf * kMtNW;
-        if (GATED) {
-          __nv_bfloat16* dst = inter_out + (size_t)(t.row0 + (mine ? m : 0)) * I + t.rb * 128;
-#pragma unroll 1
-          for (int c0 = 0; c0 < 128; c0 += 16) {
-            uint32_t g[16], v[16];
-            mt_tmem_ld16(taddr + c0, g);
-            mt_tmem_ld16(taddr + 128 + c0, v);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            uint32_t o[8];
+      const float gsc = gs[t.e];
+      const uint32_t taddr = tmem + lane_base + buf * 64;
+      for (int c0 = 0; c0 < t.n; c0 += 16) {
+        float v[16];
+        tmem_ld16(taddr + c0, v);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float a2[2];
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float hg = __bfloat162float(__float2bfloat16_rn(__uint_as_float(g[2 * i + h]) * sc));
-                const float hu = __bfloat162float(__float2bfloat16_rn(__uint_as_float(v[2 * i + h]) * sc));
-                a2[h] = hg / (1.f + expf(-hg)) * hu;
-              }
-              o[i] = pack_bf16x2(a2[0], a2[1]);
-            }
-            if (mine) {
-              *reinterpret_cast<uint4*>(dst + c0) = make_uint4(o[0], o[1], o[2], o[3]);
-              *reinterpret_cast<uint4*>(dst + c0 + 8) = make_uint4(o[4], o[5], o[6], o[7]);
-            }
-          }
-        } else {
-          __nv_bfloat16* dst = y_out + (size_t)(mine ? pairs[t.row0 + m] : 0) * NR + t.rb * 256;
-#pragma unroll 1
-          for (int c0 = 0; c0 < 256; c0 += 16) {
-            uint32_t v[16];
-            mt_tmem_ld16(taddr + c0, v);
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            uint32_t o[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              o[i] = pack_bf16x2(__uint_as_float(v[2 * i]) * sc, __uint_as_float(v[2 * i + 1]) * sc);
-            if (mine) {
-              *reinterpret_cast<uint4*>(dst + c0) = make_uint4(o[0], o[1], o[2], o[3]);
-              *reinterpret_cast<uint4*>(dst + c0 + 8) = make_uint4(o[4], o[5], o[6], o[7]);
-            }
+        for (int jj = 0; jj < 16; ++jj) {
+          const int j = c0 + jj;
+          if (j >= t.n) break;
+          const float acc = v[jj] * rs[t.row0 + j];  // exact: a power of two
+          if (GATED) {
+            const float h = __bfloat162float(__float2bfloat16_rn(acc * gsc));
+            const float up = __shfl_down_sync(0xffffffffu, h, 16);
+            if (lane < 16)
+              inter_out[(size_t)(t.row0 + j) * I + t.rb * 64 + 16 * q4 + lane] =
+                  __float2bfloat16_rn(h / (1.f + expf(-h)) * up);
+          } else {
+            y_out[(size_t)pairs[t.row0 + j] * NR + t.rb * 128 + 32 * q4 + lane] = __float2bfloat16_rn(acc * gsc);
           }
         }
       }
@@ -477,7 +471,7 @@ static bool mt_f16_map(CUtensorMap* m, const void* base, long long inner, long l
 }
 
 bool moe_tc_ok(int H, int I, int E) {
-  return H % kMtKC == 0 && I % kMtKC == 0 && I % 128 == 0 && H % 256 == 0 && H <= 8192 && E <= 256 &&
+  return H % kMtKC == 0 && I % kMtKC == 0 && I % 64 == 0 && H % 128 == 0 && H <= 8192 && E <= 256 &&
          tensor_map_encoder() != nullptr;
 }
 
@@ -498,12 +492,11 @@ int launch_moe_tc(const void* w, const void* sf, int E, const __half* act, int r
                   const int32_t* counts, const int32_t* offsets, const int32_t* pairs, const float* gs,
                   __nv_bfloat16* inter, __nv_bfloat16* y, int K, int NR, int I, int* err, cudaStream_t stream) {
   const long long wrows = (long long)E * (GATED ? 2 * I : NR);
-  const int box_rows = GATED ? 128 : 256;
-  CUtensorMap cm, sm, m16, m32, m64, m128;
+  const int box_rows = GATED ? 64 : 128;
+  CUtensorMap cm, sm, m16, m32, m64;
   if (!mt_u8_map(&cm, w, K / 2, wrows, kMtKC / 2, box_rows, true) ||
       !mt_u8_map(&sm, sf, K / 16, wrows, kMtKC / 16, box_rows, false) || !mt_f16_map(&m16, act, K, rows, 16) ||
-      !mt_f16_map(&m32, act, K, rows, 32) || !mt_f16_map(&m64, act, K, rows, 64) ||
-      !mt_f16_map(&m128, act, K, rows, 128))
+      !mt_f16_map(&m32, act, K, rows, 32) || !mt_f16_map(&m64, act, K, rows, 64))
     return OKC_ERR_INVALID;
   static bool configured = false;
   if (!configured) {
@@ -513,8 +506,8 @@ int launch_moe_tc(const void* w, const void* sf, int E, const __half* act, int r
     configured = true;
   }
   return okc_host::launch_k(moe_tc_kernel<GATED>, dim3(okc_host::num_sms()), dim3(kMtThreads), kMtSmem, stream,
-                            dim3(1), cm, sm, m16, m32, m64, m128, counts, offsets, pairs, gs, rs, inter, y, K, NR,
-                            I, E, err);
+                            dim3(1), cm, sm, m16, m32, m64, counts, offsets, pairs, gs, rs, inter, y, K, NR, I, E,
+                            err);
 }
 
 template int launch_moe_tc<true>(const void*, const void*, int, const __half*, int, const float*, const int32_t*,

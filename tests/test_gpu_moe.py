@@ -179,7 +179,7 @@ def test_experts_post_norm_fp32_share(ops, bank):
 def test_experts_kernel_families(ops, bank, T, tc, monkeypatch):
     """The tcgen05 expert kernels (OKC_MOE_TC=1: gather + dequantise-to-shared-memory +
     tcgen05.mma) and the mma.sync kernels (0) against the same oracle, on both sides of the
-    switch (96 tokens)."""
+    switch (32 tokens)."""
     monkeypatch.setenv("OKC_MOE_TC", tc)
     x = bank["x"][:T]
     ids, wts = ops.moe_route(x, bank["router"], 8)
