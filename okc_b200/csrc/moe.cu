@@ -1426,7 +1426,7 @@ size_t moe_experts_ws_bytes(int T, int topk, int H, int I) {
 
 // The tcgen05 expert kernels (moe_tc.cu) from this many tokens on; OKC_MOE_TC=0/1 forces
 // either family (tuning and tests).
-constexpr int kMoeTcMinT = 32;
+constexpr int kMoeTcMinT = 16;
 
 static int moe_tc_choice(int T) {
   const char* e = getenv("OKC_MOE_TC");

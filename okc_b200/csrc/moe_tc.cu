@@ -24,18 +24,20 @@
 //  * Warp 0 streams the unit's packed codes and e4m3 scales with 2-D TMA boxes (256 K per stage:
 //    one 128-byte row of codes per weight row, 128-byte swizzle, plus 16 scale bytes a row) into
 //    a 6-deep raw ring.  Warp 2 loads the stage's activation tiles (4 boxes of 64 K x 16/32/64
-//    rows, f16, 128-byte swizzle) into one of 3 stage slots.
+//    rows, f16, 128-byte swizzle) into one of 2 stage slots.
 //  * Warps 3..10 dequantise, two per TMEM lane quarter (one per 128-K half of a stage), lane =
 //    one weight row: cvt.rn.f16x2.e2m1x2, x the e4m3 group scale in f16 (exact), tcgen05.st into
-//    the stage's A slot (128 columns; 3 slots), tcgen05.wait::st, tcgen05.fence, mbarrier arrive.
+//    the stage's A slot (128 columns; 2 slots), tcgen05.wait::st, tcgen05.fence, mbarrier arrive.
 //    f16 rather than bf16 because the e2m1 -> f16x2 conversion is one instruction; the same
 //    product in bf16 takes about four more integer operations per pair.
-//  * Warp 1 (one thread) issues the 16 MMAs of a stage into a double-buffered TMEM accumulator and
-//    frees the stage's A slot and activation tiles with one tcgen05.commit.  For GATED the A rows
-//    are ordered so that each 32-lane quarter holds 16 gate rows and the same 16 up rows: lanes
-//    l and l + 16 of an epilogue warp hold g and u of one output column.
-//  * Warps 11..14 drain TMEM (tcgen05.ld 32x32b), apply the row scale and gs, and store inter
-//    (bf16, compact pair order) or y (bf16, scattered to the pair's row).
+//  * Two issuer threads (warps 1 and 15, on different SM sub-partitions): issuer h issues the 8
+//    MMAs of K half h of each stage into its own double-buffered TMEM accumulator and frees the
+//    stage with one tcgen05.commit (the slot's empty barrier counts both).  One thread waits
+//    ~50 cycles per MMA it issues; two threads issue concurrently (measured), which doubles the
+//    MMA rate.  For GATED the A rows are ordered so that each 32-lane quarter holds 16 gate rows
+//    and the same 16 up rows: lanes l and l + 16 of an epilogue warp hold g and u of one column.
+//  * Warps 11..14 drain TMEM (tcgen05.ld 32x32b), add the two issuers' accumulators, apply the
+//    row scale and gs, and store inter (bf16, compact pair order) or y (bf16, the pair's row).
 // Every wait is bounded (mbar_wait); on expiry a role sets the abort flag, the others stop at
 // their next wait, copies and MMAs in flight are waited for (bounded), TMEM is freed.
 #include "kernels.cuh"
@@ -46,16 +48,16 @@ namespace okc {
 constexpr int kMtNT = 64;                          // pairs per unit (MMA N <= 64)
 constexpr int kMtKC = 256;                         // K per stage
 constexpr int kMtRaw = 6;                          // raw ring depth
-constexpr int kMtNS = 3;                           // stage slots: A in TMEM + activation tiles
+constexpr int kMtNS = 2;                           // stage slots: A in TMEM + activation tiles
 constexpr int kMtCodes = 128 * (kMtKC / 2);        // 16 KB of codes per raw stage
 constexpr int kMtRawBytes = kMtCodes + 128 * (kMtKC / 16);  // + 2 KB of scales
 constexpr int kMtAtom = kMtNT * 128;               // <= 64 pairs x 64 K f16
 constexpr int kMtAct = 4 * kMtAtom;                // a stage's activation tiles
-constexpr int kMtThreads = 15 * 32;
+constexpr int kMtThreads = 16 * 32;
 constexpr int kMtBody = kMtRaw * kMtRawBytes + kMtNS * kMtAct;
 constexpr int kMtBars = 2 * kMtRaw + 2 * kMtNS + 2 + 2 + 1;
 constexpr int kMtSmem = 1024 + kMtBody + kMtBars * 8 + 16 + (2 * 257 + 2 * 256) * 4;
-constexpr uint32_t kMtAcol = 128;                  // TMEM: accumulators in columns 0..127, A slots after
+constexpr uint32_t kMtAcol = 256;                  // TMEM: 2 issuers x 2 accumulators in 0..255, A slots after
 static_assert(kMtRawBytes % 1024 == 0 && kMtAtom % 1024 == 0, "1024-aligned tiles");
 static_assert(kMtSmem <= 232448, "shared memory");
 static_assert(kMtAcol + kMtNS * 128 <= 512, "tensor memory");
@@ -171,9 +173,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
   pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < kMtRaw; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 8); }
-    for (int i = 0; i < kMtNS; ++i) { mbar_init(&sfull[i], 9); mbar_init(&sempty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 1); mbar_init(&acc_empty[i], 4); }
-    mbar_init(drain, 1);
+    for (int i = 0; i < kMtNS; ++i) { mbar_init(&sfull[i], 9); mbar_init(&sempty[i], 2); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 2); mbar_init(&acc_empty[i], 4); }
+    mbar_init(drain, 2);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -271,9 +273,13 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       for (uint32_t i = q > (uint32_t)kMtNS ? q - kMtNS : 0u; i < q; ++i)
         if (!mbar_wait(&sfull[i % kMtNS], (i / kMtNS) & 1u, err)) break;
     }
-  } else if (warp == 1) {
-    // ---------------------------------- MMA issuer ----------------------------------
+  } else if (warp == 1 || warp == 15) {
+    // ---------------------------------- MMA issuers ---------------------------------
+    // Issuer h (warp 1: h = 0, warp 15: h = 1) takes the K half h of every stage into its own
+    // accumulator; one thread issuing kind::f16 MMAs waits ~50 cycles per instruction, two
+    // threads on different SM sub-partitions issue concurrently.
     if (lane == 0) {
+      const int h = warp == 15 ? 1 : 0;
       uint32_t q = 0;
       int ui = 0;
       bool ok = true;
@@ -286,12 +292,12 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
           const int s = (int)(q % kMtNS);
           if (!mbar_wait(&sfull[s], (q / kMtNS) & 1u, err, abort_flag)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t sa = smem_u32(actt + s * kMtAct);
-          const uint32_t ta = tmem + kMtAcol + (uint32_t)s * 128u;
+          const uint32_t sa = smem_u32(actt + s * kMtAct + 2 * h * kMtAtom);
+          const uint32_t ta = tmem + kMtAcol + (uint32_t)s * 128u + 64u * h;
 #pragma unroll
-          for (int k16 = 0; k16 < 16; ++k16) {
+          for (int k16 = 0; k16 < 8; ++k16) {
             const uint64_t db = umma_desc_sw128(sa + (k16 >> 2) * kMtAtom) + 2 * (k16 & 3);
-            umma_f16_ts(tmem + buf * 64, ta + 8 * k16, db, idesc, (ks | k16) ? 1u : 0u);
+            umma_f16_ts(tmem + 128 * h + buf * 64, ta + 8 * k16, db, idesc, (ks | k16) ? 1u : 0u);
           }
           umma_commit(&sempty[s]);
         }
@@ -369,8 +375,11 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       const float gsc = gs[t.e];
       const uint32_t taddr = tmem + lane_base + buf * 64;
       for (int c0 = 0; c0 < t.n; c0 += 16) {
-        float v[16];
-        tmem_ld16(taddr + c0, v);
+        float v[16], v1[16];
+        tmem_ld16(taddr + c0, v);        // K halves 0 of the stages (issuer 0)
+        tmem_ld16(taddr + 128 + c0, v1);  // K halves 1 (issuer 1)
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) v[jj] += v1[jj];
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
           const int j = c0 + jj;

@@ -175,11 +175,11 @@ def test_experts_post_norm_fp32_share(ops, bank):
     assert torch.equal(f.to(torch.bfloat16), b)
 
 
-@pytest.mark.parametrize("T,tc", [(8, "1"), (16, "1"), (32, "1"), (32, "0"), (64, "1"), (64, "0"), (256, "1")])
+@pytest.mark.parametrize("T,tc", [(8, "1"), (8, "0"), (16, "1"), (16, "0"), (32, "1"), (64, "0"), (256, "1")])
 def test_experts_kernel_families(ops, bank, T, tc, monkeypatch):
     """The tcgen05 expert kernels (OKC_MOE_TC=1: gather + dequantise-to-shared-memory +
     tcgen05.mma) and the mma.sync kernels (0) against the same oracle, on both sides of the
-    switch (32 tokens)."""
+    switch (16 tokens)."""
     monkeypatch.setenv("OKC_MOE_TC", tc)
     x = bank["x"][:T]
     ids, wts = ops.moe_route(x, bank["router"], 8)
