@@ -141,6 +141,12 @@ __global__ void __launch_bounds__(1024) route_kernel(const __nv_bfloat16* __rest
 constexpr int kPermMaxPairs = 16384;
 constexpr int kPermMaxExperts = 256;
 
+// O(n) work: warp w owns the pairs [w * per, (w + 1) * per) in 32-pair chunks.  Pass 1 counts the
+// warp's pairs per expert (__match_any_sync; the lowest lane of each expert group adds the group's
+// size); an exclusive prefix over the warps per expert, then over the experts, gives each
+// (warp, expert) its first output slot; pass 2 walks the same chunks in order and writes each
+// pair at that slot + its rank among the chunk's earlier pairs of its expert, so every expert's
+// list comes out in ascending pair order.
 __global__ void __launch_bounds__(1024) permute_kernel(const int32_t* __restrict__ ids, int n,
                                                        int expert_lo, int E, int bm,
                                                        int32_t* __restrict__ counts,
@@ -148,23 +154,34 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int32_t* __restrict
                                                        int32_t* __restrict__ pairs,
                                                        int32_t* __restrict__ tiles, int max_tiles,
                                                        int* err) {
-  __shared__ int16_t loc[kPermMaxPairs];
+  __shared__ int16_t wcnt[32][kPermMaxExperts];  // per (warp, expert): count, then first slot in the expert
   __shared__ int cnt[kPermMaxExperts];
   __shared__ int off[kPermMaxExperts + 1];
   __shared__ int toff[kPermMaxExperts + 1];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int p = threadIdx.x; p < n; p += blockDim.x) {
-    const int e = ids[p] - expert_lo;
-    loc[p] = (e >= 0 && e < E) ? (int16_t)e : (int16_t)-1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) wcnt[i / E][i % E] = 0;
+  __syncthreads();
+  const int per = (n + 31) / 32;
+  const int p0 = warp * per, p1 = min(n, p0 + per);
+  auto expert_of = [&](int q) {
+    if (q >= p1) return -1;
+    const int v = ids[q] - expert_lo;
+    return (v >= 0 && v < E) ? v : -1;
+  };
+  for (int base = p0; base < p1; base += 32) {
+    const int e = expert_of(base + lane);
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && lane == __ffs(peers) - 1) wcnt[warp][e] += (int16_t)__popc(peers);
   }
   __syncthreads();
-  for (int e = warp; e < E; e += nw) {
-    int c = 0;
-    for (int base = 0; base < n; base += 32) {
-      const int p = base + lane;
-      c += __popc(__ballot_sync(0xffffffffu, p < n && loc[p] == e));
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = wcnt[w][e];
+      wcnt[w][e] = (int16_t)run;
+      run += c;
     }
-    if (lane == 0) cnt[e] = c;
+    cnt[e] = run;
   }
   __syncthreads();
   if (warp == 0) {
@@ -196,14 +213,16 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int32_t* __restrict
     if (total > max_tiles && err) atomicOr(err, OKC_DEVERR_INDEX);
     tiles[0] = min(total, max_tiles);
   }
-  for (int e = warp; e < E; e += nw) {
-    int run = off[e];
-    for (int base = 0; base < n; base += 32) {
-      const int p = base + lane;
-      const unsigned bal = __ballot_sync(0xffffffffu, p < n && loc[p] == e);
-      if (p < n && loc[p] == e) pairs[run + __popc(bal & ((1u << lane) - 1u))] = p;
-      run += __popc(bal);
-    }
+  for (int base = p0; base < p1; base += 32) {
+    const int q = base + lane;
+    const int e = expert_of(q);
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0) pairs[off[e] + wcnt[warp][e] + __popc(peers & ((1u << lane) - 1u))] = q;
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) wcnt[warp][e] += (int16_t)__popc(peers);
+    __syncwarp();
+  }
+  for (int e = warp; e < E; e += 32) {
     const int nt = (cnt[e] + bm - 1) / bm;
     for (int j = lane; j < nt; j += 32) {
       const int ti = toff[e] + j;
@@ -1189,16 +1208,21 @@ __global__ void __launch_bounds__(256) route_cluster_kernel(const __nv_bfloat16*
   extern __shared__ __align__(16) uint8_t rsm[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rsm);               // [RT_TT][H]
   float* lg = reinterpret_cast<float*>(rsm + (size_t)RT_TT * H * 2);        // [RT_TT][E] (used in CTA 0)
-  pdl_trigger();
-  pdl_wait();
   const int cr = (int)cluster.block_rank();
   const int t0 = (blockIdx.x / 8) * RT_TT;
   const int nt = min(RT_TT, T - t0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
+  // the group's token rows into shared memory with asynchronous 16-byte copies, all in flight
+  // at once (a load/store loop would pay a global-load latency per 16 bytes)
   for (int i = threadIdx.x * 8; i < nt * H; i += blockDim.x * 8) {
     const int tt = i / H, k = i - tt * H;
-    *reinterpret_cast<uint4*>(xs + (size_t)tt * H + k) = *reinterpret_cast<const uint4*>(x + (size_t)(t0 + tt) * H + k);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(xs + (size_t)tt * H + k)),
+                 "l"(x + (size_t)(t0 + tt) * H + k)
+                 : "memory");
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   float* lg0 = cluster.map_shared_rank(lg, 0);
   const int per_cta = (E + 7) / 8;
