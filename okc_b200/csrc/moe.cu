@@ -1187,108 +1187,19 @@ static int launch_combine(const __nv_bfloat16* y, const int32_t* ids, const floa
   return okc_host::launch_status();
 }
 
-// ---------------------------------------------------------------------------------------
-// Router, cluster form: a cluster of 8 CTAs serves RT_TT tokens; CTA r of the cluster computes
-// experts [r*E/8, (r+1)*E/8) (warp w: expert r*E/8 + w, + 8 per extra round) for every token of
-// the group, holding its expert's router row in registers, and stores the bf16-rounded logits
-// into the shared memory of CTA 0 (distributed shared memory); after a cluster barrier CTA 0's
-// warps run the top-k, one warp per token.  Each (token, expert) dot product keeps the fixed
-// summation order of route_kernel (lane l: j outer, element inner; xor butterfly), so the ids and
-// logits are identical.  The router rows are read once per token group instead of once per
-// token.
-constexpr int RT_TT = 8;
-
-__global__ void __launch_bounds__(256) route_cluster_kernel(const __nv_bfloat16* __restrict__ x,
-                                                            const __nv_bfloat16* __restrict__ wr,
-                                                            int32_t* __restrict__ ids, float* __restrict__ wts,
-                                                            float* __restrict__ logits_out, int T, int H, int E,
-                                                            int topk, int renormalize) {
-  namespace cg = cooperative_groups;
-  cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ __align__(16) uint8_t rsm[];
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rsm);               // [RT_TT][H]
-  float* lg = reinterpret_cast<float*>(rsm + (size_t)RT_TT * H * 2);        // [RT_TT][E] (used in CTA 0)
-  const int cr = (int)cluster.block_rank();
-  const int t0 = (blockIdx.x / 8) * RT_TT;
-  const int nt = min(RT_TT, T - t0);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_trigger();
-  pdl_wait();
-  // the group's token rows into shared memory with asynchronous 16-byte copies, all in flight
-  // at once (a load/store loop would pay a global-load latency per 16 bytes)
-  for (int i = threadIdx.x * 8; i < nt * H; i += blockDim.x * 8) {
-    const int tt = i / H, k = i - tt * H;
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(xs + (size_t)tt * H + k)),
-                 "l"(x + (size_t)(t0 + tt) * H + k)
-                 : "memory");
-  }
-  asm volatile("cp.async.wait_all;" ::: "memory");
-  __syncthreads();
-  float* lg0 = cluster.map_shared_rank(lg, 0);
-  const int per_cta = (E + 7) / 8;
-  const int nj = H / 256;
-  for (int ei = warp; ei < per_cta; ei += 8) {
-    const int e = cr * per_cta + ei;
-    if (e >= E) break;
-    const __nv_bfloat16* we = wr + (size_t)e * H;
-    float acc[RT_TT];
-#pragma unroll
-    for (int tt = 0; tt < RT_TT; ++tt) acc[tt] = 0.f;
-    // 16 chunks of 256 (4096 elements) of the router row per pass, held in registers and used
-    // for every token of the group
-    for (int j0 = 0; j0 < nj; j0 += 16) {
-      uint4 wv[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q)
-        if (j0 + q < nj) wv[q] = __ldg(reinterpret_cast<const uint4*>(we + 256 * (j0 + q) + 8 * lane));
-#pragma unroll
-      for (int tt = 0; tt < RT_TT; ++tt) {
-        if (tt >= nt) break;
-#pragma unroll
-        for (int q = 0; q < 16; ++q) {
-          if (j0 + q >= nj) break;
-          const uint4 xv = *reinterpret_cast<const uint4*>(xs + (size_t)tt * H + 256 * (j0 + q) + 8 * lane);
-          const uint32_t xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv[q].x, wv[q].y, wv[q].z, wv[q].w};
-#pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            acc[tt] = fmaf(bf16_lo(xa[r]), bf16_lo(wa[r]), acc[tt]);
-            acc[tt] = fmaf(bf16_hi(xa[r]), bf16_hi(wa[r]), acc[tt]);
-          }
-        }
-      }
-    }
-#pragma unroll
-    for (int tt = 0; tt < RT_TT; ++tt) {
-      if (tt >= nt) break;
-      float a = acc[tt];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
-      if (lane == 0) lg0[tt * E + e] = __bfloat162float(__float2bfloat16_rn(a));
-    }
-  }
-  cluster.sync();  // every logit of the group is in CTA 0's shared memory
-  if (cr == 0 && warp < nt) route_topk_warp(lg + warp * E, t0 + warp, E, topk, renormalize, ids, wts, logits_out, lane);
-}
 
 int launch_moe_route(const void* x, const void* wr, int32_t* ids, float* wts, float* logits,
                      int T, int H, int E, int topk, int renormalize, cudaStream_t stream) {
-  const size_t csmem = (size_t)RT_TT * H * 2 + (size_t)RT_TT * E * 4;
-  if (csmem <= 200 * 1024) {  // cluster form (H <= 12K for 8 tokens of x in shared memory)
-    static size_t configured = 0;
-    if (csmem > configured) {
-      if (cudaFuncSetAttribute(route_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem) !=
-          cudaSuccess)
-        return OKC_ERR_LAUNCH;
-      configured = csmem;
-    }
-    const int groups = (T + RT_TT - 1) / RT_TT;
-    return okc_host::launch_k(route_cluster_kernel, dim3(groups * 8), dim3(256), csmem, stream, dim3(8),
-                              reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(wr),
-                              ids, wts, logits, T, H, E, topk, renormalize);
-  }
+  // One CTA per token.  (An 8-CTA cluster per 8 tokens sharing router rows through distributed
+  // shared memory measured slower at T = 8..256 on B200: 12.6-24.5 vs 10.3-20.3 us.)
   const size_t smem = (size_t)H * 2 + (size_t)E * 4;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (smem > 232448) return OKC_ERR_INVALID;
+  static size_t configured = 0;
+  if (smem > 48 * 1024 && smem > configured) {
+    if (cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return OKC_ERR_LAUNCH;
+    configured = smem;
+  }
   route_kernel<<<T, 1024, smem, stream>>>(reinterpret_cast<const __nv_bfloat16*>(x),
                                          reinterpret_cast<const __nv_bfloat16*>(wr), ids, wts, logits,
                                          H, E, topk, renormalize);
