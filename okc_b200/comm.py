@@ -205,6 +205,7 @@ class ExpertParallelMoE:
         self.expert_lo, self.E_local = expert_lo, w13.shape[0]
         self.topk, self.group, self.renormalize = topk, group, renormalize
         self._comms: dict[int, TPComm] = {}
+        self._gather: dict = {}
 
     def comm_for(self, tokens: int) -> TPComm:
         """The exchange group for `tokens` rows (created on first use: every rank together,
@@ -224,7 +225,30 @@ class ExpertParallelMoE:
                         self.expert_lo, out=comm.partial, out_fp32=True)
         return comm.allreduce_residual(residual)
 
+    def forward_local(self, x: torch.Tensor) -> torch.Tensor:
+        """Data-parallel tokens: each rank holds its own rows x_r [T, H] (the same T on every
+        rank) and gets back bf16 [T, H] = the MoE of its rows.  Dispatch: the rows of all ranks
+        are all-gathered into [W*T, H] (NCCL over NVLink; fixed sizes, so no host
+        synchronisation and the call can be captured in a graph).  Each rank routes all W*T rows
+        (bit-exact routing: every rank computes the same ids), runs its local experts for the
+        pairs routed to them and leaves its fp32 share; combine: the exchange kernel sums the
+        shares over NVLink peer memory and rank r keeps rows [r*T, (r+1)*T).  With top-8 of 64
+        experts over 8 ranks a token reaches ~5.4 of the 8 ranks on average, so gathering every
+        row moves ~1.5x the bytes of an exact all-to-all, and needs no per-call exchange of
+        counts."""
+        T, H = x.shape
+        world = dist.get_world_size(self.group)
+        rank = dist.get_rank(self.group)
+        key = ("gather", T)
+        buf = self._gather.get(key)
+        if buf is None:
+            buf = torch.empty((world * T, H), dtype=x.dtype, device=x.device)
+            self._gather[key] = buf
+        dist.all_gather_into_tensor(buf, x.contiguous(), group=self.group)
+        return self.forward(buf)[rank * T:(rank + 1) * T]
+
     def close(self):
         for c in self._comms.values():
             c.close()
         self._comms.clear()
+        self._gather.clear()

@@ -16,6 +16,13 @@ trace of CTA 0 of each kernel (ns from its griddepcontrol.wait) for its last thr
 
     OKC_TP_TRACE=1 python -m torch.distributed.run --nnodes=1 --nproc-per-node 2 \
         --master-addr 127.0.0.1 --master-port 29513 -m okc_b200.profile_cases tp --kk 4096,1024
+
+The `moe_ep` case (also under torchrun) times the expert-parallel MoE with `--t` tokens of its
+own per rank (ExpertParallelMoE.forward_local: all-gather dispatch, local experts, NVLink
+combine), and on rank 0 the single-GPU MoE over the same world * t tokens:
+
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node 2 --master-addr 127.0.0.1 \
+        --master-port 29514 -m okc_b200.profile_cases moe_ep --t 32
 """
 
 from __future__ import annotations
@@ -145,9 +152,73 @@ def case_tp(a):
     return res if rank == 0 else None
 
 
+def case_moe_ep(a):
+    """Expert-parallel MoE with each rank's own T tokens (forward_local) under torchrun: us per
+    step (graph replays, max over ranks) and, on rank 0, the single-GPU MoE over the same W*T
+    tokens for comparison."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from .comm import ExpertParallelMoE
+    world, rank = int(os.environ["WORLD_SIZE"]), int(os.environ["RANK"])
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    T, R = a.t, 10
+    m = synth.moe_case(T=world * T, device="cuda", seed=0)
+    E = m["w13"].shape[0]
+    el = E // world
+    sl = slice(rank * el, (rank + 1) * el)
+    ep = ExpertParallelMoE(m["router"], m["w13"][sl].contiguous(), m["w13_sf"][sl].contiguous(),
+                           m["w13_gs"][sl].contiguous(), m["w2"][sl].contiguous(), m["w2_sf"][sl].contiguous(),
+                           m["w2_gs"][sl].contiguous(), rank * el, 8)
+    mine = m["x"][rank * T:(rank + 1) * T].contiguous()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            ep.forward_local(mine)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    dist.barrier()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for _ in range(R):
+            ep.forward_local(mine)
+    for _ in range(3):
+        gr.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = torch.tensor([e0.elapsed_time(e1) * 1000 / (5 * R)], device="cuda")
+    dist.all_reduce(us, op=dist.ReduceOp.MAX)
+    res = {"case": "moe_ep", "world": world, "tokens_per_rank": T, "experts_per_rank": el,
+           "ep_us": round(float(us), 2), "tokens_per_s": round(world * T / float(us) * 1e6),
+           "device_error": ops.read_device_error("tp", rank)}
+    del gr
+    torch.cuda.synchronize()
+    dist.barrier()
+    if rank == 0:
+        def one():
+            i, w_ = ops.moe_route(m["x"], m["router"], 8)
+            p_ = ops.moe_permute(i, 0, E)
+            return ops.moe_experts(m["x"], i, w_, p_, m["w13"], m["w13_sf"], m["w13_gs"], m["w2"], m["w2_sf"],
+                                   m["w2_gs"], 0)
+        res["one_gpu_same_batch_us"] = round(_time(one, 3, 10), 2)
+    dist.barrier()
+    ep.close()
+    dist.destroy_process_group()
+    return res if rank == 0 else None
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["attn", "gemv", "moe", "tp"])
+    ap.add_argument("case", choices=["attn", "gemv", "moe", "tp", "moe_ep"])
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--b", type=int, default=64)
@@ -164,7 +235,7 @@ def main(argv=None):
     ap.add_argument("--kk", default="1024", help="tp: comma-separated O-projection K per rank")
     a = ap.parse_args(argv)
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-    res = {"attn": case_attn, "gemv": case_gemv, "moe": case_moe, "tp": case_tp}[a.case](a)
+    res = {"attn": case_attn, "gemv": case_gemv, "moe": case_moe, "tp": case_tp, "moe_ep": case_moe_ep}[a.case](a)
     if res is not None:
         print(json.dumps(res), flush=True)
     return 0

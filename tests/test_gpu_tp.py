@@ -6,7 +6,8 @@
     rounding of the exact result, identical replicas, interleaved with the unfused path;
   * the decode layer at TP 2 against the CPU oracle of the whole layer;
   * expert-parallel MoE (okc_b200.comm.ExpertParallelMoE, half of the experts per rank)
-    against the single-GPU MoE over the whole bank.
+    against the single-GPU MoE over the whole bank, with the tokens replicated (forward) and
+    with each rank's own tokens (forward_local: all-gather dispatch, NVLink combine).
 Each test is skipped when fewer GPUs than its ranks are visible."""
 
 import os
@@ -137,6 +138,66 @@ def _ep_worker(rank, world, port, T, q):
         q.put((rank, rel, mx, derr))
     finally:
         dist.destroy_process_group()
+
+
+def _ep_dp_worker(rank, world, port, T, q):
+    import datetime
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from okc_b200 import ops, synth
+        from okc_b200.comm import ExpertParallelMoE
+        m = synth.moe_case(T=world * T, device="cuda", seed=4)  # the whole batch, identical on every rank
+        E = m["w13"].shape[0]
+        el = E // world
+        sl = slice(rank * el, (rank + 1) * el)
+        ep = ExpertParallelMoE(m["router"], m["w13"][sl].contiguous(), m["w13_sf"][sl].contiguous(),
+                               m["w13_gs"][sl].contiguous(), m["w2"][sl].contiguous(), m["w2_sf"][sl].contiguous(),
+                               m["w2_gs"][sl].contiguous(), rank * el, 8)
+        mine = m["x"][rank * T:(rank + 1) * T].contiguous()  # this rank's own tokens
+        got = [ep.forward_local(mine).clone() for _ in range(2)]
+        ids, wts = ops.moe_route(m["x"], m["router"], 8)
+        perm = ops.moe_permute(ids, 0, E)
+        full = ops.moe_experts(m["x"], ids, wts, perm, m["w13"], m["w13_sf"], m["w13_gs"], m["w2"], m["w2_sf"],
+                               m["w2_gs"], 0)[rank * T:(rank + 1) * T]
+        torch.cuda.synchronize()
+        d = (got[0].float() - full.float())
+        rel = float(d.norm() / full.float().norm())
+        mx = float(d.abs().max())
+        same = bool(torch.equal(got[0], got[1]))
+        derr = ops.read_device_error("tp", rank)
+        torch.cuda.synchronize()
+        dist.barrier()
+        ep.close()
+        q.put((rank, rel, mx, derr, same))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("T", [8, 64])
+def test_expert_parallel_moe_data_parallel_tokens(T):
+    """Each rank holds different tokens (forward_local: all-gather dispatch, local experts, NVLink
+    combine): rank r's output equals rows [r*T, (r+1)*T) of the single-GPU MoE over the whole
+    batch, within one bf16 rounding, and two calls agree bit for bit."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_dp_worker, args=(r, 2, port, T, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, rel, mx, derr, same in res:
+        assert derr == 0, f"rank {rank}: device error {derr}"
+        assert same, f"rank {rank}: two calls differ"
+        assert rel < 2e-3 and mx < 5e-2, f"rank {rank}: rel-L2 {rel:.2e}, max abs {mx:.2e}"
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
