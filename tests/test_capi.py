@@ -172,13 +172,20 @@ def test_every_pdl_launched_kernel_waits_before_returning():
         early = [r.start() for r in re.finditer(r"\breturn\b", body) if r.start() < w]
         if early:
             bad.append(f"{name}: returns before pdl_wait")
+        # a warp-specialised kernel splits into roles with an if / else-if chain on the warp
+        # index; the wait must come before that split, so that every role has executed it
+        split = re.search(r"\}\s*else\s+if\s*\(\s*warp\b", body)
+        if split and split.start() < w:
+            bad.append(f"{name}: role split before pdl_wait")
     assert not bad, bad
 
 
 def test_every_device_spin_wait_is_bounded():
     """Device code polls in exactly two places, both bounded by kWaitNs of %globaltimer:
     mbar_wait (common.cuh: mbarrier phases) and wait_flag (tp_comm.cu: cross-GPU flags).  No
-    other code issues mbarrier.try_wait / test_wait or loops on an acquire load."""
+    other code issues mbarrier.try_wait / test_wait, loops on an acquire or volatile load in a
+    while condition, or polls one inside an unconditional loop (for (;;), while (true),
+    do { } while)."""
     csrc = ROOT / "okc_b200" / "csrc"
     files = {f.name: f.read_text() for f in list(csrc.glob("*.cu")) + list(csrc.glob("*.cuh"))}
     for name, src in files.items():
@@ -192,6 +199,21 @@ def test_every_device_spin_wait_is_bounded():
                 head = code[:m.start()]
                 fn = re.findall(r"__device__[^{;]*?\b(\w+)\s*\([^;{]*\)\s*\{", head)
                 assert fn and fn[-1] == "wait_flag", f"{name}: flag polling outside wait_flag"
+        # unconditional loops (for (;;), while (true/1), do { } while) that poll a flag
+        for m in re.finditer(r"for\s*\(\s*;\s*;\s*\)|while\s*\(\s*(?:true|1)\s*\)|\bdo\s*\{", code):
+            start = code.index("{", m.start())
+            depth, i = 0, start
+            while i < len(code):
+                depth += code[i] == "{"
+                depth -= code[i] == "}"
+                if depth == 0:
+                    break
+                i += 1
+            loop = code[start:i]
+            if any(k in loop for k in ("ld_acquire", "ld.acquire", "volatile", "mbar_try_wait", "try_wait")):
+                head = code[:m.start()]
+                fn = re.findall(r"__device__[^{;]*?\b(\w+)\s*\([^;{]*\)\s*\{", head)
+                assert fn and fn[-1] in ("wait_flag", "mbar_wait"), f"{name}: unbounded-looking poll loop"
     common = re.sub(r"//[^\n]*", "", files["common.cuh"])
     body = common[common.index("bool mbar_wait("):]
     body = body[:body.index("\n}\n")]
