@@ -122,3 +122,57 @@ def layer_case(B=128, H=8192, Hq=64, Hkv=8, D=128, ctx=(1024, 8192), page=16, po
             "seq_lens": att["seq_lens"], "k_scale": att["k_scale"], "v_scale": att["v_scale"],
             "lens": att["lens"], "theta": theta, "eps": eps, "Hq": Hq, "Hkv": Hkv, "D": D,
             "sm_scale": 1.0 / math.sqrt(D)}
+
+
+def muse_layer_case(B=1, L=1, ctx=(1000, 3000), page=1, window=0, theta=5e5, kv_scale=1.0, local_start=32,
+                    local_bias=0.08, seed=0, device="cuda", weights=None):
+    """One Muse TP8/EP8 decode-layer step in the reference problem's data formats
+    (muse_decode_layer/decode/spec.py): weights (random init: dense ~N(0, 0.02) bf16, norm and
+    gate weights ~N(0, 0.05)/N(0, 0.3), router fp32 ~N(0, 0.02), router_bias ~N(0, 0.01) plus
+    `local_bias` on this GPU's 32 experts so that a step routes some tokens here, the 32 local
+    experts' NVFP4 banks as moe_case makes them at H = I = 4096) and inputs (stream fp32
+    ~N(0,1), attn_input bf16 ~N(0,1), B requests of ctx ~U[lo, hi] cached tokens each plus a
+    block of L new ones, e4m3 caches of N(0,1)/kv_scale codes, page table and cache rows).
+    Pass `weights` from an earlier call to reuse them.  Returns (weights, data)."""
+    g = _gen(device, seed)
+    if weights is None:
+        def dense(n, k):
+            return (torch.randn((n, k), generator=g, device=device) * 0.02).to(torch.bfloat16)
+
+        def vec(n, s):
+            return (torch.randn((n,), generator=g, device=device) * s).to(torch.bfloat16)
+        bank = moe_case(T=1, E=32, H=4096, I=4096, seed=seed + 1, device=device, gs2=(0.015, 0.025))
+        bias = torch.randn((256,), generator=g, device=device) * 0.01
+        bias[local_start:local_start + 32] += local_bias
+        weights = {"qkv_gate": dense(2304, 8192), "o": dense(8192, 1024), "attn_residual_gate": vec(8192, 0.3),
+                   "pre_ffn_norm": vec(8192, 0.05),
+                   "router": torch.randn((256, 8192), generator=g, device=device) * 0.02, "router_bias": bias,
+                   "pooler": dense(4096, 8192), "pre_expert_norm": vec(4096, 0.05),
+                   "post_expert_norm": vec(4096, 0.05), "unpooler": dense(8192, 4096), "post_ffn_norm": vec(8192, 0.05),
+                   "ffn_residual_gate": vec(8192, 0.3), "next_pre_attn_norm": vec(8192, 0.05)}
+        weights.update({k: bank[k] for k in ("w13", "w13_sf", "w13_gs", "w2", "w2_sf", "w2_gs")})
+    T = B * L
+    lens = torch.randint(ctx[0], ctx[1] + 1, (B,), generator=g, device=device)
+    lens_l = [int(v) for v in lens.tolist()]
+    pool = sum(math.ceil((n + L) / page) for n in lens_l) + 3
+    table = paged_layout(lens_l, page, pool, g, device, extra_tokens=L)
+    kc = torch.empty((pool, page, 2, 64), dtype=E4M3, device=device)
+    vc = torch.empty_like(kc)
+    fill_e4m3_normal(kc, g, torch.full((2,), kv_scale, device=device))
+    fill_e4m3_normal(vc, g, torch.full((2,), kv_scale, device=device))
+    pos = (lens.long()[:, None] + torch.arange(L, device=device)).reshape(-1)
+    rows = table.long().repeat_interleave(L, dim=0)
+    loc = rows.gather(1, (pos // page)[:, None]).reshape(-1) * page + pos % page
+    cfg = {"batch": B, "q_len": L, "tokens": T, "hidden": 8192, "num_q_heads": 16, "num_kv_heads": 2, "head_dim": 64,
+           "page_size": page, "window": window, "rope_theta": theta, "qk_scale_factor": 5.4730064863875,
+           "sm_scale": 0.125, "kv_scale": kv_scale, "n_experts": 256, "top_k": 8, "local_experts": 32}
+    s = torch.tensor(kv_scale, dtype=torch.float32, device=device)
+    data = {"stream": torch.randn((T, 8192), generator=g, device=device),
+            "attn_input": torch.randn((T, 8192), generator=g, device=device).to(torch.bfloat16),
+            "k_cache": kc, "v_cache": vc, "positions": pos, "cache_loc": loc,
+            "cache_seqlens": (lens + L).to(torch.int32),
+            "cu_seqlens_q": torch.arange(0, T + 1, L, device=device, dtype=torch.int32),
+            "scheduler_metadata": None, "k_scale": s, "v_scale": s, "page_table": table,
+            "seq_lens": lens.to(torch.int32),
+            "local_start": torch.tensor([local_start], dtype=torch.int32, device=device), "config": cfg}
+    return weights, data
