@@ -158,13 +158,15 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) my_bytes += __shfl_xor_sync(0xffffffffu, my_bytes, o);
-      // Small pages (one or two 2 KB rows: one or two KV heads of 16 tokens), units starting on
-      // a page: TMA gather4 fetches 4 rows per instruction, where a bulk copy per page pays the
-      // copy engine's fixed cost per copy (measured: 2 KB pages 5.4 vs 4.0 TB/s over 148 SMs).
-      // The row count is padded to a multiple of 4 with the last row (the extra tokens are masked).
+      // Small pages (one or two 2 KB rows: one or two KV heads of 16 tokens; or a whole page
+      // below 2 KB, e.g. one token at page size 1), units starting on a page: TMA gather4
+      // fetches 4 rows per instruction, where a bulk copy per page pays the copy engine's fixed
+      // cost per copy (measured: 2 KB pages 5.4 vs 4.0 TB/s over 148 SMs; 128-byte pages are
+      // bound by that cost at ~0.4 TB/s).  The row count is padded to a multiple of 4 with the
+      // last row (the extra tokens are masked).
       const int g4_rows = a.g4_rpp > 0 ? cur.nseg * a.g4_rpp : 0;
       const int g4_ops = (g4_rows + 3) >> 2;
-      if (g4_rows) my_bytes = (uint32_t)g4_ops * 4u * 2048u * 2u;
+      if (g4_rows) my_bytes = (uint32_t)g4_ops * 4u * (uint32_t)a.g4_rb * 2u;
       bool ok = true;
       if (lane == 0) ok = mbar_wait(&empty[stage], phase ^ 1u, a.err);
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
@@ -176,17 +178,22 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
       __syncwarp();
       uint8_t* sk = stages + (size_t)stage * C::STAGE;
       uint8_t* sv = sk + C::KV_BYTES;
-      if (g4_rows) {
+      // op o (lane o % 32, pass o / 32, warp-uniform passes for the shuffles) gathers rows
+      // 4o .. 4o + 3; segments past the first 32 read their page id from the table
+      for (int o0 = 0; o0 < g4_ops; o0 += 32) {
+        const int o = o0 + lane;
         int rid[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int r = min(4 * lane + i, g4_rows - 1);
-          const int pg = __shfl_sync(0xffffffffu, cur.page, r / a.g4_rpp);
+          const int r = min(4 * o + i, g4_rows - 1);
+          const int sg = r / a.g4_rpp;
+          const int sh = __shfl_sync(0xffffffffu, cur.page, sg & 31);
+          const int pg = sg < 32 ? sh : page_of(cur, sg);
           rid[i] = (pg >= 0 && pg < a.num_pages) ? pg * a.g4_rpp + r % a.g4_rpp : -1;
         }
-        if (lane < g4_ops) {
-          tma_gather4(sk + lane * 8192, &kmap, rid, &full[stage], pol);
-          tma_gather4(sv + lane * 8192, &vmap, rid, &full[stage], pol);
+        if (o < g4_ops) {
+          tma_gather4(sk + (size_t)o * 4 * a.g4_rb, &kmap, rid, &full[stage], pol);
+          tma_gather4(sv + (size_t)o * 4 * a.g4_rb, &vmap, rid, &full[stage], pol);
         }
       }
       for (int sg = lane; sg < cur.nseg && !g4_rows; sg += 32) {
@@ -632,13 +639,14 @@ __global__ void __launch_bounds__(256) rope_append_kernel(
 }
 
 // ---------------------------------------------------------------------------------------
-// A 2-D map over the cache as rows of 2 KB (256 x u64), one-row box: the gather4 source.
-static bool g4_map(CUtensorMap* m, const void* base, long long rows) {
+// A 2-D map over the cache as rows of rb bytes (rb / 8 x u64; rb a multiple of 16, <= 2048),
+// one-row box: the gather4 source.
+static bool g4_map(CUtensorMap* m, const void* base, long long rows, int rb) {
   auto fn = tensor_map_encoder();
-  if (!fn || !okc_host::aligned16(base)) return false;
-  cuuint64_t dims[2] = {256, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {2048};
-  cuuint32_t box[2] = {256, 1};
+  if (!fn || !okc_host::aligned16(base) || rb % 16 || rb > 2048 || rb <= 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)(rb / 8), (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)rb};
+  cuuint32_t box[2] = {(cuuint32_t)(rb / 8), 1};
   cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -658,14 +666,20 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
       return OKC_ERR_LAUNCH;
     configured = smem;
   }
-  // TMA gather4 maps when pages are one or two 2 KB rows and units start on a page
+  // TMA gather4 maps when pages are one or two 2 KB rows, or one row of a multiple of 16 bytes
+  // below 2 KB, and units start on a page (always so for one-token pages, whatever the window)
   CUtensorMap km{}, vm{};
   a.g4_rpp = 0;
+  a.g4_rb = 0;
   const long long pb = (long long)a.P * C::ROW;
-  if (a.window == 0 && pb % 2048 == 0 && pb / 2048 <= 2 && C::TS % a.P == 0 && C::KV_BYTES % 8192 == 0 &&
+  const int rb = (pb % 2048 == 0 && pb / 2048 <= 2) ? 2048 : (pb < 2048 && pb % 16 == 0 ? (int)pb : 0);
+  if (rb && (a.window == 0 || a.P == 1) && C::TS % a.P == 0 && C::KV_BYTES % (4 * rb) == 0 &&
       !getenv("OKC_ATTN_NO_GATHER")) {
-    const long long rows = a.num_pages * (pb / 2048);
-    if (rows < (1LL << 31) && g4_map(&km, a.k_cache, rows) && g4_map(&vm, a.v_cache, rows)) a.g4_rpp = (int)(pb / 2048);
+    const long long rows = a.num_pages * (pb / rb);
+    if (rows < (1LL << 31) && g4_map(&km, a.k_cache, rows, rb) && g4_map(&vm, a.v_cache, rows, rb)) {
+      a.g4_rpp = (int)(pb / rb);
+      a.g4_rb = rb;
+    }
   }
   int st = okc_host::launch_k(attn_decode_kernel<D, HKV>, dim3(a.num_ctas), dim3(C::THREADS), smem, stream, dim3(1),
                               km, vm, a);

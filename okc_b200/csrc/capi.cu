@@ -245,6 +245,7 @@ int okc_attn_decode_fp8_ex(const void* q, int ldq, const void* k_cache, const vo
   a.window = window;
   a.q_per_seq = q_per_seq;
   a.g4_rpp = 0;
+  a.g4_rb = 0;
   return okc::launch_attn_decode(a, D, Hkv, stream);
 }
 

@@ -34,7 +34,8 @@ struct AttnArgs {
   int q_per_seq;  // query tokens per request (verify blocks): sequence b reads table row b / q_per_seq
   uint8_t* ws_q8; // [B][Hkv][16][128] two-term e4m3 queries (tcgen05 kernel)
   float* ws_qf;   // [B][Hkv][8] their per-row scales
-  int g4_rpp;     // > 0: pages are fetched with TMA gather4 as this many 2 KB rows each (mma.sync kernel)
+  int g4_rpp;     // > 0: pages are fetched with TMA gather4 as this many rows each (mma.sync kernel)
+  int g4_rb;      // the gather rows' bytes: 2048, or a whole page smaller than 2 KB
 };
 size_t attn_q8_ws_bytes(int B, int Hkv);
 

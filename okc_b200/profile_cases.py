@@ -17,6 +17,13 @@ trace of CTA 0 of each kernel (ns from its griddepcontrol.wait) for its last thr
     OKC_TP_TRACE=1 python -m torch.distributed.run --nnodes=1 --nproc-per-node 2 \
         --master-addr 127.0.0.1 --master-port 29513 -m okc_b200.profile_cases tp --kk 4096,1024
 
+The `muse_layer` case times one Muse TP8/EP8 decode-layer step (problems/muse_decode_layer.py,
+`--b` requests of `--l` new tokens, context ~U[ctx-lo, ctx-hi], `--window`, page `--page`) as
+a CUDA graph of 10 steps, with the algorithmic bytes (dense weights, router, the local experts
+the step routed to, the KV rows read):
+
+    python -m okc_b200.profile_cases muse_layer --b 33 --l 1 --ctx-lo 10000 --ctx-hi 20000 --page 1
+
 The `moe_ep` case (also under torchrun) times the expert-parallel MoE with `--t` tokens of its
 own per rank (ExpertParallelMoE.forward_local: all-gather dispatch, local experts, NVLink
 combine), and on rank 0 the single-GPU MoE over the same world * t tokens:
@@ -51,13 +58,16 @@ def _time(fn, warmup, launches):
 
 
 def case_attn(a):
-    c = synth.attention_case(B=a.b, Hq=a.hq, Hkv=a.hkv, ctx=(a.ctx_lo, a.ctx_hi), pool_pages=a.pool, device="cuda",
-                             seed=0)
+    page = a.page or 16
+    pool = max(a.pool, (a.b * (a.ctx_hi + page)) // page + 8)
+    c = synth.attention_case(B=a.b, Hq=a.hq, Hkv=a.hkv, D=a.d, ctx=(a.ctx_lo, a.ctx_hi), page=page, pool_pages=pool,
+                             device="cuda", seed=0)
     fn = lambda: ops.attn_decode(c["q"], c["k_cache"], c["v_cache"], c["page_table"], c["seq_lens"],  # noqa
                                  c["k_scale"], c["v_scale"], c["sm_scale"])
     us = _time(fn, a.warmup, a.launches)
-    by = sum(c["lens"]) * a.hkv * 128 * 2
-    return {"case": "attn", "B": a.b, "hq": a.hq, "hkv": a.hkv, "ctx": [a.ctx_lo, a.ctx_hi], "us": us, "kv_bytes": by,
+    by = sum(c["lens"]) * a.hkv * a.d * 2
+    return {"case": "attn", "B": a.b, "hq": a.hq, "hkv": a.hkv, "d": a.d, "page": page, "ctx": [a.ctx_lo, a.ctx_hi],
+            "us": us, "kv_bytes": by,
             "gbs": by / us / 1e3}
 
 
@@ -84,6 +94,36 @@ def case_moe(a):
     per_expert = 3072 * 2048 + 3072 * 256 + 4096 * 768 + 4096 * 96
     by = hit * per_expert + a.t * 4096 * 4 + 64 * 4096 * 2
     return {"case": "moe", "t": a.t, "experts_hit": hit, "us": us, "bytes": by, "gbs": by / us / 1e3}
+
+
+def case_muse_layer(a):
+    from .problems import muse_decode_layer as prob
+    w, d = synth.muse_layer_case(B=a.b, L=a.l, ctx=(a.ctx_lo, a.ctx_hi), page=a.page or 1, window=a.window,
+                                 local_bias=0.0, seed=0, device="cuda")
+    state = prob.prepare(w)
+    T = a.b * a.l
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            _, _, ids = prob.kernel_fn(d, state)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    R = 10
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        for _ in range(R):
+            prob.kernel_fn(d, state)
+    us = _time(gr.replay, 3, max(1, a.launches)) / R
+    lids = torch.remainder(ids.long() - 32, 256)
+    hit = int(torch.unique(lids[lids < 32]).numel())
+    per_expert = 8192 * 2048 + 8192 * 256 + 4096 * 2048 + 4096 * 256
+    dense = 2 * (2304 * 8192 + 8192 * 1024 + 4096 * 8192 + (1024 if T <= 8 else 8192) * 4096 + 2 * 256 * 8192)
+    lens = d["seq_lens"].long() + a.l
+    kv = int((lens.clamp(max=a.window + a.l - 1) if a.window else lens).sum()) * 2 * 2 * 64
+    by = dense + hit * per_expert + kv
+    return {"case": "muse_layer", "B": a.b, "L": a.l, "T": T, "ctx": [a.ctx_lo, a.ctx_hi], "page": a.page or 1,
+            "window": a.window, "experts_hit": hit, "us": round(us, 2), "bytes": by, "gbs": round(by / us / 1e3, 1)}
 
 
 def case_tp(a):
@@ -218,7 +258,7 @@ def case_moe_ep(a):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["attn", "gemv", "moe", "tp", "moe_ep"])
+    ap.add_argument("case", choices=["attn", "gemv", "moe", "tp", "moe_ep", "muse_layer"])
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--launches", type=int, default=3)
     ap.add_argument("--b", type=int, default=64)
@@ -232,10 +272,15 @@ def main(argv=None):
     ap.add_argument("--n", type=int, default=10240)
     ap.add_argument("--family", type=int, default=0)
     ap.add_argument("--t", type=int, default=8)
+    ap.add_argument("--l", type=int, default=1, help="muse_layer: new tokens per request")
+    ap.add_argument("--page", type=int, default=0, help="page size (attn: 16, muse_layer: 1 when 0)")
+    ap.add_argument("--d", type=int, default=128, help="attn: head dim")
+    ap.add_argument("--window", type=int, default=0, help="muse_layer: sliding window (0: full)")
     ap.add_argument("--kk", default="1024", help="tp: comma-separated O-projection K per rank")
     a = ap.parse_args(argv)
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-    res = {"attn": case_attn, "gemv": case_gemv, "moe": case_moe, "tp": case_tp, "moe_ep": case_moe_ep}[a.case](a)
+    res = {"attn": case_attn, "gemv": case_gemv, "moe": case_moe, "tp": case_tp, "moe_ep": case_moe_ep,
+           "muse_layer": case_muse_layer}[a.case](a)
     if res is not None:
         print(json.dumps(res), flush=True)
     return 0
