@@ -81,9 +81,12 @@ __device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, c
       : "memory");
 }
 
-template <int D, int HKV>
-__global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kernel(
-    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+// The kernel body; G4 compiles the TMA gather4 page fetch in (attn_decode_g4_kernel, maps
+// given), else the producer only issues bulk copies (attn_decode_kernel): an instantiation with
+// the gather code measured ~1.5x slower on 16 KB pages that never take it (C4: 382 vs 248 us).
+template <int D, int HKV, bool G4>
+__device__ __forceinline__ void attn_decode_body(const CUtensorMap* kmap, const CUtensorMap* vmap,
+                                                 const AttnArgs& a) {
   using C = AttnCfg<D, HKV>;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* stages = smem;
@@ -164,7 +167,7 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
       // cost per copy (measured: 2 KB pages 5.4 vs 4.0 TB/s over 148 SMs; 128-byte pages are
       // bound by that cost at ~0.4 TB/s).  The row count is padded to a multiple of 4 with the
       // last row (the extra tokens are masked).
-      const int g4_rows = a.g4_rpp > 0 ? cur.nseg * a.g4_rpp : 0;
+      const int g4_rows = (G4 && a.g4_rpp > 0) ? cur.nseg * a.g4_rpp : 0;
       const int g4_ops = (g4_rows + 3) >> 2;
       if (g4_rows) my_bytes = (uint32_t)g4_ops * 4u * (uint32_t)a.g4_rb * 2u;
       bool ok = true;
@@ -192,8 +195,8 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kerne
           rid[i] = (pg >= 0 && pg < a.num_pages) ? pg * a.g4_rpp + r % a.g4_rpp : -1;
         }
         if (o < g4_ops) {
-          tma_gather4(sk + (size_t)o * 4 * a.g4_rb, &kmap, rid, &full[stage], pol);
-          tma_gather4(sv + (size_t)o * 4 * a.g4_rb, &vmap, rid, &full[stage], pol);
+          tma_gather4(sk + (size_t)o * 4 * a.g4_rb, kmap, rid, &full[stage], pol);
+          tma_gather4(sv + (size_t)o * 4 * a.g4_rb, vmap, rid, &full[stage], pol);
         }
       }
       for (int sg = lane; sg < cur.nseg && !g4_rows; sg += 32) {
@@ -536,6 +539,17 @@ __device__ void merge_row(const AttnArgs& a, int b, int hq, int U, int uf, int u
   }
 }
 
+template <int D, int HKV>
+__global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_kernel(AttnArgs a) {
+  attn_decode_body<D, HKV, false>(nullptr, nullptr, a);
+}
+
+template <int D, int HKV>
+__global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_g4_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, AttnArgs a) {
+  attn_decode_body<D, HKV, true>(&kmap, &vmap, a);
+}
+
 // The merge kernel: one warp per (sequence, query head), after the whole decode grid.
 __global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int NSUB, int D) {
   pdl_trigger();
@@ -662,6 +676,8 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
   if (smem > 232448) return OKC_ERR_INVALID;  // 227 KB per block on sm_100
   if (smem > configured) {
     if (cudaFuncSetAttribute(attn_decode_kernel<D, HKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_decode_g4_kernel<D, HKV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
       return OKC_ERR_LAUNCH;
     configured = smem;
@@ -681,8 +697,11 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
       a.g4_rb = rb;
     }
   }
-  int st = okc_host::launch_k(attn_decode_kernel<D, HKV>, dim3(a.num_ctas), dim3(C::THREADS), smem, stream, dim3(1),
-                              km, vm, a);
+  int st = a.g4_rpp > 0
+               ? okc_host::launch_k(attn_decode_g4_kernel<D, HKV>, dim3(a.num_ctas), dim3(C::THREADS), smem, stream,
+                                    dim3(1), km, vm, a)
+               : okc_host::launch_k(attn_decode_kernel<D, HKV>, dim3(a.num_ctas), dim3(C::THREADS), smem, stream,
+                                    dim3(1), a);
   if (st) return st;
   return launch_attn_merge(a, C::TS, C::NSUB, D, stream);
 }
