@@ -682,13 +682,16 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
       return OKC_ERR_LAUNCH;
     configured = smem;
   }
-  // TMA gather4 maps when pages are one or two 2 KB rows, or one row of a multiple of 16 bytes
-  // below 2 KB, and units start on a page (always so for one-token pages, whatever the window)
+  // TMA gather4 maps when a page is below 2 KB (a multiple of 16 bytes: one gather row each) and
+  // units start on a page (always so for one-token pages, whatever the window).  Pages of one or
+  // two 2 KB rows gather as well, but measured no faster than bulk copies in the kernel instance
+  // without the gather code (1 KV head: 64.4 vs 65.2 us; 2 heads: 103 vs 86 us), so they take
+  // that instance; one-token pages of 128 bytes gather at 2x the bulk rate (155 vs 297 us).
   CUtensorMap km{}, vm{};
   a.g4_rpp = 0;
   a.g4_rb = 0;
   const long long pb = (long long)a.P * C::ROW;
-  const int rb = (pb % 2048 == 0 && pb / 2048 <= 2) ? 2048 : (pb < 2048 && pb % 16 == 0 ? (int)pb : 0);
+  const int rb = (pb < 2048 && pb % 16 == 0) ? (int)pb : 0;
   if (rb && (a.window == 0 || a.P == 1) && C::TS % a.P == 0 && C::KV_BYTES % (4 * rb) == 0 &&
       !getenv("OKC_ATTN_NO_GATHER")) {
     const long long rows = a.num_pages * (pb / rb);
