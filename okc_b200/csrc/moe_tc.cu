@@ -18,21 +18,26 @@
 //    TMA write, one read) and the activation tiles, so its bandwidth is not the limit; per 64
 //    K the tensor pipe then needs 4 MMAs (M = 128 weight rows, N = the chunk's pairs, K = 16),
 //    issued from one thread at ~50 cycles each.
-//  * A unit = (active expert, chunk of <= 64 of its pairs, 128 weight rows: 64 gate + the same 64
+//  * A unit = (active expert, chunk of <= NT of its pairs, 128 weight rows: 64 gate + the same 64
 //    up rows (GATED) or 128 down rows) over the full K.  Units of all experts are split evenly
 //    over a persistent grid (one CTA per SM).
 //  * Warp 0 streams the unit's packed codes and e4m3 scales with 2-D TMA boxes (256 K per stage:
 //    one 128-byte row of codes per weight row, 128-byte swizzle, plus 16 scale bytes a row) into
-//    a 6-deep raw ring.  Warp 2 loads the stage's activation tiles (4 boxes of 64 K x 16/32/64
-//    rows, f16, 128-byte swizzle) into one of 2 stage slots.
+//    the raw ring (8 stages at NT = 32, 6 at NT = 64).  Warp 2 loads the stage's activation tiles
+//    (4 boxes of 64 K x 16/32/64 rows, f16, 128-byte swizzle) into the activation ring, one slot
+//    deeper than the A slots (MtCfg below).
 //  * Warps 3..10 dequantise, two per TMEM lane quarter (one per 128-K half of a stage), lane =
-//    one weight row: cvt.rn.f16x2.e2m1x2, x the e4m3 group scale in f16 (exact), tcgen05.st into
-//    the stage's A slot (128 columns; 2 slots), tcgen05.wait::st, tcgen05.fence, mbarrier arrive.
+//    one weight row: the stage's codes and scales into registers (the raw slot is freed there),
+//    cvt.rn.f16x2.e2m1x2, x the e4m3 group scale in f16 (exact), tcgen05.st into the stage's A
+//    slot (128 columns; 3 slots at NT = 32, 2 at NT = 64), tcgen05.wait::st, tcgen05.fence,
+//    mbarrier arrive (warp 3's arrival also waits for the stage's activation tiles).
 //    f16 rather than bf16 because the e2m1 -> f16x2 conversion is one instruction; the same
 //    product in bf16 takes about four more integer operations per pair.
 //  * Two issuer threads (warps 1 and 15, on different SM sub-partitions): issuer h issues the 8
 //    MMAs of K half h of each stage into its own double-buffered TMEM accumulator and frees the
-//    stage with one tcgen05.commit (the slot's empty barrier counts both).  One thread waits
+//    stage (A slot and activation slot) with one tcgen05.commit (the stage's done barrier counts
+//    both).  Measured: issuing half the MMAs (a timing-only variant) takes 10-15 % off the expert
+//    time, so the two issuing threads are part of what paces a stage (~0.67 us).  One thread waits
 //    ~50 cycles per MMA it issues; two threads issue concurrently (measured), which doubles the
 //    MMA rate.  For GATED the A rows are ordered so that each 32-lane quarter holds 16 gate rows
 //    and the same 16 up rows: lanes l and l + 16 of an epilogue warp hold g and u of one column.
@@ -45,22 +50,39 @@
 
 namespace okc {
 
-constexpr int kMtNT = 64;                          // pairs per unit (MMA N <= 64)
 constexpr int kMtKC = 256;                         // K per stage
-constexpr int kMtRaw = 6;                          // raw ring depth
-constexpr int kMtNS = 2;                           // stage slots: A in TMEM + activation tiles
 constexpr int kMtCodes = 128 * (kMtKC / 2);        // 16 KB of codes per raw stage
 constexpr int kMtRawBytes = kMtCodes + 128 * (kMtKC / 16);  // + 2 KB of scales
-constexpr int kMtAtom = kMtNT * 128;               // <= 64 pairs x 64 K f16
-constexpr int kMtAct = 4 * kMtAtom;                // a stage's activation tiles
 constexpr int kMtThreads = 16 * 32;
-constexpr int kMtBody = kMtRaw * kMtRawBytes + kMtNS * kMtAct;
-constexpr int kMtBars = 2 * kMtRaw + 2 * kMtNS + 2 + 2 + 1;
-constexpr int kMtSmem = 1024 + kMtBody + kMtBars * 8 + 16 + (2 * 257 + 2 * 256) * 4;
-constexpr uint32_t kMtAcol = 256;                  // TMEM: 2 issuers x 2 accumulators in 0..255, A slots after
-static_assert(kMtRawBytes % 1024 == 0 && kMtAtom % 1024 == 0, "1024-aligned tiles");
-static_assert(kMtSmem <= 232448, "shared memory");
-static_assert(kMtAcol + kMtNS * 128 <= 512, "tensor memory");
+static_assert(kMtRawBytes % 1024 == 0, "1024-aligned tiles");
+
+// NT = pairs per unit (the MMA's N): 32 while the experts see few tokens, 64 beyond.  TMEM holds
+// 2 issuers x 2 accumulator buffers of NT columns (0 .. 4 NT) and after them the NS A slots (128
+// columns each: NT = 32: 3, NT = 64: 2).  The stage ring has three parts of different depths:
+//  * RAW raw stages (packed codes + scales, 18 KB): a dequantising warp frees its stage as soon
+//    as it holds the stage's codes in registers, so a slot is held for the copy's latency only
+//    (~3 us under a full weight stream) and RAW stages keep RAW x 18 KB in flight per SM;
+//  * NA activation slots (NA = NS + 1), loaded ahead of the A slot they pair with: an activation
+//    copy (an L2 hit) takes ~1.5 us to land behind the weight stream;
+//  * NS A slots in TMEM (the dequantised weights).
+// Stage q's MMAs complete on sdone[q % NA], which frees activation slot q % NA and A slot q % NS.
+template <int NT_>
+struct MtCfg {
+  static constexpr int NT = NT_;
+  static constexpr int ACOL = 4 * NT;                     // first A-slot column
+  static constexpr int NS = (512 - ACOL) / 128;           // A slots
+  static constexpr int NA = NS + 1;                       // activation slots
+  static constexpr int ATOM = NT * 128;                   // <= NT pairs x 64 K f16
+  static constexpr int ACT = 4 * ATOM;                    // a stage's activation tiles
+  static constexpr int RAW_FIT = (232448 - 1024 - NA * ACT - 5120) / kMtRawBytes;
+  static constexpr int RAW = RAW_FIT > 8 ? 8 : RAW_FIT;   // NT = 32: 8, NT = 64: 6
+  static constexpr int BODY = RAW * kMtRawBytes + NA * ACT;
+  static constexpr int BARS = 2 * RAW + NS + 2 * NA + 2 + 2 + 1;
+  static constexpr int SMEM = 1024 + BODY + BARS * 8 + 16 + (2 * 257 + 2 * 256) * 4;
+  static_assert(ATOM % 1024 == 0, "1024-aligned tiles");
+  static_assert(SMEM <= 232448, "shared memory");
+  static_assert(ACOL + NS * 128 <= 512 && NS >= 2 && NA >= NS && RAW >= 4, "rings");
+};
 
 __device__ __forceinline__ void mt_tma_u8(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
                                           uint64_t policy) {
@@ -124,7 +146,7 @@ struct MtUnit {
 
 // Unit u: active expert i with upre[i] <= u < upre[i+1], then chunk-major, row block minor.
 __device__ __forceinline__ MtUnit mt_unit(const int* act, const int* upre, const int* cnt, const int* off,
-                                          int nact, int nrb, int u) {
+                                          int nact, int nrb, int u, int nt) {
   int lo = 0, hi = nact - 1;
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
@@ -135,12 +157,12 @@ __device__ __forceinline__ MtUnit mt_unit(const int* act, const int* upre, const
   const int ch = v / nrb;
   t.e = act[lo];
   t.rb = v - ch * nrb;
-  t.row0 = off[t.e] + ch * kMtNT;
-  t.n = min(kMtNT, cnt[t.e] - ch * kMtNT);
+  t.row0 = off[t.e] + ch * nt;
+  t.n = min(nt, cnt[t.e] - ch * nt);
   return t;
 }
 
-template <bool GATED>
+template <bool GATED, int NT>
 __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
     const __grid_constant__ CUtensorMap cmap, const __grid_constant__ CUtensorMap smap,
     const __grid_constant__ CUtensorMap a16, const __grid_constant__ CUtensorMap a32,
@@ -148,15 +170,17 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
     const int32_t* __restrict__ offsets, const int32_t* __restrict__ pairs, const float* __restrict__ gs,
     const float* __restrict__ rs, __nv_bfloat16* __restrict__ inter_out, __nv_bfloat16* __restrict__ y_out, int K,
     int NR, int I, int E, int* err) {
+  using C = MtCfg<NT>;
   extern __shared__ uint8_t mt_raw_smem[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(mt_raw_smem) + 1023) & ~uintptr_t(1023));
   uint8_t* rawr = base;
-  uint8_t* actt = rawr + kMtRaw * kMtRawBytes;
-  uint64_t* raw_full = reinterpret_cast<uint64_t*>(actt + kMtNS * kMtAct);
-  uint64_t* raw_empty = raw_full + kMtRaw;
-  uint64_t* sfull = raw_empty + kMtRaw;
-  uint64_t* sempty = sfull + kMtNS;
-  uint64_t* acc_full = sempty + kMtNS;
+  uint8_t* actt = rawr + C::RAW * kMtRawBytes;
+  uint64_t* raw_full = reinterpret_cast<uint64_t*>(actt + C::NA * C::ACT);
+  uint64_t* raw_empty = raw_full + C::RAW;
+  uint64_t* sfull = raw_empty + C::RAW;  // [NS] A slot q % NS written (8 dequantising warps)
+  uint64_t* afull = sfull + C::NS;       // [NA] activation tiles of stage q landed
+  uint64_t* sdone = afull + C::NA;       // [NA] stage q's MMAs completed (both issuers' commits)
+  uint64_t* acc_full = sdone + C::NA;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -172,8 +196,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
   const int nk = K / kMtKC;
   pdl_trigger();
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kMtRaw; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 8); }
-    for (int i = 0; i < kMtNS; ++i) { mbar_init(&sfull[i], 9); mbar_init(&sempty[i], 2); }
+    for (int i = 0; i < C::RAW; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 8); }
+    for (int i = 0; i < C::NS; ++i) mbar_init(&sfull[i], 8);
+    for (int i = 0; i < C::NA; ++i) { mbar_init(&afull[i], 1); mbar_init(&sdone[i], 2); }
     for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 2); mbar_init(&acc_empty[i], 4); }
     mbar_init(drain, 2);
     *abort_flag = 0;
@@ -193,7 +218,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       if (e < E) { cnt[e] = c; off[e] = offsets[e]; }
       const bool on = c > 0;
       const unsigned bal = __ballot_sync(0xffffffffu, on);
-      const int nu = on ? ((c + kMtNT - 1) / kMtNT) * nrb : 0;
+      const int nu = on ? ((c + C::NT - 1) / C::NT) * nrb : 0;
       int v = nu;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -229,11 +254,11 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       const uint64_t pol = l2_evict_first_policy();
       uint32_t r = 0;
       for (int u = u0; u < u1 && !*abort_flag; ++u) {
-        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
+        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u, C::NT);
         const int wrow = t.e * rows_w + t.rb * (GATED ? 64 : 128);
         for (int ks = 0; ks < nk; ++ks, ++r) {
-          const int s = (int)(r % kMtRaw);
-          if (!mbar_wait(&raw_empty[s], ((r / kMtRaw) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; break; }
+          const int s = (int)(r % C::RAW);
+          if (!mbar_wait(&raw_empty[s], ((r / C::RAW) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; break; }
           mbar_arrive_expect_tx(&raw_full[s], kMtRawBytes);
           uint8_t* d = rawr + s * kMtRawBytes;
           if (GATED) {  // raw rows 0-63: gate rows, 64-127: the same up rows
@@ -247,8 +272,8 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
           }
         }
       }
-      for (uint32_t i = r > (uint32_t)kMtRaw ? r - kMtRaw : 0u; i < r; ++i)  // copies in flight land
-        if (!mbar_wait(&raw_full[i % kMtRaw], (i / kMtRaw) & 1u, err)) break;
+      for (uint32_t i = r > (uint32_t)C::RAW ? r - C::RAW : 0u; i < r; ++i)  // copies in flight land
+        if (!mbar_wait(&raw_full[i % C::RAW], (i / C::RAW) & 1u, err)) break;
     }
   } else if (warp == 2) {
     // ---------------------------- activation producer ----------------------------
@@ -256,22 +281,21 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       uint32_t q = 0;
       bool ok = true;
       for (int u = u0; u < u1 && ok && !*abort_flag; ++u) {
-        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
+        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u, C::NT);
         const int box = t.n <= 16 ? 16 : (t.n <= 32 ? 32 : 64);
         const CUtensorMap* map = box == 16 ? &a16 : (box == 32 ? &a32 : &a64);
         for (int ks = 0; ks < nk; ++ks, ++q) {
-          const int s = (int)(q % kMtNS);
-          if (!mbar_wait(&sempty[s], ((q / kMtNS) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; ok = false; break; }
-          mbar_arrive_expect_tx(&sfull[s], (uint32_t)box * 128u * 4u);
-          uint8_t* d = actt + s * kMtAct;
+          const int s = (int)(q % C::NA);
+          if (!mbar_wait(&sdone[s], ((q / C::NA) & 1u) ^ 1u, err, abort_flag)) { *abort_flag = 1; ok = false; break; }
+          mbar_arrive_expect_tx(&afull[s], (uint32_t)box * 128u * 4u);
+          uint8_t* d = actt + s * C::ACT;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) tma_load_2d(d + j * kMtAtom, map, ks * kMtKC + 64 * j, t.row0, &sfull[s]);
+          for (int j = 0; j < 4; ++j) tma_load_2d(d + j * C::ATOM, map, ks * kMtKC + 64 * j, t.row0, &afull[s]);
         }
       }
-      // the copies issued land before the CTA can leave: a slot's full phase completes only
-      // with them (and the dequant arrivals, bounded by the same wait)
-      for (uint32_t i = q > (uint32_t)kMtNS ? q - kMtNS : 0u; i < q; ++i)
-        if (!mbar_wait(&sfull[i % kMtNS], (i / kMtNS) & 1u, err)) break;
+      // the copies issued land before the CTA can leave
+      for (uint32_t i = q > (uint32_t)C::NA ? q - C::NA : 0u; i < q; ++i)
+        if (!mbar_wait(&afull[i % C::NA], (i / C::NA) & 1u, err)) break;
     }
   } else if (warp == 1 || warp == 15) {
     // ---------------------------------- MMA issuers ---------------------------------
@@ -284,22 +308,23 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       int ui = 0;
       bool ok = true;
       for (int u = u0; u < u1 && ok; ++u, ++ui) {
-        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
+        const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u, C::NT);
         const uint32_t idesc = umma_idesc_f16((t.n + 15) & ~15);
         const int buf = ui & 1;
         if (!mbar_wait(&acc_empty[buf], ((uint32_t)(ui >> 1) & 1u) ^ 1u, err, abort_flag)) { ok = false; break; }
         for (int ks = 0; ks < nk; ++ks, ++q) {
-          const int s = (int)(q % kMtNS);
-          if (!mbar_wait(&sfull[s], (q / kMtNS) & 1u, err, abort_flag)) { ok = false; break; }
+          const int s = (int)(q % C::NS), sx = (int)(q % C::NA);
+          // sfull[s] completes only after the stage's activation tiles landed (warp 3 waits for them)
+          if (!mbar_wait(&sfull[s], (q / C::NS) & 1u, err, abort_flag)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t sa = smem_u32(actt + s * kMtAct + 2 * h * kMtAtom);
-          const uint32_t ta = tmem + kMtAcol + (uint32_t)s * 128u + 64u * h;
+          const uint32_t sa = smem_u32(actt + sx * C::ACT + 2 * h * C::ATOM);
+          const uint32_t ta = tmem + C::ACOL + (uint32_t)s * 128u + 64u * h;
 #pragma unroll
           for (int k16 = 0; k16 < 8; ++k16) {
-            const uint64_t db = umma_desc_sw128(sa + (k16 >> 2) * kMtAtom) + 2 * (k16 & 3);
-            umma_f16_ts(tmem + 128 * h + buf * 64, ta + 8 * k16, db, idesc, (ks | k16) ? 1u : 0u);
+            const uint64_t db = umma_desc_sw128(sa + (k16 >> 2) * C::ATOM) + 2 * (k16 & 3);
+            umma_f16_ts(tmem + 2 * C::NT * h + buf * C::NT, ta + 8 * k16, db, idesc, (ks | k16) ? 1u : 0u);
           }
-          umma_commit(&sempty[s]);
+          umma_commit(&sdone[sx]);
         }
         if (ok) umma_commit(&acc_full[buf]);
       }
@@ -317,21 +342,34 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
     const int m = 32 * qd + lane;  // A row = TMEM lane
     const int rho = GATED ? (lane < 16 ? 16 * qd + lane : 64 + 16 * qd + lane - 16) : m;  // raw row
     const int sw = rho & 7;
-    const uint32_t tbase = tmem + ((uint32_t)(32 * qd) << 16) + kMtAcol + 64u * half;
+    const uint32_t tbase = tmem + ((uint32_t)(32 * qd) << 16) + C::ACOL + 64u * half;
     uint32_t q = 0;
     bool ok = true;
     for (int u = u0; u < u1 && ok; ++u) {
       for (int ks = 0; ks < nk; ++ks, ++q) {
-        const int sr = (int)(q % kMtRaw), s = (int)(q % kMtNS);
-        if (!mbar_wait(&raw_full[sr], (q / kMtRaw) & 1u, err, abort_flag) ||
-            !mbar_wait(&sempty[s], ((q / kMtNS) & 1u) ^ 1u, err, abort_flag)) {
+        const int sr = (int)(q % C::RAW), s = (int)(q % C::NS);
+        if (!mbar_wait(&raw_full[sr], (q / C::RAW) & 1u, err, abort_flag)) {
           *abort_flag = 1;
           ok = false;
           break;
         }
+        // the stage's codes and scales into registers, then the raw slot is free again
         const uint8_t* rw = rawr + sr * kMtRawBytes;
         const uint8_t* crow = rw + rho * 128;
         const uint2 sc8 = *reinterpret_cast<const uint2*>(rw + kMtCodes + rho * 16 + 8 * half);
+        uint4 cw[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) cw[i] = *reinterpret_cast<const uint4*>(crow + (((4 * half + i) ^ sw) << 4));
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&raw_empty[sr]);
+        // A slot s is free once stage q - NS's MMAs completed (sdone of that stage; the phase
+        // after it needs stage q - NS + NA >= q, not yet written, so the parity is unambiguous)
+        if (q >= (uint32_t)C::NS &&
+            !mbar_wait(&sdone[(q - C::NS) % C::NA], ((q - C::NS) / C::NA) & 1u, err, abort_flag)) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
         uint32_t sd[8];
         mt_scales2(sc8.x & 0xffffu, sd[0], sd[1]);
         mt_scales2(sc8.x >> 16, sd[2], sd[3]);
@@ -339,7 +377,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
         mt_scales2(sc8.y >> 16, sd[6], sd[7]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {  // 16 code bytes = K [128 half + 32 i, + 32), scale groups 2i, 2i+1
-          const uint4 c = *reinterpret_cast<const uint4*>(crow + (((4 * half + i) ^ sw) << 4));
+          const uint4 c = cw[i];
           const uint32_t wv[4] = {c.x, c.y, c.z, c.w};
           uint32_t o[16];
 #pragma unroll
@@ -357,8 +395,10 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         __syncwarp();
         if (lane == 0) {
+          // one of the 8 arrivals waits for the stage's activation tiles, so the MMA issuers wait
+          // on one barrier per stage (afull's next phase needs this stage's MMAs: unambiguous)
+          if (warp == 3 && !mbar_wait(&afull[q % C::NA], (q / C::NA) & 1u, err, abort_flag)) *abort_flag = 1;
           mbar_arrive(&sfull[s]);
-          mbar_arrive(&raw_empty[sr]);
         }
       }
     }
@@ -368,16 +408,16 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
     const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
     int ui = 0;
     for (int u = u0; u < u1; ++u, ++ui) {
-      const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u);
+      const MtUnit t = mt_unit(act, upre, cnt, off, nact, nrb, u, C::NT);
       const int buf = ui & 1;
       if (!mbar_wait(&acc_full[buf], (uint32_t)(ui >> 1) & 1u, err, abort_flag) || *abort_flag) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const float gsc = gs[t.e];
-      const uint32_t taddr = tmem + lane_base + buf * 64;
+      const uint32_t taddr = tmem + lane_base + buf * C::NT;
       for (int c0 = 0; c0 < t.n; c0 += 16) {
         float v[16], v1[16];
         tmem_ld16(taddr + c0, v);        // K halves 0 of the stages (issuer 0)
-        tmem_ld16(taddr + 128 + c0, v1);  // K halves 1 (issuer 1)
+        tmem_ld16(taddr + 2 * C::NT + c0, v1);  // K halves 1 (issuer 1)
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) v[jj] += v1[jj];
 #pragma unroll
@@ -494,6 +534,25 @@ int launch_moe_rows_f16(const void* src, const int32_t* pairs, const int32_t* of
                             reinterpret_cast<const __nv_bfloat16*>(src), pairs, offsets, E, topk, K, dst, rs);
 }
 
+template <bool GATED, int NT>
+static int launch_moe_tc_nt(const CUtensorMap& cm, const CUtensorMap& sm, const CUtensorMap& m16,
+                            const CUtensorMap& m32, const CUtensorMap& m64, const int32_t* counts,
+                            const int32_t* offsets, const int32_t* pairs, const float* gs, const float* rs,
+                            __nv_bfloat16* inter, __nv_bfloat16* y, int K, int NR, int I, int E, int* err,
+                            cudaStream_t stream) {
+  using C = MtCfg<NT>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(moe_tc_kernel<GATED, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+        cudaSuccess)
+      return OKC_ERR_LAUNCH;
+    configured = true;
+  }
+  return okc_host::launch_k(moe_tc_kernel<GATED, NT>, dim3(okc_host::num_sms()), dim3(kMtThreads), C::SMEM, stream,
+                            dim3(1), cm, sm, m16, m32, m64, counts, offsets, pairs, gs, rs, inter, y, K, NR, I, E,
+                            err);
+}
+
 // GATED: act = xg [rows][K = H], weights W13, out inter; else act = inter as f16 [rows][K = I],
 // weights W2, out y.  rs: the activation rows' scales.
 template <bool GATED>
@@ -507,16 +566,12 @@ int launch_moe_tc(const void* w, const void* sf, int E, const __half* act, int r
       !mt_u8_map(&sm, sf, K / 16, wrows, kMtKC / 16, box_rows, false) || !mt_f16_map(&m16, act, K, rows, 16) ||
       !mt_f16_map(&m32, act, K, rows, 32) || !mt_f16_map(&m64, act, K, rows, 64))
     return OKC_ERR_INVALID;
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(moe_tc_kernel<GATED>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMtSmem) !=
-        cudaSuccess)
-      return OKC_ERR_LAUNCH;
-    configured = true;
-  }
-  return okc_host::launch_k(moe_tc_kernel<GATED>, dim3(okc_host::num_sms()), dim3(kMtThreads), kMtSmem, stream,
-                            dim3(1), cm, sm, m16, m32, m64, counts, offsets, pairs, gs, rs, inter, y, K, NR, I, E,
-                            err);
+  // chunks of <= 32 pairs (3 A slots, 8 raw stages) while the experts see few tokens each, 64 beyond
+  if (rows <= 8 * 128)
+    return launch_moe_tc_nt<GATED, 32>(cm, sm, m16, m32, m64, counts, offsets, pairs, gs, rs, inter, y, K, NR, I, E,
+                                       err, stream);
+  return launch_moe_tc_nt<GATED, 64>(cm, sm, m16, m32, m64, counts, offsets, pairs, gs, rs, inter, y, K, NR, I, E,
+                                     err, stream);
 }
 
 template int launch_moe_tc<true>(const void*, const void*, int, const __half*, int, const float*, const int32_t*,
