@@ -132,11 +132,11 @@ def test_ctypes_signatures_match_header_prototypes():
     assert not bad, "\n".join(bad)
 
 
-def _kernel_bodies():
+def _kernel_bodies(pattern=r"__global__\s+void\s+(?:__launch_bounds__\([^)]*\)\s*)?(\w+)\s*\("):
     bodies = {}
     for f in sorted((ROOT / "okc_b200" / "csrc").glob("*.cu")):
         src = f.read_text()
-        for m in re.finditer(r"__global__\s+void\s+(?:__launch_bounds__\([^)]*\)\s*)?(\w+)\s*\(", src):
+        for m in re.finditer(pattern, src):
             i = src.index("{", m.end())
             depth, j = 0, i
             while True:
@@ -160,11 +160,16 @@ def test_every_pdl_launched_kernel_waits_before_returning():
     src = "".join(f.read_text() for f in (ROOT / "okc_b200" / "csrc").glob("*.cu"))
     launched = set(re.findall(r"launch_k\(\s*(?:okc::)?(\w+)", src))
     bodies = _kernel_bodies()
+    # device functions a kernel delegates to (a kernel body that is a call of a templated body
+    # function): their text is spliced in place of the call, one level deep
+    helpers = _kernel_bodies(r"__device__\s+(?:__forceinline__\s+|__noinline__\s+)?void\s+(\w+)\s*\(")
     assert launched, "no launch_k call found"
     bad = []
     for name in sorted(launched):
         assert name in bodies, f"launch_k of unknown kernel {name}"
         body = bodies[name]
+        for h, hb in helpers.items():
+            body = re.sub(r"\b" + h + r"\s*(<[^;{}]*>)?\s*\([^;]*\);", lambda _m, hb=hb: hb, body)
         w = body.find("pdl_wait()")
         if w < 0:
             bad.append(f"{name}: no pdl_wait")
