@@ -58,7 +58,8 @@ int okc_read_device_error(const void* workspace, okc_stream_t stream);
  * (`_project`: M=1 `_gemv` :8-15, split-K `_small_gemm` :18-39 + `_reduce_projection`
  * :42-48) and muse_bf16_proj/projection/runtime.py:80-220 (`run_config`).
  * Picks the split-K skinny kernel (M <= 32, cluster/DSMEM split-K reduction) or the
- * tcgen05 kernel (M >= 33) itself.  out_fp32 != 0 writes fp32 y (a row-parallel partial
+ * tcgen05 kernel (M >= 33) itself; M > 256 (prefill) runs as 256-row blocks of the tcgen05
+ * kernel (the workspace covers one block).  out_fp32 != 0 writes fp32 y (a row-parallel partial
  * that an all-reduce sums), else bf16.  residual (bf16, may be NULL) is added to the
  * fp32 accumulator before the single rounding.  K must be a multiple of 8, ldx/ldw
  * multiples of 8 elements, x and w 16-byte aligned (y and residual element-aligned).
@@ -128,7 +129,8 @@ int okc_gemm_bf16_rope_kv_append(const void* x, int ldx, const void* w, int ldw,
  * muse_prefill_layer/submission.py:155-156.
  * qkv: bf16 [B, ldqkv] holding q (Hq*D) | k (Hkv*D) | v (Hkv*D) per row.
  * positions: int64 [B] (the new token's position = cached length).  page_table int32
- * [B, max_pages] (ld = table_ld).  Slot = page_table[b][pos / P] * P + pos % P.
+ * [B, max_pages] (ld = table_ld; table_ld 0: every row reads table row 0, e.g. a block of
+ * one request's tokens).  Slot = page_table[b][pos / P] * P + pos % P.
  * Writes q_out bf16 [B, Hq, D] (rotated), k_cache/v_cache e4m3 [num_pages, P, Hkv, D] at
  * the slot (k rotated, / k_scale[h]; v / v_scale[h]; RNE, overflow -> NaN like torch),
  * and slots_out int64 [B] (may be NULL).  inv_freq fp32 [D/2] (NULL = no RoPE).  D % 8 == 0,

@@ -38,7 +38,7 @@ int okc_read_device_error(const void* workspace, okc_stream_t stream) {
 
 // ------------------------------------------------------------------------------ GEMM
 size_t okc_gemm_bf16_workspace_bytes(int M, int N, int K) {
-  size_t tc = okc::tc_gemm_ws_bytes(M, N, K);
+  size_t tc = okc::tc_gemm_ws_bytes(M > 256 ? 256 : M, N, K);  // M > 256 runs in 256-row blocks
   return 256 + tc;
 }
 
@@ -50,6 +50,21 @@ int okc_gemm_bf16_ex(const void* x, int ldx, const void* w, int ldw, void* y, in
   if (!aligned16(x) || !aligned16(w)) return OKC_ERR_ALIGNMENT;
   const uintptr_t ya = reinterpret_cast<uintptr_t>(y), ra = reinterpret_cast<uintptr_t>(residual);
   if ((ya & (out_fp32 ? 3u : 1u)) || (ra & 1u)) return OKC_ERR_ALIGNMENT;
+  if (M > 256 && family != 1) {
+    // prefill token counts: 256-row blocks through the tcgen05 path (a block's weight tiles are
+    // re-read from L2 by the next block); a tail of <= 32 rows takes the skinny kernel
+    const size_t esz = out_fp32 ? 4 : 2;
+    for (int m0 = 0; m0 < M; m0 += 256) {
+      const int mm = M - m0 < 256 ? M - m0 : 256;
+      const void* rs = residual ? reinterpret_cast<const uint8_t*>(residual) + (size_t)m0 * ldy * 2 : nullptr;
+      const int st = okc_gemm_bf16_ex(reinterpret_cast<const uint8_t*>(x) + (size_t)m0 * ldx * 2, ldx, w, ldw,
+                                      reinterpret_cast<uint8_t*>(y) + (size_t)m0 * ldy * esz, ldy, rs, mm, N, K,
+                                      out_fp32, family == 2 && mm > 32 ? 2 : 0, splits, workspace,
+                                      workspace_bytes, stream);
+      if (st) return st;
+    }
+    return OKC_OK;
+  }
   if (family == 0) family = (M > 32 && okc::tc_gemm_supported(M, N, K, ldx, ldw) && ldy % 8 == 0) ? 2 : 1;
   if (family == 2) {
     if (!okc::tc_gemm_supported(M, N, K, ldx, ldw)) return OKC_ERR_INVALID;
@@ -111,7 +126,8 @@ int okc_rope_kv_append_ex(const void* qkv, int ldqkv, const int64_t* positions, 
   if (!qkv || !positions || !page_table || !k_scale || !v_scale || !q_out || !k_cache || !v_cache)
     return OKC_ERR_INVALID;
   if (B <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || D % 2 || page_size <= 0 || num_pages <= 0 ||
-      max_pages <= 0 || table_ld < max_pages || ldqkv < (Hq + 2 * Hkv) * D || ldqkv % 8 || D % 8 || D > 512)
+      max_pages <= 0 || (table_ld != 0 && table_ld < max_pages) || table_ld < 0 || ldqkv < (Hq + 2 * Hkv) * D ||
+      ldqkv % 8 || D % 8 || D > 512)
     return OKC_ERR_INVALID;
   if (qk_norm && (D > 256 || (D & (D - 1)))) return OKC_ERR_INVALID;  // a head's lanes fit one warp
   if (!aligned16(qkv) || !aligned16(q_out) || (reinterpret_cast<uintptr_t>(k_cache) & 7) ||

@@ -24,6 +24,13 @@ Stages, each on this library's kernels:
     decode/projections.py:54-57) and the final boundary (post_ffn_norm scaling, ffn gate,
     next_pre_attn_norm).
 
+Token counts: decode steps and verify blocks (q_len 1 / 8), and prefill blocks (q_len 200-16384,
+muse_prefill_layer/submission.py:201-218, the same layer): projections beyond 256 tokens run as
+256-row tcgen05 blocks, the append of a long block runs per request with its table row shared,
+the experts run in passes of 2048 tokens, and attention is the decode kernel with one query
+row per token (each token reads its own visible span: O(q_len^2) cache reads, correct but not
+a prefill attention kernel).
+
 Queries: the reference's window-0 path hands FA3 an e4m3-rounded query
 (decode/attention.py:150-165); here every layer keeps the bf16 query of its split-attention
 path (q x qk_scale_factor rounded to bf16), the more precise of the two."""
@@ -43,6 +50,7 @@ POST_NORM_EPS = 1e-8    # decode/spec.py:76
 ROPE_BASE = 500000.0    # decode/runtime.py:33
 ROUTE_SCALE = 0.1767766952966369   # decode/runtime.py:31 (router_output_multiplier)
 ROUTE_EPS = 1e-15
+MOE_CHUNK = 2048        # tokens per expert pass (okc_moe_permute: T * top_k <= 16384)
 
 
 def _gate_coeffs(w: torch.Tensor):
@@ -80,10 +88,18 @@ def _attention(data: dict, state: dict) -> torch.Tensor:
     vs = data["v_scale"].float().reshape(-1).expand(hkv).contiguous()
     positions = data["positions"].reshape(-1).long()
     table = data["page_table"]
-    table_rows = table.repeat_interleave(L, dim=0) if L > 1 else table
     inv = state["inv_freq"] if cfg.get("rope_theta", 0) else None
-    q = ops.rope_kv_append(qkv, positions, table_rows, data["k_cache"], data["v_cache"], ks, vs, hq, hkv, d, inv,
-                           q_scale=cfg["qk_scale_factor"], qk_norm=True, norm_eps=RMS_EPS)
+    if L <= 8:
+        table_rows = table.repeat_interleave(L, dim=0) if L > 1 else table
+        q = ops.rope_kv_append(qkv, positions, table_rows, data["k_cache"], data["v_cache"], ks, vs, hq, hkv, d, inv,
+                               q_scale=cfg["qk_scale_factor"], qk_norm=True, norm_eps=RMS_EPS)
+    else:  # prefill blocks: one append per request, its table row shared by its L tokens (row stride 0)
+        q = torch.empty((B * L, hq, d), dtype=torch.bfloat16, device=qkv.device)
+        for b in range(B):
+            r = slice(b * L, (b + 1) * L)
+            ops.rope_kv_append(qkv[r], positions[r], table[b:b + 1].expand(L, -1), data["k_cache"], data["v_cache"],
+                               ks, vs, hq, hkv, d, inv, q_out=q[r], q_scale=cfg["qk_scale_factor"], qk_norm=True,
+                               norm_eps=RMS_EPS)
     lens = (positions + 1).to(torch.int32)
     gate = qkv[:, (hq + 2 * hkv) * d:(2 * hq + 2 * hkv) * d]
     out = ops.attn_decode(q, data["k_cache"], data["v_cache"], table, lens, ks, vs, cfg["sm_scale"], gate=gate,
@@ -111,10 +127,13 @@ def kernel_fn(data: dict, state: dict):
         ids, wts = ops.route_sigmoid(logits, state["router_bias"], TOP_K, scale=ROUTE_SCALE, eps=ROUTE_EPS)
     # this GPU's experts are global ids local_start .. local_start + 31 (decode/runtime.py:71)
     lids = torch.remainder(ids - data["local_start"].to(torch.int32), N_EXPERTS).to(torch.int32)
-    perm = ops.moe_permute(lids, 0, LOCAL_EXPERTS)
-    ex = ops.moe_experts(x, lids, wts, perm, state["w13"], state["w13_sf"], state["w13_gs"], state["w2"],
-                         state["w2_sf"], state["w2_gs"], 0, post_gain=state["post_expert_gain"],
-                         post_eps=POST_NORM_EPS)
+    ex = torch.empty_like(x)
+    for c0 in range(0, T, MOE_CHUNK):  # the permutation takes up to 2048 tokens x 8 slots
+        c = slice(c0, min(T, c0 + MOE_CHUNK))
+        perm = ops.moe_permute(lids[c], 0, LOCAL_EXPERTS)
+        ops.moe_experts(x[c], lids[c], wts[c], perm, state["w13"], state["w13_sf"], state["w13_gs"], state["w2"],
+                        state["w2_sf"], state["w2_gs"], 0, out=ex[c], post_gain=state["post_expert_gain"],
+                        post_eps=POST_NORM_EPS)
     if small:  # only this GPU's 1024 rows of the unpooler; the boundary sees zeros beyond them
         ffn = torch.zeros((T, HIDDEN), dtype=torch.bfloat16, device=ex.device)
         ops.gemm(ex, state["unpooler"][:1024], out=ffn[:, :1024])

@@ -93,6 +93,17 @@ def test_tcgen05_family(ops, M, K, N):
     torch.testing.assert_close(y3.cpu(), ref.gemm(x.cpu(), w.cpu(), out_fp32=True), rtol=1e-3, atol=1e-3)
 
 
+@pytest.mark.parametrize("M,family", [(300, 0), (544, 0), (600, 2)])
+def test_prefill_token_counts(ops, M, family):
+    """M > 256 (prefill blocks): 256-row blocks of the tcgen05 kernel, a tail of <= 32 rows on the
+    skinny kernel (M = 544 = 2 x 256 + 32), with and without a residual."""
+    from okc_b200 import synth
+    x, w = synth.projection_case(M, 4096, 2304, seed=M, device="cuda")
+    _close(ops.gemm(x, w, family=family), ref.gemm(x.cpu(), w.cpu()), f"prefill M{M}")
+    r = torch.randn((M, 2304), device="cuda").to(torch.bfloat16)
+    _close(ops.gemm(x, w, residual=r, family=family), ref.gemm(x.cpu(), w.cpu(), residual=r.cpu()), f"prefill+res M{M}")
+
+
 def test_contract_short_names(ops):
     """okc_gemv_bf16 / okc_rmsnorm (the contract's short names) give the same bytes as the
     full entry points."""
