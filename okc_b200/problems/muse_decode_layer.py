@@ -51,6 +51,7 @@ ROPE_BASE = 500000.0    # decode/runtime.py:33
 ROUTE_SCALE = 0.1767766952966369   # decode/runtime.py:31 (router_output_multiplier)
 ROUTE_EPS = 1e-15
 MOE_CHUNK = 2048        # tokens per expert pass (okc_moe_permute: T * top_k <= 16384)
+ATTN_CHUNK = 2048       # query rows per attention call in a prefill block (okc_attn_decode_fp8: <= 4096)
 
 
 def _gate_coeffs(w: torch.Tensor):
@@ -102,8 +103,19 @@ def _attention(data: dict, state: dict) -> torch.Tensor:
                                norm_eps=RMS_EPS)
     lens = (positions + 1).to(torch.int32)
     gate = qkv[:, (hq + 2 * hkv) * d:(2 * hq + 2 * hkv) * d]
-    out = ops.attn_decode(q, data["k_cache"], data["v_cache"], table, lens, ks, vs, cfg["sm_scale"], gate=gate,
-                          out_eps=RMS_EPS, window=int(cfg.get("window", 0) or 0), q_per_seq=L)
+    window = int(cfg.get("window", 0) or 0)
+    if L <= 8:
+        out = ops.attn_decode(q, data["k_cache"], data["v_cache"], table, lens, ks, vs, cfg["sm_scale"], gate=gate,
+                              out_eps=RMS_EPS, window=window, q_per_seq=L)
+        return out.view(B * L, hq * d)
+    # prefill blocks: per request, up to ATTN_CHUNK query rows per call (its table row for all)
+    out = torch.empty((B * L, hq, d), dtype=torch.bfloat16, device=qkv.device)
+    for b in range(B):
+        for c0 in range(0, L, ATTN_CHUNK):
+            r = slice(b * L + c0, b * L + min(L, c0 + ATTN_CHUNK))
+            n = r.stop - r.start
+            ops.attn_decode(q[r], data["k_cache"], data["v_cache"], table[b:b + 1], lens[r], ks, vs, cfg["sm_scale"],
+                            out=out[r], gate=gate[r], out_eps=RMS_EPS, window=window, q_per_seq=n)
     return out.view(B * L, hq * d)
 
 
