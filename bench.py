@@ -19,8 +19,9 @@ roofline  = the attention kernel (the dominant kernel) measured with CUDA events
             instrumented copy of the step graph: algorithmic KV bytes / duration vs
             MEASURED_PEAKS.json hbm_gbs; stages_us = per-stage times from the same copy.
 rooflines = (N = 1) standalone records of the other workloads: paged attention decode (batch 64,
-            ctx U[512, 32768]), the projection at M = 1 and M = 128 (K 8192, N 10240) and the
-            W4A16 MoE at T = 8 and T = 256, each µs, algorithmic bytes and fraction of HBM.
+            ctx U[512, 32768]), the projection at M = 1 and M = 128 (K 8192, N 10240), the
+            W4A16 MoE at T = 8 and T = 256 and the Muse decode-layer drop-in at 33 tokens (page 1),
+            each µs, algorithmic bytes and fraction of HBM.
 cpu_baseline / --impl reference = the oracle (the reference's PyTorch path restated, CPU
             fp32) on the host cores: one warm-up, then the median of 5 samples; a sample runs
             the projections at all 128 tokens and the attention of 8 of the 128 sequences,
@@ -281,6 +282,24 @@ def extra_rooflines(dev, peak, peak_kind):
                                           f"T {T}, E 64 top-8 softmax, H 4096, I 1536, NVFP4 weights; "
                                           f"{statistics.mean(hit):.1f} distinct experts hit")
     del banks
+    torch.cuda.empty_cache()
+    # Muse TP8/EP8 decode layer drop-in (problems/muse_decode_layer.py): 33 requests x 1 token,
+    # ctx U[10000, 20000], page 1, no local routing preference; 1.1 GB of weights per step
+    from okc_b200.problems import muse_decode_layer as muse
+    w, d = synth.muse_layer_case(B=33, L=1, ctx=(10000, 20000), page=1, local_bias=0.0, seed=40, device=dev)
+    st = muse.prepare(w)
+    _, _, ids = muse.kernel_fn(d, st)
+    lids = torch.remainder(ids.long() - 32, 256)
+    hit = int(torch.unique(lids[lids < 32]).numel())
+    us = _graph_us([lambda: muse.kernel_fn(d, st)] * 4)
+    dense = 2 * (2304 * 8192 + 8192 * 1024 + 4096 * 8192 + 8192 * 4096 + 2 * 256 * 8192)
+    per_exp = 8192 * 2048 + 8192 * 256 + 4096 * 2048 + 4096 * 256
+    kv = int((d["seq_lens"].long() + 1).sum()) * 2 * 2 * 64
+    recs["muse_decode_layer_t33_page1"] = _record(us, dense + hit * per_exp + kv, peak, peak_kind,
+                                                  "problems/muse_decode_layer.py (23 okc kernels per step)",
+                                                  f"33 x 1 token, ctx U[10000,20000], page 1, 16q/2kv D64, "
+                                                  f"32 local NVFP4 experts (H = I = 4096), {hit} hit")
+    del w, d, st
     torch.cuda.empty_cache()
     return recs
 

@@ -101,7 +101,11 @@ def _attention(data: dict, state: dict) -> torch.Tensor:
             ops.rope_kv_append(qkv[r], positions[r], table[b:b + 1].expand(L, -1), data["k_cache"], data["v_cache"],
                                ks, vs, hq, hkv, d, inv, q_out=q[r], q_scale=cfg["qk_scale_factor"], qk_norm=True,
                                norm_eps=RMS_EPS)
-    lens = (positions + 1).to(torch.int32)
+    cs = data.get("cache_seqlens")
+    if L == 1 and cs is not None and cs.dtype == torch.int32 and cs.is_contiguous():
+        lens = cs  # seq_lens + 1: each token's own position + 1 (spec.py:64)
+    else:
+        lens = (positions + 1).to(torch.int32)
     gate = qkv[:, (hq + 2 * hkv) * d:(2 * hq + 2 * hkv) * d]
     window = int(cfg.get("window", 0) or 0)
     if L <= 8:
@@ -129,9 +133,10 @@ def kernel_fn(data: dict, state: dict):
                                                  pre_eps=RMS_EPS, router=small)
     x = ops.rmsnorm(ops.gemm(h, state["pooler"]), state["pre_expert_norm"], RMS_EPS, unit_offset=True)
     if small:
-        xh = router_in.to(torch.bfloat16)
-        xl = (router_in - xh.float()).to(torch.bfloat16)
-        logits = ops.router_logits(torch.cat([xh, xl], 0), state["router_hilo"])
+        hl = torch.empty((2 * T, HIDDEN), dtype=torch.bfloat16, device=h.device)  # [hi; lo] of router_in
+        hl[:T].copy_(router_in)
+        torch.sub(router_in, hl[:T], out=hl[T:])  # fp32 difference, rounded once to bf16
+        logits = ops.router_logits(hl, state["router_hilo"])
         ids, wts = ops.route_sigmoid(logits[:T], state["router_bias"], TOP_K, logits_lo=logits[T:],
                                      scale=ROUTE_SCALE, eps=ROUTE_EPS)
     else:
@@ -147,7 +152,10 @@ def kernel_fn(data: dict, state: dict):
                         state["w2_sf"], state["w2_gs"], 0, out=ex[c], post_gain=state["post_expert_gain"],
                         post_eps=POST_NORM_EPS)
     if small:  # only this GPU's 1024 rows of the unpooler; the boundary sees zeros beyond them
-        ffn = torch.zeros((T, HIDDEN), dtype=torch.bfloat16, device=ex.device)
+        bufs = state.setdefault("_ffn_small", {})
+        if T not in bufs:  # columns 1024.. are zero once and never written
+            bufs[T] = torch.zeros((T, HIDDEN), dtype=torch.bfloat16, device=ex.device)
+        ffn = bufs[T]
         ops.gemm(ex, state["unpooler"][:1024], out=ffn[:, :1024])
     else:
         ffn = ops.gemm(ex, state["unpooler"])
