@@ -33,11 +33,13 @@
 //    mbarrier arrive (warp 3's arrival also waits for the stage's activation tiles).
 //    f16 rather than bf16 because the e2m1 -> f16x2 conversion is one instruction; the same
 //    product in bf16 takes about four more integer operations per pair.
-//  * Two issuer threads (warps 1 and 15, on different SM sub-partitions): issuer h issues the 8
-//    MMAs of K half h of each stage into its own double-buffered TMEM accumulator and frees the
+//  * Two issuer threads (warps 1 and 15, on different SM sub-partitions; four at NT = 32): issuer
+//    h issues the 8 MMAs of K half h of each stage into its own double-buffered TMEM accumulator and frees the
 //    stage (A slot and activation slot) with one tcgen05.commit (the stage's done barrier counts
-//    both).  Measured: issuing half the MMAs (a timing-only variant) takes 10-15 % off the expert
-//    time, so the two issuing threads are part of what paces a stage (~0.67 us).  One thread waits
+//    both).  At NT = 32 four threads (warps 1, 15, 16, 18) issue a K quarter each.  Measured:
+//    issuing half the MMAs (a timing-only variant) takes 10-15 % off the expert time, four
+//    issuers instead of two only 2-3 %: the tensor pipe's time per MMA (A read from TMEM, one
+//    M = 128 x K = 16 step whatever N) rather than the issuing threads paces a stage.  One thread waits
 //    ~50 cycles per MMA it issues; two threads issue concurrently (measured), which doubles the
 //    MMA rate.  For GATED the A rows are ordered so that each 32-lane quarter holds 16 gate rows
 //    and the same 16 up rows: lanes l and l + 16 of an epilogue warp hold g and u of one column.
@@ -53,7 +55,6 @@ namespace okc {
 constexpr int kMtKC = 256;                         // K per stage
 constexpr int kMtCodes = 128 * (kMtKC / 2);        // 16 KB of codes per raw stage
 constexpr int kMtRawBytes = kMtCodes + 128 * (kMtKC / 16);  // + 2 KB of scales
-constexpr int kMtThreads = 16 * 32;
 static_assert(kMtRawBytes % 1024 == 0, "1024-aligned tiles");
 
 // NT = pairs per unit (the MMA's N): 32 while the experts see few tokens, 64 beyond.  TMEM holds
@@ -69,7 +70,11 @@ static_assert(kMtRawBytes % 1024 == 0, "1024-aligned tiles");
 template <int NT_>
 struct MtCfg {
   static constexpr int NT = NT_;
-  static constexpr int ACOL = 4 * NT;                     // first A-slot column
+  // MMA-issuing threads: 4 at NT = 32 (one per SM sub-partition, each a K quarter of a stage;
+  // their 4 x 2 accumulators fit beside 2 A slots), 2 at NT = 64 (K halves)
+  static constexpr int NI = NT == 32 ? 4 : 2;
+  static constexpr int THREADS = (NI == 4 ? 19 : 16) * 32;  // NI = 4: issuers on warps 1, 15, 16, 18
+  static constexpr int ACOL = 2 * NI * NT;                // first A-slot column
   static constexpr int NS = (512 - ACOL) / 128;           // A slots
   static constexpr int NA = NS + 1;                       // activation slots
   static constexpr int ATOM = NT * 128;                   // <= NT pairs x 64 K f16
@@ -163,7 +168,7 @@ __device__ __forceinline__ MtUnit mt_unit(const int* act, const int* upre, const
 }
 
 template <bool GATED, int NT>
-__global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
+__global__ void __launch_bounds__(MtCfg<NT>::THREADS, 1) moe_tc_kernel(
     const __grid_constant__ CUtensorMap cmap, const __grid_constant__ CUtensorMap smap,
     const __grid_constant__ CUtensorMap a16, const __grid_constant__ CUtensorMap a32,
     const __grid_constant__ CUtensorMap a64, const int32_t* __restrict__ counts,
@@ -198,9 +203,9 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::RAW; ++i) { mbar_init(&raw_full[i], 1); mbar_init(&raw_empty[i], 8); }
     for (int i = 0; i < C::NS; ++i) mbar_init(&sfull[i], 8);
-    for (int i = 0; i < C::NA; ++i) { mbar_init(&afull[i], 1); mbar_init(&sdone[i], 2); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], 2); mbar_init(&acc_empty[i], 4); }
-    mbar_init(drain, 2);
+    for (int i = 0; i < C::NA; ++i) { mbar_init(&afull[i], 1); mbar_init(&sdone[i], C::NI); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&acc_full[i], C::NI); mbar_init(&acc_empty[i], 4); }
+    mbar_init(drain, C::NI);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -297,13 +302,14 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       for (uint32_t i = q > (uint32_t)C::NA ? q - C::NA : 0u; i < q; ++i)
         if (!mbar_wait(&afull[i % C::NA], (i / C::NA) & 1u, err)) break;
     }
-  } else if (warp == 1 || warp == 15) {
+  } else if (warp == 1 || warp == 15 || (C::NI == 4 && (warp == 16 || warp == 18))) {
     // ---------------------------------- MMA issuers ---------------------------------
-    // Issuer h (warp 1: h = 0, warp 15: h = 1) takes the K half h of every stage into its own
-    // accumulator; one thread issuing kind::f16 MMAs waits ~50 cycles per instruction, two
-    // threads on different SM sub-partitions issue concurrently.
+    // Issuer h (warps 1, 15, 16, 18: h = 0, 1, 2, 3) takes the K slice h (of NI) of every stage
+    // into its own accumulator; one thread issuing kind::f16 MMAs waits ~50-76 cycles per
+    // instruction, and threads on different SM sub-partitions issue concurrently (measured at
+    // full rate each for up to 4).
     if (lane == 0) {
-      const int h = warp == 15 ? 1 : 0;
+      const int h = warp == 1 ? 0 : (warp == 15 ? 1 : (warp == 16 ? 2 : 3));
       uint32_t q = 0;
       int ui = 0;
       bool ok = true;
@@ -317,10 +323,10 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
           // sfull[s] completes only after the stage's activation tiles landed (warp 3 waits for them)
           if (!mbar_wait(&sfull[s], (q / C::NS) & 1u, err, abort_flag)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const uint32_t sa = smem_u32(actt + sx * C::ACT + 2 * h * C::ATOM);
-          const uint32_t ta = tmem + C::ACOL + (uint32_t)s * 128u + 64u * h;
+          const uint32_t sa = smem_u32(actt + sx * C::ACT + (4 / C::NI) * h * C::ATOM);
+          const uint32_t ta = tmem + C::ACOL + (uint32_t)s * 128u + (128u / C::NI) * h;
 #pragma unroll
-          for (int k16 = 0; k16 < 8; ++k16) {
+          for (int k16 = 0; k16 < 16 / C::NI; ++k16) {
             const uint64_t db = umma_desc_sw128(sa + (k16 >> 2) * C::ATOM) + 2 * (k16 & 3);
             umma_f16_ts(tmem + 2 * C::NT * h + buf * C::NT, ta + 8 * k16, db, idesc, (ks | k16) ? 1u : 0u);
           }
@@ -336,7 +342,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       umma_commit(drain);  // arrives once every MMA issued above has completed
       mbar_wait(drain, 0u, err);
     }
-  } else if (warp <= 10) {
+  } else if (warp >= 3 && warp <= 10) {
     // -------------------------------- dequantisation --------------------------------
     const int qd = warp & 3, half = (warp - 3) >> 2;
     const int m = 32 * qd + lane;  // A row = TMEM lane
@@ -402,7 +408,7 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
         }
       }
     }
-  } else {
+  } else if (warp >= 11 && warp <= 14) {
     // ------------------------------------ epilogue ------------------------------------
     const int q4 = warp & 3;
     const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
@@ -416,10 +422,13 @@ __global__ void __launch_bounds__(kMtThreads, 1) moe_tc_kernel(
       const uint32_t taddr = tmem + lane_base + buf * C::NT;
       for (int c0 = 0; c0 < t.n; c0 += 16) {
         float v[16], v1[16];
-        tmem_ld16(taddr + c0, v);        // K halves 0 of the stages (issuer 0)
-        tmem_ld16(taddr + 2 * C::NT + c0, v1);  // K halves 1 (issuer 1)
+        tmem_ld16(taddr + c0, v);  // issuer 0's K slices of the stages
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) v[jj] += v1[jj];
+        for (int h = 1; h < C::NI; ++h) {  // + the other issuers' slices
+          tmem_ld16(taddr + 2 * C::NT * h + c0, v1);
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) v[jj] += v1[jj];
+        }
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) {
           const int j = c0 + jj;
@@ -548,7 +557,7 @@ static int launch_moe_tc_nt(const CUtensorMap& cm, const CUtensorMap& sm, const 
       return OKC_ERR_LAUNCH;
     configured = true;
   }
-  return okc_host::launch_k(moe_tc_kernel<GATED, NT>, dim3(okc_host::num_sms()), dim3(kMtThreads), C::SMEM, stream,
+  return okc_host::launch_k(moe_tc_kernel<GATED, NT>, dim3(okc_host::num_sms()), dim3(C::THREADS), C::SMEM, stream,
                             dim3(1), cm, sm, m16, m32, m64, counts, offsets, pairs, gs, rs, inter, y, K, NR, I, E,
                             err);
 }
