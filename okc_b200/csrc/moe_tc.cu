@@ -38,8 +38,9 @@
 //    stage (A slot and activation slot) with one tcgen05.commit (the stage's done barrier counts
 //    both).  At NT = 32 four threads (warps 1, 15, 16, 18) issue a K quarter each.  Measured:
 //    issuing half the MMAs (a timing-only variant) takes 10-15 % off the expert time, four
-//    issuers instead of two only 2-3 %: the tensor pipe's time per MMA (A read from TMEM, one
-//    M = 128 x K = 16 step whatever N) rather than the issuing threads paces a stage.  One thread waits
+//    issuers instead of two only 2-3 %, and ncu counts the tensor pipe active ~22 % of the
+//    time: a cost per MMA that neither the issuing threads nor the pipe's busy cycles show
+//    (the A operand read from TMEM is the remaining suspect) paces a stage.  One thread waits
 //    ~50 cycles per MMA it issues; two threads issue concurrently (measured), which doubles the
 //    MMA rate.  For GATED the A rows are ordered so that each 32-lane quarter holds 16 gate rows
 //    and the same 16 up rows: lanes l and l + 16 of an epilogue warp hold g and u of one column.
