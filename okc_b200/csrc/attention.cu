@@ -464,54 +464,66 @@ __device__ __forceinline__ void attn_decode_body(const CUtensorMap* kmap, const 
 // ---------------------------------------------------------------------------------------
 // Merge of one (sequence b, query head hq): out = v_scale[h] * sum_parts 2^(m_i - M) acc_i /
 // sum_parts 2^(m_i - M) l_i over the split-KV partials of the CTAs that covered b (units
-// [uf, ul] of U over C CTAs; NSUB sub-tiles per unit), by one warp, lane owning D/32
-// consecutive d.  Parts are read in a fixed order (and through L2: they may come from other
-// SMs of the running grid), so the result does not depend on which CTA finished first.
-__device__ void merge_row(const AttnArgs& a, int b, int hq, int U, int uf, int ul, int NSUB, int D, int lane) {
+// [uf, ul] of U over C CTAs; NSUB sub-tiles per unit).  S warps share a (b, hq): warp s folds
+// the contiguous part range s of S (merge_fold, lane owning D/32 consecutive d), then warp 0
+// combines the folds in split order (merge_store).  Parts are read in a fixed order and through
+// L2 (they may come from other SMs of the running grid), so the result does not depend on which
+// CTA finished first.  S = 4 where units hold >= 4 sub-tiles (1-2 KV heads: with one KV head a
+// sequence has ~24 parts, which one warp reads in three dependent round trips; the merge took
+// ~10 of ~62 us at 128 sequences, 4 warps take it to ~57 us); S = 1 otherwise (8 KV heads: 2-3
+// parts per sequence, where the 4-warp form measured 268 vs 248 us for C4).
+
+__device__ void merge_fold(const AttnArgs& a, int b, int hq, int U, int uf, int ul, int NSUB, int D, int lane,
+                           int s, int S, float& M, float& L, float (&o)[4]) {
   const int per = D / 32;  // 4 (D = 128) or 2 (D = 64)
-  __nv_bfloat16* dst = a.out + (size_t)b * a.ldo + (size_t)hq * D + lane * per;
-  float o[4] = {0.f, 0.f, 0.f, 0.f};
-  float L = 0.f;
-  if (ul >= uf) {
-    const int cf = cta_of_unit(U, a.num_ctas, uf), cl = cta_of_unit(U, a.num_ctas, ul);
-    const int nparts = (cl - cf + 1) * NSUB;
-    auto row_of = [&](int p) { return ((size_t)(cf + p / NSUB + b) * NSUB + p % NSUB) * a.Hq + hq; };
-    // Batches of 8 parts: the (m, l) of part p0 + i sit in lane i, and the 8 parts' slices
-    // of acc are loaded in the same round, so one batch costs one memory round trip.  A
-    // running maximum carries the log-sum-exp across batches.
-    float M = -INFINITY;
-    for (int p0 = 0; p0 < nparts; p0 += 8) {
-      const int n = min(8, nparts - p0);
-      float2 ml = make_float2(-INFINITY, 0.f);
-      if (lane < n) ml = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + row_of(p0 + lane) * 2));
-      float4 v[8];
+  o[0] = o[1] = o[2] = o[3] = 0.f;
+  L = 0.f;
+  M = -INFINITY;
+  if (ul < uf) return;
+  const int cf = cta_of_unit(U, a.num_ctas, uf), cl = cta_of_unit(U, a.num_ctas, ul);
+  const int nparts = (cl - cf + 1) * NSUB;
+  const int q0 = nparts * s / S, q1 = nparts * (s + 1) / S;
+  auto row_of = [&](int p) { return ((size_t)(cf + p / NSUB + b) * NSUB + p % NSUB) * a.Hq + hq; };
+  // Batches of 8 parts: the (m, l) of part p0 + i sit in lane i, and the 8 parts' slices of acc
+  // are loaded in the same round, so one batch costs one memory round trip.  A running maximum
+  // carries the log-sum-exp across batches.
+  for (int p0 = q0; p0 < q1; p0 += 8) {
+    const int n = min(8, q1 - p0);
+    float2 ml = make_float2(-INFINITY, 0.f);
+    if (lane < n) ml = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + row_of(p0 + lane) * 2));
+    float4 v[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < n) {
-          const float* src = a.ws_acc + row_of(p0 + i) * D + lane * per;
-          if (per == 4) v[i] = __ldcg(reinterpret_cast<const float4*>(src));
-          else { const float2 t = __ldcg(reinterpret_cast<const float2*>(src)); v[i].x = t.x; v[i].y = t.y; }
-        }
-      }
-      const float Mn = fmaxf(M, warp_max(ml.x));
-      if (Mn == -INFINITY) continue;  // nothing attended yet
-      if (M != -INFINITY && M != Mn) {
-        const float r = exp2f(M - Mn);
-        L *= r;
-        o[0] *= r; o[1] *= r; o[2] *= r; o[3] *= r;
-      }
-      M = Mn;
-      const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
-      L += w * ml.y;  // per lane; summed over the warp at the end
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float wi = __shfl_sync(0xffffffffu, w, i);
-        o[0] += wi * v[i].x; o[1] += wi * v[i].y; o[2] += wi * v[i].z; o[3] += wi * v[i].w;
+    for (int i = 0; i < 8; ++i) {
+      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (i < n) {
+        const float* src = a.ws_acc + row_of(p0 + i) * D + lane * per;
+        if (per == 4) v[i] = __ldcg(reinterpret_cast<const float4*>(src));
+        else { const float2 t = __ldcg(reinterpret_cast<const float2*>(src)); v[i].x = t.x; v[i].y = t.y; }
       }
     }
-    L = warp_sum(L);
+    const float Mn = fmaxf(M, warp_max(ml.x));
+    if (Mn == -INFINITY) continue;  // nothing attended yet
+    if (M != -INFINITY && M != Mn) {
+      const float r = exp2f(M - Mn);
+      L *= r;
+      o[0] *= r; o[1] *= r; o[2] *= r; o[3] *= r;
+    }
+    M = Mn;
+    const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+    L += w * ml.y;  // per lane; summed over the warp at the end
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float wi = __shfl_sync(0xffffffffu, w, i);
+      o[0] += wi * v[i].x; o[1] += wi * v[i].y; o[2] += wi * v[i].z; o[3] += wi * v[i].w;
+    }
   }
+  L = warp_sum(L);
+}
+
+// out[b][hq] = o / L * v_scale (then Muse's rms(o) * sigmoid(gate) when a.gate), as bf16.
+__device__ void merge_store(const AttnArgs& a, int b, int hq, int D, int lane, float L, float (&o)[4]) {
+  const int per = D / 32;
+  __nv_bfloat16* dst = a.out + (size_t)b * a.ldo + (size_t)hq * D + lane * per;
   const float scale = L > 0.f ? a.v_scale[hq / a.G] / L : 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) o[i] *= scale;
@@ -551,14 +563,43 @@ __global__ void __launch_bounds__(AttnCfg<D, HKV>::THREADS, 1) attn_decode_g4_ke
 }
 
 // The merge kernel: one warp per (sequence, query head), after the whole decode grid.
-__global__ void __launch_bounds__(256) attn_merge_kernel(AttnArgs a, int TS, int NSUB, int D) {
+template <int S>
+__global__ void __launch_bounds__(256 * S) attn_merge_kernel(AttnArgs a, int TS, int NSUB, int D) {
   pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hq = blockIdx.y * 8 + warp;
-  if (hq >= a.Hq) return;
-  merge_row(a, b, hq, a.ws_prefix[a.B], a.ws_prefix[b], a.ws_prefix[b + 1] - 1, NSUB, D, lane);
+  const int hl = warp / S, s = warp % S;
+  const int hq = blockIdx.y * 8 + hl;
+  const bool on = hq < a.Hq;
+  float M = -INFINITY, L = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+  if (on) merge_fold(a, b, hq, a.ws_prefix[a.B], a.ws_prefix[b], a.ws_prefix[b + 1] - 1, NSUB, D, lane, s, S, M, L, o);
+  if constexpr (S == 1) {
+    if (on) merge_store(a, b, hq, D, lane, L, o);
+    return;
+  }
+  __shared__ float fold[8][S][6][32];  // per head of the CTA and split: M, L, o[0..3]
+  fold[hl][s][0][lane] = M;
+  fold[hl][s][1][lane] = L;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) fold[hl][s][2 + i][lane] = o[i];
+  __syncthreads();
+  if (!on || s != 0) return;
+  float Ma = -INFINITY;
+#pragma unroll
+  for (int t = 0; t < S; ++t) Ma = fmaxf(Ma, fold[hl][t][0][lane]);
+  float La = 0.f, oa[4] = {0.f, 0.f, 0.f, 0.f};
+  if (Ma != -INFINITY) {
+#pragma unroll
+    for (int t = 0; t < S; ++t) {  // split order: deterministic
+      const float Mt = fold[hl][t][0][lane];
+      const float w = Mt == -INFINITY ? 0.f : exp2f(Mt - Ma);
+      La += w * fold[hl][t][1][lane];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) oa[i] += w * fold[hl][t][2 + i][lane];
+    }
+  }
+  merge_store(a, b, hq, D, lane, La, oa);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -710,7 +751,10 @@ static int launch_attn_t(AttnArgs& a, cudaStream_t stream) {
 }
 
 int launch_attn_merge(AttnArgs& a, int TS, int NSUB, int D, cudaStream_t stream) {
-  return okc_host::launch_k(attn_merge_kernel, dim3(a.B, (a.Hq + 7) / 8), dim3(256), 0, stream, dim3(1), a, TS,
+  if (NSUB >= 4)
+    return okc_host::launch_k(attn_merge_kernel<4>, dim3(a.B, (a.Hq + 7) / 8), dim3(1024), 0, stream, dim3(1), a, TS,
+                              NSUB, D);
+  return okc_host::launch_k(attn_merge_kernel<1>, dim3(a.B, (a.Hq + 7) / 8), dim3(256), 0, stream, dim3(1), a, TS,
                             NSUB, D);
 }
 
