@@ -18,8 +18,14 @@ Needs a checkout of the reference, named by $OKC_REFERENCE, and runs on CPU:
                      under Triton's CPU interpreter.  That interpreter rounds fp32 -> bf16 toward
                      zero (the GPU rounds to nearest even), so the tests pin the oracle's formula
                      against these with its rounding set to "trunc".
+  muse_layer_ref.pt  the whole layer, `kernel_fn` of muse_prefill_layer/submission.py:201-218, on
+                     three seeded cases (q_len 1 and 8, page 1 and 64, full and window 2048)
+                     whose inputs synth.muse_layer_case regenerates from the stored seeds; its
+                     `nvfp4` import is stubbed with oracle.moe.dequantize (pinned to the
+                     reference's `_decode_nvfp4` by nvfp4_decode.json).
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py              # every fixture
+    python tests/golden/make_golden.py muse_layer   # muse_layer_ref.pt only
 """
 
 from __future__ import annotations
@@ -263,6 +269,49 @@ def prefill_ops():
     return out
 
 
+# ------------------------------------------------------------- whole Muse layer (kernel_fn)
+MUSE_LAYER_CASES = [  # (B, q_len, ctx, page, window, data seed); weights from seed 500
+    (2, 1, (300, 600), 1, 0, 501),
+    (1, 8, (200, 400), 1, 2048, 502),
+    (3, 1, (100, 300), 64, 0, 503),
+]
+
+
+def muse_layer_reference():
+    """The reference's own PyTorch layer, muse_prefill_layer/submission.py:201-218 `kernel_fn`
+    (the layer the decode and prefill tasks share), on CPU inputs that synth.muse_layer_case
+    regenerates bit for bit from their seeds (1.1 GB of weights are not stored).  Its `nvfp4`
+    import (a module of the challenge harness, not in the checkout) is stubbed with
+    oracle.moe.dequantize, which tests/test_oracle_golden.py pins bit-exact to the reference's own
+    `_decode_nvfp4`.  Stored per case: hidden, stream, ids and the routing scores + bias the
+    reference chose from (its `route` wrapped to record its input)."""
+    import torch
+    sys.path.insert(0, str(HERE.parent.parent))
+    from oracle.moe import dequantize
+    from okc_b200 import synth
+    sys.modules["nvfp4"] = types.SimpleNamespace(dequantize=dequantize)
+    spec = importlib.util.spec_from_file_location("prefill_layer_ref", REF / "muse_prefill_layer/submission.py")
+    ref = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(ref)
+    seen = {}
+    route = ref.route
+
+    def recording_route(h, weights, top_k):
+        seen["h"] = h
+        return route(h, weights, top_k)
+    ref.route = recording_route
+    w, _ = synth.muse_layer_case(B=1, ctx=(4, 8), seed=500, device="cpu")
+    out = {"source": "muse_prefill_layer/submission.py:201-218 (kernel_fn), CPU", "weights_seed": 500, "cases": []}
+    for B, L, ctx, page, window, seed in MUSE_LAYER_CASES:
+        _, d = synth.muse_layer_case(B=B, L=L, ctx=ctx, page=page, window=window, seed=seed, device="cpu",
+                                     weights=w)
+        hidden, stream, ids = ref.kernel_fn(d, w)
+        scores = torch.sigmoid((seen["h"].float() @ w["router"].T) * 0.1767766952966369) + w["router_bias"]
+        out["cases"].append({"B": B, "L": L, "ctx": ctx, "page": page, "window": window, "seed": seed,
+                             "hidden": hidden, "stream": stream, "ids": ids, "scores": scores})
+    return out
+
+
 def main():
     if not REF.exists():
         raise SystemExit(f"reference checkout not found at {REF}")
@@ -271,8 +320,13 @@ def main():
     import torch
     torch.save(prefill_ops(), HERE / "prefill_ops.pt")
     finalize_boundary(HERE / "moe_boundary.pt")
+    torch.save(muse_layer_reference(), HERE / "muse_layer_ref.pt")
     print("wrote", *(p.name for p in sorted(HERE.glob("*")) if p.suffix in (".json", ".pt")))
 
 
 if __name__ == "__main__":
-    main()
+    if sys.argv[1:] == ["muse_layer"]:  # only the whole-layer fixture (the others unchanged)
+        import torch
+        torch.save(muse_layer_reference(), HERE / "muse_layer_ref.pt")
+    else:
+        main()
