@@ -19,7 +19,8 @@ Needs a checkout of the reference, named by $OKC_REFERENCE, and runs on CPU:
                      zero (the GPU rounds to nearest even), so the tests pin the oracle's formula
                      against these with its rounding set to "trunc".
   muse_layer_ref.pt  the whole layer, `kernel_fn` of muse_prefill_layer/submission.py:201-218, on
-                     three seeded cases (q_len 1 and 8, page 1 and 64, full and window 2048)
+                     four seeded cases (q_len 1, 8 and a 200-token prefill block, page 1 and
+                     64, full and window 2048; the prefill block's every 25th token stored)
                      whose inputs synth.muse_layer_case regenerates from the stored seeds; its
                      `nvfp4` import is stubbed with oracle.moe.dequantize (pinned to the
                      reference's `_decode_nvfp4` by nvfp4_decode.json).
@@ -270,10 +271,11 @@ def prefill_ops():
 
 
 # ------------------------------------------------------------- whole Muse layer (kernel_fn)
-MUSE_LAYER_CASES = [  # (B, q_len, ctx, page, window, data seed); weights from seed 500
-    (2, 1, (300, 600), 1, 0, 501),
-    (1, 8, (200, 400), 1, 2048, 502),
-    (3, 1, (100, 300), 64, 0, 503),
+MUSE_LAYER_CASES = [  # (B, q_len, ctx, page, window, data seed, stored row stride); weights seed 500
+    (2, 1, (300, 600), 1, 0, 501, 1),
+    (1, 8, (200, 400), 1, 2048, 502, 1),
+    (3, 1, (100, 300), 64, 0, 503, 1),
+    (1, 200, (100, 200), 1, 0, 504, 25),  # a prefill block: every 25th token's rows stored
 ]
 
 
@@ -302,13 +304,15 @@ def muse_layer_reference():
     ref.route = recording_route
     w, _ = synth.muse_layer_case(B=1, ctx=(4, 8), seed=500, device="cpu")
     out = {"source": "muse_prefill_layer/submission.py:201-218 (kernel_fn), CPU", "weights_seed": 500, "cases": []}
-    for B, L, ctx, page, window, seed in MUSE_LAYER_CASES:
+    for B, L, ctx, page, window, seed, stride in MUSE_LAYER_CASES:
         _, d = synth.muse_layer_case(B=B, L=L, ctx=ctx, page=page, window=window, seed=seed, device="cpu",
                                      weights=w)
         hidden, stream, ids = ref.kernel_fn(d, w)
         scores = torch.sigmoid((seen["h"].float() @ w["router"].T) * 0.1767766952966369) + w["router_bias"]
+        rows = torch.arange(0, B * L, stride)
         out["cases"].append({"B": B, "L": L, "ctx": ctx, "page": page, "window": window, "seed": seed,
-                             "hidden": hidden, "stream": stream, "ids": ids, "scores": scores})
+                             "rows": rows, "hidden": hidden[rows].clone(), "stream": stream[rows].clone(),
+                             "ids": ids[rows].clone(), "scores": scores[rows].clone()})
     return out
 
 

@@ -131,6 +131,7 @@ def test_muse_layer_oracle_matches_reference_kernel_fn():
     w, _ = synth.muse_layer_case(B=1, ctx=(4, 8), seed=fx["weights_seed"], device="cpu")
     _, d = synth.muse_layer_case(B=c["B"], L=c["L"], ctx=tuple(c["ctx"]), page=c["page"], window=c["window"],
                                  seed=c["seed"], device="cpu", weights=w)
+    assert torch.equal(c["rows"], torch.arange(c["B"] * c["L"]))
     h, st, _, _ = olayer.muse_decode_layer(d, w, ids_in=c["ids"])
     for got, exp, what in ((h, c["hidden"], "hidden"), (st, c["stream"], "stream")):
         torch.testing.assert_close(got.float(), exp.float(), rtol=2e-2, atol=8e-2, msg=what)
