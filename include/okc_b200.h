@@ -157,6 +157,25 @@ int okc_rope_kv_append_ex(const void* qkv, int ldqkv, const int64_t* positions,
                           void* workspace, size_t workspace_bytes, okc_stream_t stream);
 
 /* ------------------------------------------------------------------------------------
+ * Paged FP8 attention for prefill blocks: B requests of L new tokens each (rows b*L .. b*L+L-1
+ * of q / positions / out, their K/V already appended), each token attending the positions
+ * p <= its own (and p > own - window when window > 0) of its request's cache.  Replaces
+ * `attention` of muse_prefill_layer/submission.py:137-176 for q_len 200-16384 (after its
+ * cache write): q bf16 [B*L][ldq] (Hq heads of D, the scaled and rounded queries), caches e4m3
+ * [num_pages, P, Hkv, D] with per-head fp32 scales, page_table int32 [B][table_ld] (max_pages
+ * valid columns), positions int64 [B*L].  out bf16 [B*L][ldo] = softmax(q k^T * sm_scale) v,
+ * or with gate (bf16 [B*L][ld_gate], may be NULL) rms(o) * sigmoid(gate) per head (eps out_eps).
+ * D 64 or 128, Hq / Hkv <= 8.  Workspace >= 256 bytes, its first int the device error word
+ * (OKC_DEVERR_PAGE for a page id outside the pool; those positions read zeros).
+ * ---------------------------------------------------------------------------------- */
+int okc_attn_prefill_fp8(const void* q, int ldq, const void* k_cache, const void* v_cache,
+                         const int32_t* page_table, int table_ld, int max_pages, const int64_t* positions,
+                         const float* k_scale, const float* v_scale, const void* gate, int ld_gate,
+                         float out_eps, void* out, int ldo, int B, int L, int Hq, int Hkv, int D,
+                         int page_size, int64_t num_pages, float sm_scale, int window,
+                         void* workspace, size_t workspace_bytes, okc_stream_t stream);
+
+/* ------------------------------------------------------------------------------------
  * Paged FP8 attention decode (q_len = 1), split-KV with a log-sum-exp merge.
  * Replaces `_fused_attn` muse_attention_decode/submission.py:191-351 (its cached-context
  * splits and two-level merge), `_attention_parts`/`_attention_finish`

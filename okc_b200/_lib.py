@@ -52,6 +52,8 @@ SIGNATURES: dict[str, tuple] = {
                                        _i, _i, _i, _i, _i, _i64, _f, _i, _p, _i, _f, _p, _sz, _p]),
     "okc_attn_decode_fp8_ex": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
                                     _i, _i, _i, _i, _i, _i64, _f, _i, _i, _i, _p, _i, _f, _p, _sz, _p]),
+    "okc_attn_prefill_fp8": (_i, [_p, _i, _p, _p, _p, _i, _i, _p, _p, _p, _p, _i, _f, _p, _i, _i, _i, _i, _i, _i,
+                                  _i, _i64, _f, _i, _p, _sz, _p]),
     "okc_attn_decode_fp8": (_i, [_p, _i, _p, _p, _p, _i, _p, _p, _p, _p, _i,
                                  _i, _i, _i, _i, _i, _i64, _f, _i, _p, _sz, _p]),
     "okc_gemv_bf16": (_i, [_p, _p, _p, _i, _i, _i, _i, _p, _p]),

@@ -116,6 +116,28 @@ int okc_residual_boundary(const float* stream_in, const void* branch, int ld_bra
                                        router_out, T, H, post_eps, pre_eps, stream);
 }
 
+// --------------------------------------------------------------- prefill attention
+int okc_attn_prefill_fp8(const void* q, int ldq, const void* k_cache, const void* v_cache, const int32_t* page_table,
+                         int table_ld, int max_pages, const int64_t* positions, const float* k_scale,
+                         const float* v_scale, const void* gate, int ld_gate, float out_eps, void* out, int ldo,
+                         int B, int L, int Hq, int Hkv, int D, int page_size, int64_t num_pages, float sm_scale,
+                         int window, void* workspace, size_t workspace_bytes, okc_stream_t stream) {
+  if (!q || !k_cache || !v_cache || !page_table || !positions || !k_scale || !v_scale || !out) return OKC_ERR_INVALID;
+  if (B <= 0 || L <= 0 || (long long)B * L >= (1LL << 31) || Hkv <= 0 || Hq % Hkv || Hq / Hkv > 8) return OKC_ERR_INVALID;
+  if (!(D == 64 || D == 128) || page_size <= 0 || num_pages <= 0 || max_pages <= 0 || table_ld < max_pages ||
+      window < 0)
+    return OKC_ERR_INVALID;
+  if (ldq < Hq * D || ldq % 8 || ldo < Hq * D || ldo % 2 || (gate && (ld_gate < Hq * D || ld_gate % 2)))
+    return OKC_ERR_INVALID;
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || (reinterpret_cast<uintptr_t>(out) & 3) ||
+      (gate && (reinterpret_cast<uintptr_t>(gate) & 3)))
+    return OKC_ERR_ALIGNMENT;
+  if (!workspace || workspace_bytes < 256) return OKC_ERR_WORKSPACE;
+  return okc::launch_attn_prefill(q, ldq, k_cache, v_cache, page_table, table_ld, max_pages, positions, k_scale,
+                                  v_scale, gate, ld_gate, out, ldo, B, L, Hq, Hkv, D, page_size, num_pages, sm_scale,
+                                  window, out_eps, reinterpret_cast<int*>(workspace), stream);
+}
+
 // ------------------------------------------------------------------- RoPE + append
 int okc_rope_kv_append_ex(const void* qkv, int ldqkv, const int64_t* positions, const int32_t* page_table,
                           int table_ld, int max_pages, const float* inv_freq, const float* k_scale,

@@ -73,6 +73,11 @@ int launch_residual_boundary(const float* stream_in, const void* branch, int ldb
                              float* stream_out, float* router_out, int T, int H, float post_eps, float pre_eps,
                              cudaStream_t stream);
 int launch_attn_decode(AttnArgs& a, int D, int Hkv, cudaStream_t stream);
+int launch_attn_prefill(const void* q, int ldq, const void* k_cache, const void* v_cache, const int32_t* page_table,
+                        int table_ld, int max_pages, const int64_t* positions, const float* k_scale,
+                        const float* v_scale, const void* gate, int ld_gate, void* out, int ldo, int B, int L, int Hq,
+                        int Hkv, int D, int page_size, long long num_pages, float sm_scale, int window, float out_eps,
+                        int* err, cudaStream_t stream);
 int launch_rope_append(const void* qkv, int ldqkv, const int64_t* positions,
                        const int32_t* page_table, int table_ld, int max_pages, const float* inv_freq,
                        const float* k_scale, const float* v_scale, void* q_out, void* k_cache,

@@ -338,6 +338,35 @@ def moe_experts(x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor, perm: dic
     return out
 
 
+def attn_prefill(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, page_table: torch.Tensor,
+                 positions: torch.Tensor, k_scale: torch.Tensor, v_scale: torch.Tensor, sm_scale: float,
+                 B: int, L: int, gate: torch.Tensor | None = None, out_eps: float = 1e-5, window: int = 0,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Prefill-block attention (okc_attn_prefill_fp8): q bf16 [B*L, Hq, D] (rows request-major),
+    caches e4m3 [pages, P, Hkv, D], page_table int32 [B, max_pages], positions int64 [B*L];
+    returns bf16 [B*L, Hq, D] (with `gate`: Muse's rms(o) * sigmoid(gate) per head)."""
+    dev = _dev_index(q)
+    _need(q, torch.bfloat16, "q")
+    T, Hq, D = q.shape
+    if T != B * L:
+        raise _lib.OkcError(f"q has {T} rows, B * L = {B * L}")
+    Hkv = k_cache.shape[2]
+    if out is None:
+        out = torch.empty((T, Hq, D), dtype=torch.bfloat16, device=q.device)
+    if gate is not None:
+        _need(gate, torch.bfloat16, "gate")
+    lib = _lib.load()
+    ws = workspace(dev, "attn_prefill", 256)
+    st = lib.okc_attn_prefill_fp8(q.data_ptr(), q.stride(0), k_cache.data_ptr(), v_cache.data_ptr(),
+                                  page_table.data_ptr(), page_table.stride(0), page_table.shape[1],
+                                  positions.data_ptr(), k_scale.data_ptr(), v_scale.data_ptr(), _ptr(gate),
+                                  gate.stride(0) if gate is not None else 0, float(out_eps), out.data_ptr(),
+                                  out.stride(0), B, L, Hq, Hkv, D, k_cache.shape[1], k_cache.shape[0],
+                                  float(sm_scale), int(window), ws.data_ptr(), ws.numel(), _stream(dev))
+    check(st, "okc_attn_prefill_fp8")
+    return out
+
+
 def attn_workspace_bytes(B: int, Hq: int, Hkv: int, D: int, num_ctas: int = 0) -> int:
     return int(_lib.load().okc_attn_decode_workspace_bytes(B, Hq, Hkv, D, num_ctas))
 

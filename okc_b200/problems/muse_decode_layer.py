@@ -27,9 +27,9 @@ Stages, each on this library's kernels:
 Token counts: decode steps and verify blocks (q_len 1 / 8), and prefill blocks (q_len 200-16384,
 muse_prefill_layer/submission.py:201-218, the same layer): projections beyond 256 tokens run as
 256-row tcgen05 blocks, the append of a long block runs per request with its table row shared,
-the experts run in passes of 2048 tokens, and attention is the decode kernel with one query
-row per token (each token reads its own visible span: O(q_len^2) cache reads, correct but not
-a prefill attention kernel).
+the experts run in passes of 2048 tokens, and attention runs on the prefill kernel
+(okc_attn_prefill_fp8: 8 tokens x the query heads of one KV head per CTA, the request's keys
+streamed once for them).
 
 Queries: the reference's window-0 path hands FA3 an e4m3-rounded query
 (decode/attention.py:150-165); here every layer keeps the bf16 query of its split-attention
@@ -51,7 +51,6 @@ ROPE_BASE = 500000.0    # decode/runtime.py:33
 ROUTE_SCALE = 0.1767766952966369   # decode/runtime.py:31 (router_output_multiplier)
 ROUTE_EPS = 1e-15
 MOE_CHUNK = 2048        # tokens per expert pass (okc_moe_permute: T * top_k <= 16384)
-ATTN_CHUNK = 2048       # query rows per attention call in a prefill block (okc_attn_decode_fp8: <= 4096)
 
 
 def _gate_coeffs(w: torch.Tensor):
@@ -112,14 +111,10 @@ def _attention(data: dict, state: dict) -> torch.Tensor:
         out = ops.attn_decode(q, data["k_cache"], data["v_cache"], table, lens, ks, vs, cfg["sm_scale"], gate=gate,
                               out_eps=RMS_EPS, window=window, q_per_seq=L)
         return out.view(B * L, hq * d)
-    # prefill blocks: per request, up to ATTN_CHUNK query rows per call (its table row for all)
-    out = torch.empty((B * L, hq, d), dtype=torch.bfloat16, device=qkv.device)
-    for b in range(B):
-        for c0 in range(0, L, ATTN_CHUNK):
-            r = slice(b * L + c0, b * L + min(L, c0 + ATTN_CHUNK))
-            n = r.stop - r.start
-            ops.attn_decode(q[r], data["k_cache"], data["v_cache"], table[b:b + 1], lens[r], ks, vs, cfg["sm_scale"],
-                            out=out[r], gate=gate[r], out_eps=RMS_EPS, window=window, q_per_seq=n)
+    # prefill blocks: the prefill kernel (8 tokens x the query heads of a KV head per CTA, the
+    # request's keys streamed once for them)
+    out = ops.attn_prefill(q, data["k_cache"], data["v_cache"], table, positions, ks, vs, cfg["sm_scale"], B, L,
+                           gate=gate, out_eps=RMS_EPS, window=window)
     return out.view(B * L, hq * d)
 
 
