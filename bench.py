@@ -11,10 +11,13 @@ memory (okc_tp_oproj_allreduce_residual).  Rank 0 prints ONE JSON line.
 value     = device time per step (CUDA events around K graph replays, max over ranks), µs.  Where
             one rank's working set (weights + its KV heads) is under 4x the 126 MB L2 (N >= 4),
             the replays rotate over several independent sets of weights and caches.
-e2e       = the same step through the public API (DecodeLayer.step) with the step's input copied
-            in from pinned host memory and its output copied back every step, copies and step in
-            one graph, µs.  At N > 1 each rank copies in its 1/N of the token rows (gathered over
-            NVLink) and copies out the 1/N of the output rows it owns.
+e2e       = the same step through the public API (DecodeLayer.step driven by
+            okc_b200.pipeline.HostPipeline) with the step's input copied in from pinned host
+            memory and its output copied back every step, µs per step over K steps: step k's
+            copy-in and step k-1's copy-out overlap step k's compute (double-buffered, three
+            streams).  serial_value: the same with copy in, step and copy out in series (one
+            graph).  At N > 1 each rank copies in its 1/N of the token rows (gathered over NVLink)
+            and copies out the 1/N of the output rows it owns.
 roofline  = the attention kernel (the dominant kernel) measured with CUDA events inside an
             instrumented copy of the step graph: algorithmic KV bytes / duration vs
             MEASURED_PEAKS.json hbm_gbs; stages_us = per-stage times from the same copy.
@@ -483,9 +486,13 @@ def run_okc(args):
 
     # e2e: through the public API with host buffers in and out every step, on input set 0.  The
     # step's input travels as ONE pinned host buffer into one device buffer (x rows, positions);
-    # the output comes back into pinned memory; the copies and the step are one graph.  At N > 1
-    # rank r copies in only its 1/N of the x rows (gathered over NVLink into the full x by an
-    # NCCL all-gather in the same graph) and copies out only the 1/N of the output rows it owns.
+    # the output comes back into pinned memory.  At N > 1 rank r copies in only its 1/N of the x
+    # rows (gathered over NVLink into the full x by an NCCL all-gather in the step) and copies out
+    # only the 1/N of the output rows it owns.  Two forms, each K steps timed with CUDA events,
+    # max over ranks: serial (copy in, step, copy out as one graph, one step after another) and
+    # the headline, okc_b200.pipeline.HostPipeline (step k's copy-in and step k-1's copy-out run
+    # on their own streams while step k computes; every step still copies its input in and its
+    # output out).
     rows = B // world
     r0 = rank * rows
     xb = rows * H * 2
@@ -525,11 +532,43 @@ def run_okc(args):
         graph_e.replay()
     f1.record()
     torch.cuda.synchronize()
-    e2e_us = f0.elapsed_time(f1) * 1000.0 / args.steps
-    t = torch.tensor([e2e_us], device=dev)
+    e2e_serial_us = f0.elapsed_time(f1) * 1000.0 / args.steps
+
+    from okc_b200.pipeline import HostPipeline
+
+    def step_io(inp):
+        x_in = inp[:xb].view(torch.bfloat16).view(rows, H)
+        pos_in = inp[xb:].view(torch.int64)
+        xf = x_in
+        if world > 1:
+            xf = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
+            dist.all_gather_into_tensor(xf, x_in, group=group)
+        r = layer.step(xf, pos_in, table, kc, vc, lens=lens)
+        # at N > 1 the step's result is the exchange's shared buffer: copy the owned rows out of
+        # it, so that the next step cannot overwrite them while they travel to the host
+        return r[r0:r0 + rows].clone() if world > 1 else r
+
+    pipe = HostPipeline(step_io, xb + B * 8, dev)
+    for _ in range(max(3, args.warmup)):
+        pipe.submit(io_host, out_host)
+    pipe.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    p0 = torch.cuda.Event(enable_timing=True)
+    p1 = torch.cuda.Event(enable_timing=True)
+    p0.record(pipe.s_in)
+    for _ in range(args.steps):
+        pipe.submit(io_host, out_host)
+    p1.record(pipe.s_out)
+    torch.cuda.synchronize()
+    e2e_us = p0.elapsed_time(p1) * 1000.0 / args.steps
+    pipe.close()
+    del pipe
+    t = torch.tensor([e2e_us, e2e_serial_us], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_us = float(t.item())
+    e2e_us, e2e_serial_us = (float(v) for v in t.tolist())
 
     traffic = None
     tp = ROOT / "profiles" / "traffic.json"
@@ -561,7 +600,9 @@ def run_okc(args):
             "input_sets": nsets,
             "e2e": {"value": round(e2e_us, 2), "unit": "us/step", "h2d_bytes_per_step": xb + B * 8,
                     "d2h_bytes_per_step": rows * H * 2,
-                    "io": "whole batch" if world == 1 else f"1/{world} of the rows per rank, NCCL all-gather of x"},
+                    "io": "whole batch" if world == 1 else f"1/{world} of the rows per rank, NCCL all-gather of x",
+                    "overlap": "HostPipeline: copy-in of step k and copy-out of step k-1 overlap step k",
+                    "serial_value": round(e2e_serial_us, 2)},
             "roofline": {"kernel": "okc::attn_decode_kernel<128,%d> + merge" % lkv, "bound": "hbm",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
