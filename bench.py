@@ -16,8 +16,9 @@ e2e       = the same step through the public API (DecodeLayer.step driven by
             memory and its output copied back every step, µs per step over K steps: step k's
             copy-in and step k-1's copy-out overlap step k's compute (double-buffered, three
             streams).  serial_value: the same with copy in, step and copy out in series (one
-            graph).  At N > 1 each rank copies in its 1/N of the token rows (gathered over NVLink)
-            and copies out the 1/N of the output rows it owns.
+            graph).  At N > 1 each rank copies out the 1/N of the output rows it owns; it copies
+            in the whole x when pipelined (the copy overlaps the previous step), and its 1/N of
+            the x rows, gathered over NVLink by an NCCL all-gather in the step, when serial.
 roofline  = the attention kernel (the dominant kernel) measured with CUDA events inside an
             instrumented copy of the step graph: algorithmic KV bytes / duration vs
             MEASURED_PEAKS.json hbm_gbs; stages_us = per-stage times from the same copy.
@@ -536,21 +537,24 @@ def run_okc(args):
 
     from okc_b200.pipeline import HostPipeline
 
+    # Pipelined, every rank copies in the whole x: the tensor-parallel step needs all rows on
+    # every rank, and the copy overlaps the previous step, where an all-gather would sit inside
+    # the step (measured at 2 GPUs: 247 us/step with the 1/N copy + all-gather vs 207 device).
+    xfb = B * H * 2
+    io_full_host = torch.cat([x.contiguous().view(torch.uint8).reshape(-1).cpu(),
+                              positions.contiguous().view(torch.uint8).reshape(-1).cpu()]).pin_memory()
+
     def step_io(inp):
-        x_in = inp[:xb].view(torch.bfloat16).view(rows, H)
-        pos_in = inp[xb:].view(torch.int64)
-        xf = x_in
-        if world > 1:
-            xf = torch.empty((B, H), dtype=torch.bfloat16, device=dev)
-            dist.all_gather_into_tensor(xf, x_in, group=group)
-        r = layer.step(xf, pos_in, table, kc, vc, lens=lens)
+        x_in = inp[:xfb].view(torch.bfloat16).view(B, H)
+        pos_in = inp[xfb:].view(torch.int64)
+        r = layer.step(x_in, pos_in, table, kc, vc, lens=lens)
         # at N > 1 the step's result is the exchange's shared buffer: copy the owned rows out of
         # it, so that the next step cannot overwrite them while they travel to the host
         return r[r0:r0 + rows].clone() if world > 1 else r
 
-    pipe = HostPipeline(step_io, xb + B * 8, dev)
+    pipe = HostPipeline(step_io, xfb + B * 8, dev)
     for _ in range(max(3, args.warmup)):
-        pipe.submit(io_host, out_host)
+        pipe.submit(io_full_host, out_host)
     pipe.synchronize()
     if world > 1:
         dist.barrier()
@@ -559,7 +563,7 @@ def run_okc(args):
     p1 = torch.cuda.Event(enable_timing=True)
     p0.record(pipe.s_in)
     for _ in range(args.steps):
-        pipe.submit(io_host, out_host)
+        pipe.submit(io_full_host, out_host)
     p1.record(pipe.s_out)
     torch.cuda.synchronize()
     e2e_us = p0.elapsed_time(p1) * 1000.0 / args.steps
@@ -598,11 +602,13 @@ def run_okc(args):
             "data": "synthetic (seeded; decode-layer workload shapes)",
             "config": dict(WORKLOAD, parallelism=f"tp{world}"),
             "input_sets": nsets,
-            "e2e": {"value": round(e2e_us, 2), "unit": "us/step", "h2d_bytes_per_step": xb + B * 8,
+            "e2e": {"value": round(e2e_us, 2), "unit": "us/step", "h2d_bytes_per_step": xfb + B * 8,
                     "d2h_bytes_per_step": rows * H * 2,
-                    "io": "whole batch" if world == 1 else f"1/{world} of the rows per rank, NCCL all-gather of x",
+                    "io": "whole batch" if world == 1 else f"whole x in per rank, 1/{world} of the output rows out",
                     "overlap": "HostPipeline: copy-in of step k and copy-out of step k-1 overlap step k",
-                    "serial_value": round(e2e_serial_us, 2)},
+                    "serial_value": round(e2e_serial_us, 2),
+                    "serial_io": "whole batch" if world == 1 else
+                    f"1/{world} of the x rows in per rank + NCCL all-gather, 1/{world} of the output rows out"},
             "roofline": {"kernel": "okc::attn_decode_kernel<128,%d> + merge" % lkv, "bound": "hbm",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
