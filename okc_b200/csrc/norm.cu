@@ -8,7 +8,9 @@ namespace okc {
 
 constexpr int kNormMaxVec = 8;  // 16-byte vectors per thread: H <= 256 * 8 * 8 = 16384
 
-// Single pass: the row stays in registers between the sum of squares and the scaling.
+// Single pass: the row stays in registers between the sum of squares and the scaling; the
+// weight is loaded with the row, so its latency overlaps the row's instead of following the
+// reduction.
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                                       const __nv_bfloat16* __restrict__ w,
                                                       __nv_bfloat16* __restrict__ y, int ldy, int H,
@@ -19,12 +21,13 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
   const __nv_bfloat16* xr = x + (size_t)t * ldx;
   __nv_bfloat16* yr = y + (size_t)t * ldy;
   __shared__ float red[8];
-  uint4 v[kNormMaxVec];
+  uint4 v[kNormMaxVec], gw[kNormMaxVec];
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < kNormMaxVec; ++j) {
     const int i = (j * blockDim.x + threadIdx.x) * 8;
     v[j] = i < H ? *reinterpret_cast<const uint4*>(xr + i) : make_uint4(0, 0, 0, 0);
+    gw[j] = i < H ? *reinterpret_cast<const uint4*>(w + i) : make_uint4(0, 0, 0, 0);
     const uint32_t wv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
@@ -42,8 +45,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const __nv_bfloat16* __res
   for (int j = 0; j < kNormMaxVec; ++j) {
     const int i = (j * blockDim.x + threadIdx.x) * 8;
     if (i >= H) break;
-    const uint4 gw = *reinterpret_cast<const uint4*>(w + i);
-    const uint32_t xv[4] = {v[j].x, v[j].y, v[j].z, v[j].w}, gv[4] = {gw.x, gw.y, gw.z, gw.w};
+    const uint32_t xv[4] = {v[j].x, v[j].y, v[j].z, v[j].w}, gv[4] = {gw[j].x, gw[j].y, gw[j].z, gw[j].w};
     uint32_t o[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
