@@ -60,11 +60,21 @@ class HostPipeline:
         self.ev_run = [torch.cuda.Event() for _ in range(2)]
         self.ev_out = [torch.cuda.Event() for _ in range(2)]
         self.k = 0
+        self._checked: set = set()
 
     def submit(self, host_in: torch.Tensor, host_out: torch.Tensor) -> None:
         """Enqueues one step: host_in (pinned, in_nbytes) in, the step, its output into host_out
         (pinned, the output's shape and dtype).  Returns without waiting."""
         i = self.k & 1
+        key = (host_in.data_ptr(), host_in.numel(), host_out.data_ptr(), tuple(host_out.shape), host_out.dtype)
+        if key not in self._checked:  # checked once per buffer pair (is_pinned asks the driver)
+            if not (host_in.is_pinned() and host_out.is_pinned()):
+                raise RuntimeError("HostPipeline needs pinned host buffers (unpinned copies would not overlap)")
+            if host_in.numel() * host_in.element_size() != self.inp[i].numel():
+                raise RuntimeError("host_in must hold exactly the step's input bytes")
+            if host_out.shape != self.out[i].shape or host_out.dtype != self.out[i].dtype:
+                raise RuntimeError(f"host_out must be {tuple(self.out[i].shape)} {self.out[i].dtype}")
+            self._checked.add(key)
         self.s_in.wait_event(self.ev_run[i])
         with torch.cuda.stream(self.s_in):
             self.inp[i].copy_(host_in, non_blocking=True)

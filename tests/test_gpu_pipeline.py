@@ -50,3 +50,20 @@ def test_pipeline_keeps_submission_order():
         want = float((k + 1) * (k + 2) // 2)
         assert torch.all(host_out[k] == want), f"step {k}: {host_out[k][0].item()} != {want}"
     pipe.close()
+
+
+def test_pipeline_rejects_unpinned_or_mis_sized_buffers():
+    from okc_b200.pipeline import HostPipeline
+    pipe = HostPipeline(lambda inp: inp.view(torch.float32) * 2, 64, "cuda")
+    ok_in = torch.arange(64, dtype=torch.uint8).pin_memory()
+    ok_out = torch.empty(16, dtype=torch.float32).pin_memory()
+    with pytest.raises(RuntimeError, match="pinned"):
+        pipe.submit(torch.zeros(64, dtype=torch.uint8), ok_out)
+    with pytest.raises(RuntimeError, match="input bytes"):
+        pipe.submit(torch.zeros(32, dtype=torch.uint8).pin_memory(), ok_out)
+    with pytest.raises(RuntimeError, match="host_out"):
+        pipe.submit(ok_in, torch.empty(8, dtype=torch.float32).pin_memory())
+    pipe.submit(ok_in, ok_out)
+    pipe.synchronize()
+    assert torch.equal(ok_out, ok_in.view(torch.float32) * 2)
+    pipe.close()
