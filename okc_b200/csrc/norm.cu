@@ -76,7 +76,8 @@ __device__ __forceinline__ float bf16_rn_f(float v) { return __bfloat162float(__
 // input is hidden = bf16(stream' * rsqrt(mean(stream'^2) + pre_eps) * (1 + pre_w)), also stored
 // unrounded in fp32 for the router when router_out is given.  Products and sums are rounded one
 // at a time (the reference compiles this kernel with fp fusion off).  One CTA of 512 threads a
-// row, the row in registers between the two reductions; stream_out may alias stream.
+// row, the row in registers between the two reductions; stream_out may alias stream (a thread
+// reads its stream elements, with pre_w, in the first pass, before it writes them).
 constexpr int kBndVec = 4;  // 512 threads x 4 x 8 elements: H <= 16384
 
 __global__ void __launch_bounds__(512) residual_boundary_kernel(
@@ -89,13 +90,20 @@ __global__ void __launch_bounds__(512) residual_boundary_kernel(
   __shared__ float red[16];
   const int t = blockIdx.x, tid = threadIdx.x;
   const __nv_bfloat16* br = branch + (size_t)t * ldb;
+  const float* sr = stream + (size_t)t * H;
   float v[kBndVec][8];
+  float4 sv[kBndVec][2];
+  uint4 pre4[kBndVec];
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < kBndVec; ++j) {
     const int i = (j * 512 + tid) * 8;
     if (i >= H) break;
     const uint4 u4 = *reinterpret_cast<const uint4*>(br + i);
+    // issued with the branch row: their latency overlaps its, not the reductions
+    sv[j][0] = *reinterpret_cast<const float4*>(sr + i);
+    sv[j][1] = *reinterpret_cast<const float4*>(sr + i + 4);
+    pre4[j] = *reinterpret_cast<const uint4*>(pre_w + i);
     const uint32_t u[4] = {u4.x, u4.y, u4.z, u4.w};
     uint32_t pw[4] = {0u, 0u, 0u, 0u};
     if (post_w) {
@@ -115,7 +123,6 @@ __global__ void __launch_bounds__(512) residual_boundary_kernel(
     }
   }
   const float inv_b = rsqrtf(block_sum(ss, red) / (float)H + post_eps);
-  const float* sr = stream + (size_t)t * H;
   float* so = stream_out + (size_t)t * H;
   ss = 0.f;
 #pragma unroll
@@ -124,7 +131,7 @@ __global__ void __launch_bounds__(512) residual_boundary_kernel(
     if (i >= H) break;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
-      const float4 o = *reinterpret_cast<const float4*>(sr + i + 4 * h);
+      const float4 o = sv[j][h];
       const float4 al = *reinterpret_cast<const float4*>(alpha + i + 4 * h);
       const float4 be = *reinterpret_cast<const float4*>(beta + i + 4 * h);
       const float ov[4] = {o.x, o.y, o.z, o.w}, av[4] = {al.x, al.y, al.z, al.w}, bv[4] = {be.x, be.y, be.z, be.w};
@@ -144,8 +151,7 @@ __global__ void __launch_bounds__(512) residual_boundary_kernel(
   for (int j = 0; j < kBndVec; ++j) {
     const int i = (j * 512 + tid) * 8;
     if (i >= H) break;
-    const uint4 p4 = *reinterpret_cast<const uint4*>(pre_w + i);
-    const uint32_t pw[4] = {p4.x, p4.y, p4.z, p4.w};
+    const uint32_t pw[4] = {pre4[j].x, pre4[j].y, pre4[j].z, pre4[j].w};
     float h[8];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
